@@ -1,0 +1,323 @@
+#!/usr/bin/env python
+"""Throughput benchmark of the SPINNV2 B200 CUDA target (BASELINE.json metric:
+ResNet-101 img/s at batch 64 per GPU on 1/2/4/8 B200).
+
+One step = one ResNet-101 v1.5 forward pass (fp32 activations, 3xTF32 conv
+math by default) over a batch of 64 synthetic N(0,1) 3x224x224 images with
+seeded random-init weights, executed by libspkv2_runtime.so.  Multi-GPU is
+batch-sharded inference with no data-path collective: every rank holds its
+own SPK, weights and arenas and runs its own batch of 64 (weak scaling);
+torch.distributed only provides the start/stop barrier and the max-over-ranks
+of the timed region.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line on rank 0.  --impl reference times the reference
+SPINNV2 CPU runtime (oracle/_ref, built from the reference's own sources) on
+the host cores for the same config, on a bounded batch sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "ResNet-101 img/s (bs64 per GPU)"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def conv_flops(pkg) -> tuple[float, list[int]]:
+    total, ids = 0.0, []
+    for n in pkg.nodes:
+        if n.op_type == "Conv":
+            w = pkg.tensors[n.inputs[1]].shape
+            y = pkg.tensors[n.outputs[0]].shape
+            total += 2.0 * y[0] * y[1] * y[2] * y[3] * w[1] * w[2] * w[3]
+            ids.append(n.id)
+    return total, ids
+
+
+def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
+    """Reference CPU runtime (oracle/_ref) img/s on a bounded sample."""
+    from oracle import refrt
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.spk import read_spk
+
+    spk = pipeline.compile_config(config, batch, targets=("cpu_generic_x86",))["cpu_generic_x86"]
+    pkg = read_spk(spk)
+    x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+    rt = refrt.RefRuntime(spk, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs])
+    rt.run(x)  # warm-up (lazy weight packing)
+    times = []
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds and (max_steps is None or len(times) < max_steps):
+        t0 = time.perf_counter()
+        rt.run(x)
+        times.append(time.perf_counter() - t0)
+    rt.close()
+    per = statistics.median(times)
+    return {"value": batch / per, "step_s": per, "steps": len(times), "times": times}
+
+
+def run_reference_arm(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    sample = min(args.batch, args.reference_sample)
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    res = cpu_reference_throughput(args.config, sample, seconds=1e9, max_steps=args.warmup + args.steps)
+    timed = res["times"][args.warmup:] or res["times"]
+    ms = 1000.0 * sum(timed) / len(timed)
+    value = sample / (ms / 1000.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": args.gpus,
+        "steps": len(timed), "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} fp32 forward, batch {args.batch}", "model": args.config,
+                   "global_batch": args.batch, "sample_batch_per_step": sample, "runtime": "reference cpu_generic "
+                   "(AVX2/FMA, OpenMP), BNNS token removed from the profile"},
+        "cpu_baseline": {"value": value, "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+                         "kind": "reference", "sample": f"{sample} images per step, {len(timed)} steps"},
+        "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu_arm(args, world: int, rank: int, local: int) -> None:
+    import torch
+
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import MATH_3XTF32, MATH_FP32, MATH_SPEC, MATH_TF32, Runtime
+
+    math_mode = {"spec": MATH_SPEC, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32, "fp32": MATH_FP32}[args.math]
+    torch.cuda.set_device(local)
+    spk = pipeline.compile_config(args.config, args.batch, targets=("cuda_b200",), seed=0)["cuda_b200"]
+    rt = Runtime(spk, device=local, math_mode=math_mode, graph=True)
+    pkg = rt.package
+    in_t, out_t = pkg.inputs[0], pkg.outputs[0]
+    rng = np.random.default_rng(1 + rank)
+    x = rng.standard_normal(in_t.shape, dtype=np.float32)
+    stream = torch.cuda.ExternalStream(rt.stream())
+
+    # ---- device-resident timing (inputs already in HBM) ----
+    d_in = torch.from_numpy(x).cuda(local)
+    rt.bind_input(0, d_in.data_ptr())
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local}")  # > 126 MB L2
+    for _ in range(args.warmup):
+        rt.run_async()
+    rt.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = []
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            rt.run_async()
+            e.record(stream)
+            evs.append((s, e))
+    rt.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in evs]
+    local_total_ms = sum(step_ms)
+    total_ms = max_over_ranks(local_total_ms, world)
+    ms_per_step = total_ms / args.steps
+    value = world * args.batch * args.steps / (total_ms / 1000.0)
+
+    # ---- roofline of the conv kernels (per-node events) ----
+    flops, conv_ids = conv_flops(pkg)
+    prof = np.stack([rt.profile_nodes() for _ in range(3)])
+    node_ms = prof.mean(axis=0)
+    conv_ms = float(node_ms[conv_ids].sum())
+    pk, basis = peaks()
+    tf32_peak = pk["bf16_tflops"] / 2.0
+    achieved = flops / (conv_ms / 1000.0) / 1e12
+    variants = sorted({rt.node_variant(i) for i in conv_ids})
+
+    # ---- end to end through the public API: pinned host in/out, spkv2_run ----
+    rt2 = Runtime(spk, device=local, math_mode=math_mode, graph=True)
+    h_in = torch.from_numpy(x).pin_memory()
+    h_out = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory()
+    rt2.bind_input(0, h_in.data_ptr())
+    rt2.bind_output(0, h_out.data_ptr())
+    for _ in range(max(args.warmup, 2)):
+        rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = world * args.batch * args.steps / e2e_s
+    launches = rt.launches_per_run() * args.steps
+    rt2.close()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config} v1.5 forward, batch {args.batch} per GPU, 224x224, fp32 "
+                                   f"activations, conv math {args.math}",
+                       "model": args.config, "global_batch": args.batch * world, "per_gpu_batch": args.batch,
+                       "seq_len": None, "parallelism": f"batch-sharded x{world}, no collectives",
+                       "l2": "flushed between steps (256 MiB write)", "conv_variants": variants},
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
+                    "d2h_bytes_per_step": int(np.prod(out_t.shape) * 4)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tf32_peak, "traffic": None,
+                         "kernel": "all Conv launches of one step", "flops_per_step": flops,
+                         "conv_ms_per_step": conv_ms,
+                         "peak_basis": f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+            cb = cpu_reference_throughput(args.config, 1, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": cb["value"], "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+                                    "kind": "reference",
+                                    "sample": f"batch 1, {cb['steps']} runs over ~{args.cpu_seconds:.0f} s"}
+        print(json.dumps(line), flush=True)
+    rt.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="resnet101")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--math", default="spec", choices=["spec", "3xtf32", "tf32", "fp32"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--reference-sample", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, world, rank)
+        else:
+            run_gpu_arm(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,303 @@
+"""SIR graph builders for the benchmark configurations.
+
+ONNX and onnxruntime are not available, so the graphs of the five configs are
+written directly in SIR, with seeded random weights:
+
+  lenet5(batch)                 C1  LeNet-5, input U[0,1) 1x28x28
+  conv_sweep(case, batch)       C2  single Conv + bias + Relu (or one Gemm)
+  resnet(depth, batch)          C3  ResNet-101 v1.5 (C4 uses depth 50)
+  yolo_style(batch)             C5  YOLOv10n-style detector, pre-NMS top-300
+
+Weights are Kaiming-normal (std sqrt(2 / fan_in)); biases N(0, 0.01);
+BatchNorm gamma U(0.5,1.5), beta N(0,0.1), mean N(0,0.1), var U(0.5,1.5).
+BatchNorm, Relu, Sigmoid*Mul and residual Add appear as separate nodes, as an
+ONNX import would produce them; the pass pipeline folds them into the convs.
+Gemm weights are stored [K, N] with transB = 0.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .ir import DTYPE_FP32, Graph, GraphBuilder
+
+
+class _Init:
+    def __init__(self, seed: int) -> None:
+        self.rng = np.random.default_rng(seed)
+
+    def kaiming(self, shape, fan_in: int) -> np.ndarray:
+        return (self.rng.standard_normal(shape, dtype=np.float32) * np.float32(np.sqrt(2.0 / fan_in))).astype(np.float32)
+
+    def bias(self, n: int) -> np.ndarray:
+        return (self.rng.standard_normal(n, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+
+    def bn(self, c: int) -> list[np.ndarray]:
+        gamma = self.rng.uniform(0.5, 1.5, c).astype(np.float32)
+        beta = (self.rng.standard_normal(c, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+        mean = (self.rng.standard_normal(c, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+        var = self.rng.uniform(0.5, 1.5, c).astype(np.float32)
+        return [gamma, beta, mean, var]
+
+
+def _out_hw(h: int, w: int, k: int, s: int, p: int) -> tuple[int, int]:
+    return (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+
+
+class _Net:
+    """Op-level helpers over a GraphBuilder."""
+
+    def __init__(self, name: str, seed: int) -> None:
+        self.b = GraphBuilder(name)
+        self.init = _Init(seed)
+        self.n = 0
+
+    def _name(self, kind: str) -> str:
+        self.n += 1
+        return f"{kind}{self.n}"
+
+    def conv(self, x: int, cout: int, k: int, s: int = 1, p: int | None = None, bias: bool = False,
+             bn: bool = False, act: str | None = None) -> int:
+        nm = self._name("conv")
+        n, c, h, w = self.b.shape(x)
+        p = k // 2 if p is None else p
+        oh, ow = _out_hw(h, w, k, s, p)
+        ins = [x, self.b.weight(f"{nm}_w", self.init.kaiming((cout, c, k, k), c * k * k))]
+        if bias:
+            ins.append(self.b.weight(f"{nm}_b", self.init.bias(cout)))
+        y = self.b.op("Conv", ins, [n, cout, oh, ow], {"kernel_shape": [k, k], "strides": [s, s],
+                                                       "pads": [p, p, p, p], "dilations": [1, 1], "group": 1},
+                      name=nm)
+        if bn:
+            params = [self.b.weight(f"{nm}_bn{i}", v) for i, v in enumerate(self.init.bn(cout))]
+            y = self.b.op("BatchNormalization", [y] + params, [n, cout, oh, ow], {"epsilon": 1e-5}, name=f"{nm}_bn")
+        if act == "Relu":
+            y = self.relu(y)
+        elif act == "Silu":
+            sig = self.b.op("Sigmoid", [y], self.b.shape(y), name=f"{nm}_sig")
+            y = self.b.op("Mul", [y, sig], self.b.shape(y), name=f"{nm}_silu")
+        return y
+
+    def relu(self, x: int) -> int:
+        return self.b.op("Relu", [x], self.b.shape(x))
+
+    def maxpool(self, x: int, k: int, s: int, p: int) -> int:
+        n, c, h, w = self.b.shape(x)
+        oh, ow = _out_hw(h, w, k, s, p)
+        return self.b.op("MaxPool", [x], [n, c, oh, ow], {"kernel_shape": [k, k], "strides": [s, s],
+                                                          "pads": [p, p, p, p]})
+
+    def add(self, a: int, c: int) -> int:
+        return self.b.op("Add", [a, c], self.b.shape(a))
+
+    def gemm(self, x: int, nout: int) -> int:
+        m, k = self.b.shape(x)
+        w = self.b.weight(self._name("fc_w"), self.init.kaiming((k, nout), k))
+        bias = self.b.weight(self._name("fc_b"), self.init.bias(nout))
+        return self.b.op("Gemm", [x, w, bias], [m, nout], {"alpha": 1.0, "beta": 1.0, "transA": 0, "transB": 0})
+
+    def const(self, name: str, values) -> int:
+        return self.b.weight(name, np.asarray(values, dtype=np.float32))
+
+    def flatten(self, x: int) -> int:
+        s = self.b.shape(x)
+        return self.b.op("Flatten", [x], [s[0], int(np.prod(s[1:]))], {"axis": 1})
+
+
+# ---------------------------------------------------------------- C1
+
+def lenet5(batch: int = 1, seed: int = 0) -> Graph:
+    net = _Net(f"lenet5_b{batch}", seed)
+    x = net.b.input("input", [batch, 1, 28, 28])
+    y = net.conv(x, 6, 5, p=2, bias=True, act="Relu")
+    y = net.maxpool(y, 2, 2, 0)
+    y = net.conv(y, 16, 5, p=0, bias=True, act="Relu")
+    y = net.maxpool(y, 2, 2, 0)
+    y = net.flatten(y)
+    y = net.relu(net.gemm(y, 120))
+    y = net.relu(net.gemm(y, 84))
+    y = net.gemm(y, 10)
+    net.b.mark_output(y)
+    return net.b.graph
+
+
+# ---------------------------------------------------------------- C2
+
+SWEEP_CASES = {
+    # name: (cin, cout, k, stride, pad, hw)  or ("gemm", k, n)
+    "conv7x7s2_3_64_224": (3, 64, 7, 2, 3, 224),
+    "conv3x3_64_56": (64, 64, 3, 1, 1, 56),
+    "conv3x3_128_28": (128, 128, 3, 1, 1, 28),
+    "conv3x3_256_14": (256, 256, 3, 1, 1, 14),
+    "conv3x3_512_7": (512, 512, 3, 1, 1, 7),
+    "conv1x1_256_64_56": (256, 64, 1, 1, 0, 56),
+    "conv1x1_1024_256_14": (1024, 256, 1, 1, 0, 14),
+    "conv1x1_2048_512_7": (2048, 512, 1, 1, 0, 7),
+    "conv3x3s2_128_128_56": (128, 128, 3, 2, 1, 56),
+    "gemm_2048_1000": ("gemm", 2048, 1000),
+}
+
+
+def sweep_flops(case: str, batch: int) -> float:
+    spec = SWEEP_CASES[case]
+    if spec[0] == "gemm":
+        return 2.0 * batch * spec[1] * spec[2]
+    cin, cout, k, s, p, hw = spec
+    oh, ow = _out_hw(hw, hw, k, s, p)
+    return 2.0 * batch * cout * oh * ow * cin * k * k
+
+
+def conv_sweep(case: str, batch: int = 1, seed: int = 0) -> Graph:
+    spec = SWEEP_CASES[case]
+    net = _Net(f"sweep_{case}_b{batch}", seed)
+    if spec[0] == "gemm":
+        x = net.b.input("input", [batch, spec[1]])
+        y = net.gemm(x, spec[2])
+    else:
+        cin, cout, k, s, p, hw = spec
+        x = net.b.input("input", [batch, cin, hw, hw])
+        y = net.conv(x, cout, k, s=s, p=p, bias=True, act="Relu")
+    net.b.mark_output(y)
+    return net.b.graph
+
+
+# ---------------------------------------------------------------- C3 / C4
+
+RESNET_LAYERS = {50: [3, 4, 6, 3], 101: [3, 4, 23, 3]}
+
+
+def resnet(depth: int = 101, batch: int = 1, seed: int = 0) -> Graph:
+    """ResNet v1.5 (stride on the 3x3), head ReduceMean -> Gemm -> Softmax."""
+    net = _Net(f"resnet{depth}_b{batch}", seed)
+    x = net.b.input("input", [batch, 3, 224, 224])
+    y = net.conv(x, 64, 7, s=2, p=3, bn=True, act="Relu")
+    y = net.maxpool(y, 3, 2, 1)
+    cin = 64
+    for stage, (blocks, width) in enumerate(zip(RESNET_LAYERS[depth], [64, 128, 256, 512])):
+        for i in range(blocks):
+            stride = 2 if (i == 0 and stage > 0) else 1
+            shortcut = y
+            t = net.conv(y, width, 1, bn=True, act="Relu")
+            t = net.conv(t, width, 3, s=stride, p=1, bn=True, act="Relu")
+            t = net.conv(t, width * 4, 1, bn=True)
+            if i == 0:
+                shortcut = net.conv(y, width * 4, 1, s=stride, p=0, bn=True)
+            y = net.relu(net.add(t, shortcut))
+            cin = width * 4
+    n = net.b.shape(y)[0]
+    y = net.b.op("ReduceMean", [y], [n, cin, 1, 1], {"axes": [2, 3], "keepdims": 1})
+    y = net.flatten(y)
+    y = net.gemm(y, 1000)
+    y = net.b.op("Softmax", [y], net.b.shape(y), {"axis": 1})
+    net.b.mark_output(y)
+    return net.b.graph
+
+
+def resnet_gflop_per_image(depth: int) -> float:
+    """Algorithmic conv + FC GFLOP per 224x224 image (2 * MACs)."""
+    g = resnet(depth, 1)
+    flops = 0.0
+    for node in g.nodes:
+        if node.op_type == "Conv":
+            w = g.tensors[node.inputs[1]].shape
+            y = g.tensors[node.outputs[0]].shape
+            flops += 2.0 * y[1] * y[2] * y[3] * w[1] * w[2] * w[3]
+        elif node.op_type == "Gemm":
+            w = g.tensors[node.inputs[1]].shape
+            flops += 2.0 * w[0] * w[1]
+    return flops / 1e9
+
+
+# ---------------------------------------------------------------- C5
+
+def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80, topk: int = 300) -> Graph:
+    net = _Net(f"yolo_style_b{batch}", seed)
+    b = net.b
+
+    def cbs(x, cout, k, s=1):
+        return net.conv(x, cout, k, s=s, p=k // 2, bn=True, act="Silu")
+
+    def c2f(x, cout, n, shortcut):
+        c = cout // 2
+        y = cbs(x, 2 * c, 1)
+        nb, _, h, w = b.shape(y)
+        parts = b.node("Split", [y], [[nb, c, h, w], [nb, c, h, w]], {"axis": 1})
+        outs = list(parts)
+        cur = parts[1]
+        for _ in range(n):
+            t = cbs(cbs(cur, c, 3), c, 3)
+            cur = net.add(cur, t) if shortcut else t
+            outs.append(cur)
+        cat = b.op("Concat", outs, [nb, c * len(outs), h, w], {"axis": 1})
+        return cbs(cat, cout, 1)
+
+    def resize2x(x):
+        n, c, h, w = b.shape(x)
+        return b.op("Resize", [x], [n, c, 2 * h, 2 * w], {"mode": "nearest"})
+
+    def concat(xs):
+        n, _, h, w = b.shape(xs[0])
+        return b.op("Concat", xs, [n, sum(b.shape(t)[1] for t in xs), h, w], {"axis": 1})
+
+    x = b.input("images", [batch, 3, size, size])
+    y = cbs(x, 16, 3, 2)
+    y = cbs(y, 32, 3, 2)
+    y = c2f(y, 32, 1, True)
+    y = cbs(y, 64, 3, 2)
+    p3 = c2f(y, 64, 2, True)
+    y = cbs(p3, 128, 3, 2)
+    p4 = c2f(y, 128, 2, True)
+    y = cbs(p4, 256, 3, 2)
+    y = c2f(y, 256, 1, True)
+    # SPPF
+    t = cbs(y, 128, 1)
+    m1 = net.maxpool(t, 5, 1, 2)
+    m2 = net.maxpool(m1, 5, 1, 2)
+    m3 = net.maxpool(m2, 5, 1, 2)
+    p5 = cbs(concat([t, m1, m2, m3]), 256, 1)
+    # PAN neck
+    n4 = c2f(concat([resize2x(p5), p4]), 128, 1, False)
+    n3 = c2f(concat([resize2x(n4), p3]), 64, 1, False)
+    n4b = c2f(concat([cbs(n3, 64, 3, 2), n4]), 128, 1, False)
+    n5b = c2f(concat([cbs(n4b, 128, 3, 2), p5]), 256, 1, False)
+    # decoupled heads
+    boxes, scores = [], []
+    for feat in (n3, n4b, n5b):
+        nb, _, h, w = b.shape(feat)
+        bx = net.conv(cbs(cbs(feat, 64, 3), 64, 3), 4, 1, p=0, bias=True)
+        cl = net.conv(cbs(cbs(feat, 80, 3), 80, 3), classes, 1, p=0, bias=True)
+        boxes.append(b.op("Reshape", [bx, net.const(net._name("shape"), [nb, 4, h * w])], [nb, 4, h * w]))
+        scores.append(b.op("Reshape", [cl, net.const(net._name("shape"), [nb, classes, h * w])],
+                           [nb, classes, h * w]))
+    anchors = sum(b.shape(t)[2] for t in boxes)
+    box = b.op("Concat", boxes, [batch, 4, anchors], {"axis": 2})
+    cls = b.op("Concat", scores, [batch, classes, anchors], {"axis": 2})
+    cls = b.op("Sigmoid", [cls], b.shape(cls))
+    best = b.op("ReduceMax", [cls], [batch, anchors], {"axes": [1], "keepdims": 0})
+    vals, idx = b.node("TopK", [best, net.const("k", [topk])], [[batch, topk], [batch, topk]],
+                       {"axis": 1, "largest": 1, "sorted": 1})
+    box_t = b.op("Transpose", [box], [batch, anchors, 4], {"perm": [0, 2, 1]})
+    idx3 = b.op("Unsqueeze", [idx], [batch, topk, 1], {"axes": [2]})
+    idx4 = b.op("Tile", [idx3, net.const("repeats", [1, 1, 4])], [batch, topk, 4])
+    sel = b.op("GatherElements", [box_t, idx4], [batch, topk, 4], {"axis": 1})
+    b.mark_output(vals)
+    b.mark_output(sel)
+    return b.graph
+
+
+def build_config(name: str, batch: int, seed: int = 0) -> Graph:
+    if name == "lenet5":
+        return lenet5(batch, seed)
+    if name == "resnet101":
+        return resnet(101, batch, seed)
+    if name == "resnet50":
+        return resnet(50, batch, seed)
+    if name == "yolo_style":
+        return yolo_style(batch, seed)
+    if name in SWEEP_CASES:
+        return conv_sweep(name, batch, seed)
+    raise KeyError(name)
+
+
+__all__ = ["lenet5", "conv_sweep", "resnet", "yolo_style", "build_config", "SWEEP_CASES", "sweep_flops",
+           "resnet_gflop_per_image", "DTYPE_FP32"]

@@ -1,0 +1,77 @@
+"""Graph -> SPK packages for the CUDA target and the CPU reference profiles.
+
+The pass pipeline runs ONCE per graph (with the fused-residual pass enabled),
+then the same fused graph is packaged for every requested profile, so the
+CUDA package and the CPU-baseline/oracle packages describe identical math.
+Packages are cached under _build/spk_cache keyed by config, batch, seed and
+a hash of the compiler sources.
+"""
+
+from __future__ import annotations
+
+import copy
+import hashlib
+import os
+from pathlib import Path
+
+from . import builders
+from .ir import Graph
+from .passes import run_pass_pipeline
+from .profile import load_target_profile
+from .spk_writer import build_spk
+
+REPO_DIR = Path(__file__).resolve().parents[2]
+CACHE_DIR = Path(os.environ.get("SPKV2_SPK_CACHE", REPO_DIR / "_build" / "spk_cache"))
+
+FUSING_PROFILE = {"backends": ["delegate"]}
+
+
+def fuse(graph: Graph) -> Graph:
+    run_pass_pipeline(graph, profile=FUSING_PROFILE)
+    return graph
+
+
+def package(graph: Graph, profile: str | dict, quant_params: list | None = None) -> bytes:
+    prof = load_target_profile(profile) if isinstance(profile, str) else profile
+    data, _ = build_spk(graph, prof, quant_params=quant_params)
+    return data
+
+
+def _compiler_hash() -> str:
+    h = hashlib.sha256()
+    here = Path(__file__).resolve().parent
+    for p in sorted(here.rglob("*")):
+        if p.suffix in (".py", ".json") and "__pycache__" not in p.parts:
+            h.update(p.name.encode())
+            h.update(p.read_bytes())
+    return h.hexdigest()[:16]
+
+
+def compile_config(name: str, batch: int, targets=("cuda_b200",), *, seed: int = 0, int8: bool = False,
+                   calib_images: int = 32, use_cache: bool = True) -> dict[str, bytes]:
+    """Build config `name` at `batch` and package it for each target profile."""
+    key = f"{name}_b{batch}_s{seed}{'_int8' if int8 else ''}_{_compiler_hash()}"
+    out: dict[str, bytes] = {}
+    missing = []
+    for t in targets:
+        path = CACHE_DIR / f"{key}_{t}.spk"
+        if use_cache and path.exists():
+            out[t] = path.read_bytes()
+        else:
+            missing.append(t)
+    if not missing:
+        return out
+    graph = fuse(builders.build_config(name, batch, seed))
+    quant = None
+    if int8:
+        from .quantize import quantize_int8_model
+        graph, quant = quantize_int8_model(graph, calib_images=calib_images, seed=seed + 1000)
+    for t in missing:
+        data = package(copy.deepcopy(graph), t, quant_params=quant)
+        out[t] = data
+        if use_cache:
+            CACHE_DIR.mkdir(parents=True, exist_ok=True)
+            tmp = CACHE_DIR / f".{key}_{t}.{os.getpid()}.tmp"
+            tmp.write_bytes(data)
+            tmp.replace(CACHE_DIR / f"{key}_{t}.spk")
+    return out

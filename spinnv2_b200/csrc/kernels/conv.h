@@ -1,0 +1,56 @@
+// Conv node plan shared by the CUDA-core (SIMT) and tcgen05 conv kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace spkv2 {
+
+// Numeric mode of a conv node, from the dtypes of x / w / y.
+enum ConvMode : int {
+  kConvF32 = 0,     // fp32 x, fp32 w -> fp32 y
+  kConvF32ToI8 = 1, // fp32 x, fp32 w -> int8 y   (quantising epilogue)
+  kConvI8 = 2,      // int8 x, int8 w -> int8 y   (int32 acc, requantised)
+};
+
+// Geometry and epilogue parameters, passed by value to the kernels.
+struct ConvGeo {
+  int N, C, H, W;       // input
+  int M, OH, OW;        // output channels and spatial size
+  int KH, KW, sh, sw, ph, pw, dh, dw;
+  int groups, Cg, Mg;   // per-group input / output channels
+  int K;                // KH * KW * Cg, ordered (r, s, c) with c fastest
+  int64_t P;            // N * OH * OW output pixels
+  int64_t xs[4], ys[4], rs[4];  // element strides (n, c, h, w) of x, y, residual
+  int act;              // 0 none, 1 Relu, 2 SiLU
+  int has_bias, has_res;
+  float out_scale_inv;  // 1 / s_y            (kConvF32ToI8)
+  float res_scale;      // s_r / s_y          (kConvI8 with residual)
+};
+
+struct ConvPlan : NodePlan {
+  ConvGeo g{};
+  int mode = kConvF32;
+  int math = 0;            // SPKV2_CUDA_MATH_* actually used
+  void *w_simt = nullptr;  // [groups][K][Mg] packed weights (fp32 or int8)
+  void *w_tc = nullptr;    // tcgen05 operand panels (see conv_tc.cu)
+  int32_t *bias_q = nullptr;  // int32 requantisation bias (kConvI8)
+  float *scale_m = nullptr;   // per-channel requant multiplier M[c] (kConvI8)
+  const float *bias_f = nullptr;  // fp32 bias (device weights)
+  int tc_block_n = 0;      // tcgen05 tile width in output channels
+  int tc_kpad = 0;         // padded K of the tcgen05 panels
+  ~ConvPlan() override {
+    device_free(w_simt);
+    device_free(w_tc);
+    device_free(bias_q);
+    device_free(scale_m);
+  }
+};
+
+int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res, cudaStream_t s);
+
+// tcgen05 path (conv_tc.cu): returns 0 when the node is eligible and its
+// operand panels were built; SPKV2_ERR_UNSUPPORTED when the shape is not.
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, cudaStream_t s);
+int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
+
+}  // namespace spkv2

@@ -1,0 +1,199 @@
+// Gemm: Y[M,N] = alpha * op(A)[M,K] * op(B)[K,N] + C[n].
+//
+// Semantics (reference/mm/gemm.c:3-33, reference/mm/gemm_cpu_direct.c:3-37,
+// optimized/mm/gemm.c:9-85): beta is ignored, C is read as a per-column bias
+// c[n], transA/transB are honoured.
+// Device design (fp32 CUDA-core, exact fp32 products):
+//   M <= 8, no transposes  - weight-streaming GEMV: a warp reads 32 adjacent
+//     columns of B per k (coalesced), K is split over warps and blocks, and a
+//     second kernel sums the partial results in a fixed order (deterministic).
+//   otherwise, no transposes - 64x64x16 shared-memory tiles, 4x4 per thread.
+//   with transposes        - one thread per output, strided loads.
+#include <string.h>
+
+#include "common.cuh"
+
+namespace spkv2 {
+
+namespace {
+
+constexpr int kGemvMaxM = 8;
+constexpr int kGemvWarps = 8;
+
+struct GemmPlan : NodePlan {
+  int M = 0, K = 0, N = 0;
+  int trans_a = 0, trans_b = 0;
+  float alpha = 1.0f;
+  int ksplit = 1;
+  float *partials = nullptr;  // [ksplit][M][N] for the GEMV path
+  ~GemmPlan() override { device_free(partials); }
+};
+
+// grid (ceil(N/32), ksplit); block 32 x kGemvWarps.  Each block reduces its
+// warps in shared memory and writes one partial per (split, m, n).
+__global__ void gemv_partial_kernel(float *__restrict__ part, const float *__restrict__ A, const float *__restrict__ B,
+                                    int M, int K, int N, int k_per_block) {
+  __shared__ float red[kGemvWarps][kGemvMaxM][32];
+  const int lane = threadIdx.x, warp = threadIdx.y;
+  const int n = blockIdx.x * 32 + lane;
+  const int k0 = blockIdx.y * k_per_block;
+  const int k1 = min(K, k0 + k_per_block);
+  float acc[kGemvMaxM];
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) acc[m] = 0.0f;
+  if (n < N) {
+    for (int k = k0 + warp; k < k1; k += kGemvWarps) {
+      const float b = B[int64_t(k) * N + n];
+#pragma unroll
+      for (int m = 0; m < kGemvMaxM; ++m)
+        if (m < M) acc[m] = fmaf(A[int64_t(m) * K + k], b, acc[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kGemvMaxM; ++m) red[warp][m][lane] = acc[m];
+  __syncthreads();
+  if (warp == 0 && n < N) {
+    for (int m = 0; m < M; ++m) {
+      float s = 0.0f;
+      for (int w = 0; w < kGemvWarps; ++w) s += red[w][m][lane];
+      part[(int64_t(blockIdx.y) * M + m) * N + n] = s;
+    }
+  }
+}
+
+__global__ void gemv_finish_kernel(float *__restrict__ Y, const float *__restrict__ part, const float *__restrict__ bias,
+                                   int M, int N, int ksplit, float alpha) {
+  const int64_t total = int64_t(M) * N;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    float s = 0.0f;
+    for (int k = 0; k < ksplit; ++k) s += part[int64_t(k) * total + i];
+    Y[i] = alpha * s + (bias ? bias[i % N] : 0.0f);
+  }
+}
+
+// 64x64 output tile, K step 16, 256 threads each owning a 4x4 sub-tile.
+__global__ void __launch_bounds__(256) sgemm_tile_kernel(float *__restrict__ Y, const float *__restrict__ A,
+                                                         const float *__restrict__ B, const float *__restrict__ bias,
+                                                         int M, int K, int N, float alpha) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int e = tid; e < 64 * 16; e += 256) {
+      const int mm = e / 16, kk = e % 16;
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? A[int64_t(m) * K + k] : 0.0f;
+      const int kb = e / 64, nn = e % 64;
+      const int kg = k0 + kb, n = n0 + nn;
+      Bs[kb][nn] = (kg < K && n < N) ? B[int64_t(kg) * N + n] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n < N) Y[int64_t(m) * N + n] = alpha * acc[i][j] + (bias ? bias[n] : 0.0f);
+    }
+  }
+}
+
+__global__ void gemm_naive_kernel(float *__restrict__ Y, const float *__restrict__ A, const float *__restrict__ B,
+                                  const float *__restrict__ bias, int M, int K, int N, int ta, int tb, float alpha) {
+  const int64_t total = int64_t(M) * N;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int m = int(i / N), n = int(i % N);
+    float s = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float av = ta ? A[int64_t(k) * M + m] : A[int64_t(m) * K + k];
+      const float bv = tb ? B[int64_t(n) * K + k] : B[int64_t(k) * N + n];
+      s = fmaf(av, bv, s);
+    }
+    Y[i] = alpha * s + (bias ? bias[n] : 0.0f);
+  }
+}
+
+}  // namespace
+
+int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 2 || node->output_count < 1) return -3;
+  if (node->op_type != SPKV2_OP_GEMM) return SPKV2_ERR_UNSUPPORTED;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &ta = ctx->tensors[node->inputs[0]];
+  const TensorState &tb = ctx->tensors[node->inputs[1]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (ta.record->rank != 2 || tb.record->rank != 2 || ty.record->rank != 2) return -11;
+  if (ta.record->dtype != SPKV2_DTYPE_FP32 || tb.record->dtype != SPKV2_DTYPE_FP32 ||
+      ty.record->dtype != SPKV2_DTYPE_FP32)
+    return SPKV2_ERR_UNSUPPORTED;
+  GemmPlan *p = new GemmPlan();
+  p->trans_a = a.trans_a;
+  p->trans_b = a.trans_b;
+  p->alpha = a.alpha;
+  p->M = int(a.trans_a ? ta.record->shape[1] : ta.record->shape[0]);
+  p->K = int(a.trans_a ? ta.record->shape[0] : ta.record->shape[1]);
+  p->N = int(a.trans_b ? tb.record->shape[0] : tb.record->shape[1]);
+  if (!p->trans_a && !p->trans_b && p->M <= kGemvMaxM) {
+    p->ksplit = std::max(1, std::min(16, p->K / 128));
+    p->partials = static_cast<float *>(device_alloc(size_t(p->ksplit) * p->M * p->N * sizeof(float) + 16));
+    if (!p->partials) {
+      delete p;
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+    p->launches = 2;
+    p->variant = "gemv_splitk_fp32";
+  } else if (!p->trans_a && !p->trans_b) {
+    p->variant = "sgemm_tile64_fp32";
+  } else {
+    p->variant = "gemm_naive_fp32";
+  }
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int gemm_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  GemmPlan *p = node_plan<GemmPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->M == 0 || p->N == 0) return 0;
+  float *Y = reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data);
+  const float *A = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
+  const float *B = reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data);
+  const float *bias = node->input_count > 2 ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
+  if (p->partials) {
+    const int kpb = int(ceil_div(p->K, p->ksplit));
+    dim3 grid(unsigned(ceil_div(p->N, 32)), unsigned(p->ksplit));
+    gemv_partial_kernel<<<grid, dim3(32, kGemvWarps), 0, ctx->stream>>>(p->partials, A, B, p->M, p->K, p->N, kpb);
+    gemv_finish_kernel<<<grid_for(int64_t(p->M) * p->N, 256), 256, 0, ctx->stream>>>(Y, p->partials, bias, p->M, p->N,
+                                                                                      p->ksplit, p->alpha);
+  } else if (!p->trans_a && !p->trans_b) {
+    dim3 grid(unsigned(ceil_div(p->N, 64)), unsigned(ceil_div(p->M, 64)));
+    sgemm_tile_kernel<<<grid, 256, 0, ctx->stream>>>(Y, A, B, bias, p->M, p->K, p->N, p->alpha);
+  } else {
+    gemm_naive_kernel<<<grid_for(int64_t(p->M) * p->N, 256), 256, 0, ctx->stream>>>(Y, A, B, bias, p->M, p->K, p->N,
+                                                                                     p->trans_a, p->trans_b, p->alpha);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace spkv2

@@ -1,0 +1,329 @@
+// MaxPool / AveragePool / GlobalAveragePool and nearest Resize.
+//
+// Semantics (reference):
+//   MaxPool  reference/pool/maxpool.c:5-43   window max, padding skipped,
+//            -inf when the window holds no input element
+//   AveragePool reference/pool/avgpool.c     sum / (number of in-range taps)
+//   GlobalAveragePool reference/pool/avgpool.c  sum * (1 / (H*W))
+//   Resize   reference/shape/resize.c:5-31   nearest, asymmetric:
+//            ih = min(floor(oh / (OH / H)), H - 1) in fp32
+// INT8 MaxPool (quantised models) keeps the input's scale and returns the
+// largest int8 code, -128 for an empty window.
+// Device design: one thread per output element (four channels per thread
+// when both tensors are NHWC with C % 4 == 0), iterating the output in its
+// physical order so stores coalesce; NHWC reads are coalesced along C.
+#include <string.h>
+
+#include "common.cuh"
+
+namespace spkv2 {
+
+namespace {
+
+struct Geo {
+  int N, C, H, W, OH, OW;
+  int kh, kw, sh, sw, ph, pw;
+  // element strides (n, c, h, w) of input and output
+  int64_t xs[4], ys[4];
+};
+
+enum PoolKind : int { kMax, kAvg, kGlobalAvg };
+
+struct PoolPlan : NodePlan {
+  Geo g;
+  int kind = kMax;
+  int vec = 1;
+  bool out_nhwc = false;
+  bool is_int8 = false;
+};
+
+template <typename T>
+struct PoolTraits;
+template <>
+struct PoolTraits<float> {
+  __device__ static float lowest() { return -INFINITY; }
+};
+template <>
+struct PoolTraits<int8_t> {
+  __device__ static int8_t lowest() { return -128; }
+};
+
+// Output coordinate of linear index i in the output's physical order.
+__device__ __forceinline__ void out_coords(int64_t i, const Geo &g, bool nhwc, int C, int &n, int &c, int &oh,
+                                           int &ow) {
+  if (nhwc) {
+    c = int(i % C);
+    i /= C;
+    ow = int(i % g.OW);
+    i /= g.OW;
+    oh = int(i % g.OH);
+    n = int(i / g.OH);
+  } else {
+    ow = int(i % g.OW);
+    i /= g.OW;
+    oh = int(i % g.OH);
+    i /= g.OH;
+    c = int(i % C);
+    n = int(i / C);
+  }
+}
+
+template <typename T>
+__global__ void pool_kernel(T *__restrict__ y, const T *__restrict__ x, Geo g, int kind, bool out_nhwc,
+                            int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int n, c, oh, ow;
+    out_coords(i, g, out_nhwc, g.C, n, c, oh, ow);
+    const T *xb = x + n * g.xs[0] + c * g.xs[1];
+    float acc = 0.0f;
+    T best = PoolTraits<T>::lowest();
+    int count = 0;
+    for (int r = 0; r < g.kh; ++r) {
+      const int ih = oh * g.sh + r - g.ph;
+      if (ih < 0 || ih >= g.H) continue;
+      for (int s = 0; s < g.kw; ++s) {
+        const int iw = ow * g.sw + s - g.pw;
+        if (iw < 0 || iw >= g.W) continue;
+        const T v = xb[ih * g.xs[2] + iw * g.xs[3]];
+        if (kind == kMax) {
+          if (v > best) best = v;
+        } else {
+          acc += float(v);
+          ++count;
+        }
+      }
+    }
+    T out;
+    if (kind == kMax)
+      out = best;
+    else if (kind == kAvg)
+      out = T(count > 0 ? acc / float(count) : 0.0f);
+    else
+      out = T(acc * (1.0f / float(g.H * g.W)));
+    y[n * g.ys[0] + c * g.ys[1] + oh * g.ys[2] + ow * g.ys[3]] = out;
+  }
+}
+
+// Both tensors NHWC, C % 4 == 0, fp32 max pooling: one float4 of channels
+// per thread.
+__global__ void maxpool_nhwc4_kernel(float *__restrict__ y, const float *__restrict__ x, Geo g, int64_t total4) {
+  const int C4 = g.C / 4;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c4 = int(r % C4);
+    r /= C4;
+    const int ow = int(r % g.OW);
+    r /= g.OW;
+    const int oh = int(r % g.OH);
+    const int n = int(r / g.OH);
+    float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    const float *xb = x + int64_t(n) * g.H * g.W * g.C + c4 * 4;
+    for (int rr = 0; rr < g.kh; ++rr) {
+      const int ih = oh * g.sh + rr - g.ph;
+      if (ih < 0 || ih >= g.H) continue;
+      for (int s = 0; s < g.kw; ++s) {
+        const int iw = ow * g.sw + s - g.pw;
+        if (iw < 0 || iw >= g.W) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(xb + (int64_t(ih) * g.W + iw) * g.C);
+        best.x = v.x > best.x ? v.x : best.x;
+        best.y = v.y > best.y ? v.y : best.y;
+        best.z = v.z > best.z ? v.z : best.z;
+        best.w = v.w > best.w ? v.w : best.w;
+      }
+    }
+    reinterpret_cast<float4 *>(y)[i] = best;
+  }
+}
+
+void strides_of(const TensorState &t, int64_t s[4]) {
+  View v = make_view(t);
+  for (int i = 0; i < 4; ++i) s[i] = v.stride[i];
+}
+
+struct ResizeGeo {
+  int N, C, H, W, OH, OW;
+  int64_t xs[4], ys[4];
+  bool out_nhwc;
+};
+
+struct ResizePlan : NodePlan {
+  ResizeGeo g;
+  bool vec4 = false;
+  int esize = 4;
+};
+
+template <typename T>
+__global__ void resize_nearest_kernel(T *__restrict__ y, const T *__restrict__ x, ResizeGeo g, int64_t total) {
+  const float scale_h = float(g.OH) / float(g.H);
+  const float scale_w = float(g.OW) / float(g.W);
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    int n, c, oh, ow;
+    if (g.out_nhwc) {
+      c = int(r % g.C);
+      r /= g.C;
+      ow = int(r % g.OW);
+      r /= g.OW;
+      oh = int(r % g.OH);
+      n = int(r / g.OH);
+    } else {
+      ow = int(r % g.OW);
+      r /= g.OW;
+      oh = int(r % g.OH);
+      r /= g.OH;
+      c = int(r % g.C);
+      n = int(r / g.C);
+    }
+    int ih = int(floorf(float(oh) / scale_h));
+    if (ih >= g.H) ih = g.H - 1;
+    int iw = int(floorf(float(ow) / scale_w));
+    if (iw >= g.W) iw = g.W - 1;
+    y[n * g.ys[0] + c * g.ys[1] + oh * g.ys[2] + ow * g.ys[3]] =
+        x[n * g.xs[0] + c * g.xs[1] + ih * g.xs[2] + iw * g.xs[3]];
+  }
+}
+
+__global__ void resize_nearest_nhwc4_kernel(float4 *__restrict__ y, const float4 *__restrict__ x, ResizeGeo g,
+                                            int64_t total4) {
+  const float scale_h = float(g.OH) / float(g.H);
+  const float scale_w = float(g.OW) / float(g.W);
+  const int C4 = g.C / 4;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c4 = int(r % C4);
+    r /= C4;
+    const int ow = int(r % g.OW);
+    r /= g.OW;
+    const int oh = int(r % g.OH);
+    const int n = int(r / g.OH);
+    int ih = int(floorf(float(oh) / scale_h));
+    if (ih >= g.H) ih = g.H - 1;
+    int iw = int(floorf(float(ow) / scale_w));
+    if (iw >= g.W) iw = g.W - 1;
+    y[i] = x[((int64_t(n) * g.H + ih) * g.W + iw) * C4 + c4];
+  }
+}
+
+}  // namespace
+
+int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *spec) {
+  (void)spec;
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (tx.record->rank != 4 || ty.record->rank != 4) return -11;
+  if (tx.record->dtype != ty.record->dtype) return SPKV2_ERR_UNSUPPORTED;
+  const bool is_int8 = tx.record->dtype == SPKV2_DTYPE_INT8;
+  if (!is_int8 && tx.record->dtype != SPKV2_DTYPE_FP32) return SPKV2_ERR_UNSUPPORTED;
+  PoolPlan *p = new PoolPlan();
+  p->kind = node->op_type == SPKV2_OP_MAXPOOL ? kMax : node->op_type == SPKV2_OP_AVERAGEPOOL ? kAvg : kGlobalAvg;
+  if (is_int8 && p->kind != kMax) {
+    delete p;
+    return SPKV2_ERR_UNSUPPORTED;
+  }
+  Geo &g = p->g;
+  memset(&g, 0, sizeof(g));
+  g.N = int(tx.record->shape[0]);
+  g.C = int(tx.record->shape[1]);
+  g.H = int(tx.record->shape[2]);
+  g.W = int(tx.record->shape[3]);
+  g.OH = int(ty.record->shape[2]);
+  g.OW = int(ty.record->shape[3]);
+  if (p->kind == kGlobalAvg) {
+    g.kh = g.H;
+    g.kw = g.W;
+    g.sh = g.sw = 1;
+  } else {
+    Spkv2AttrRecord a;
+    int rc = get_attr(ctx, node, &a);
+    if (rc) {
+      delete p;
+      return rc;
+    }
+    g.kh = a.kernel_shape[0];
+    g.kw = a.kernel_shape[1];
+    g.sh = a.strides[0];
+    g.sw = a.strides[1];
+    g.ph = a.pads[0];
+    g.pw = a.pads[1];
+  }
+  strides_of(tx, g.xs);
+  strides_of(ty, g.ys);
+  p->out_nhwc = ty.layout == kNHWC;
+  p->is_int8 = is_int8;
+  p->vec = (!is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 4 == 0) ? 4 : 1;
+  p->variant = p->vec == 4 ? "maxpool_nhwc_vec4" : "pool_generic";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int pool_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
+  (void)scratch;
+  PoolPlan *p = node_plan<PoolPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  const Geo &g = p->g;
+  const int64_t total = int64_t(g.N) * g.C * g.OH * g.OW;
+  if (total == 0) return 0;
+  void *y = ctx->tensors[node->outputs[0]].data;
+  const void *x = ctx->tensors[node->inputs[0]].data;
+  if (p->vec == 4) {
+    maxpool_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
+        static_cast<float *>(y), static_cast<const float *>(x), g, total / 4);
+  } else if (p->is_int8) {
+    pool_kernel<int8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+        static_cast<int8_t *>(y), static_cast<const int8_t *>(x), g, p->kind, p->out_nhwc, total);
+  } else {
+    pool_kernel<float><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+        static_cast<float *>(y), static_cast<const float *>(x), g, p->kind, p->out_nhwc, total);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+int resize_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *spec) {
+  (void)spec;
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (tx.record->rank != 4 || ty.record->rank != 4) return -11;
+  if (tx.record->dtype != ty.record->dtype) return SPKV2_ERR_UNSUPPORTED;
+  ResizePlan *p = new ResizePlan();
+  ResizeGeo &g = p->g;
+  g.N = int(ty.record->shape[0]);
+  g.C = int(ty.record->shape[1]);
+  g.OH = int(ty.record->shape[2]);
+  g.OW = int(ty.record->shape[3]);
+  g.H = int(tx.record->shape[2]);
+  g.W = int(tx.record->shape[3]);
+  strides_of(tx, g.xs);
+  strides_of(ty, g.ys);
+  g.out_nhwc = ty.layout == kNHWC;
+  p->esize = int(dtype_size(ty.record->dtype));
+  p->vec4 = p->esize == 4 && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 4 == 0;
+  p->variant = p->vec4 ? "resize_nearest_nhwc_vec4" : "resize_nearest_generic";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int resize_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
+  (void)scratch;
+  ResizePlan *p = node_plan<ResizePlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  const ResizeGeo &g = p->g;
+  const int64_t total = int64_t(g.N) * g.C * g.OH * g.OW;
+  if (total == 0) return 0;
+  void *y = ctx->tensors[node->outputs[0]].data;
+  const void *x = ctx->tensors[node->inputs[0]].data;
+  if (p->vec4) {
+    resize_nearest_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
+        static_cast<float4 *>(y), static_cast<const float4 *>(x), g, total / 4);
+  } else if (p->esize == 1) {
+    resize_nearest_kernel<uint8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+        static_cast<uint8_t *>(y), static_cast<const uint8_t *>(x), g, total);
+  } else {
+    resize_nearest_kernel<uint32_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+        static_cast<uint32_t *>(y), static_cast<const uint32_t *>(x), g, total);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace spkv2

@@ -1,0 +1,394 @@
+// ReduceMean / ReduceMax, Softmax and TopK.
+//
+// Semantics (reference):
+//   Reduce  reference/reduce/reduce.c:5-45   axes from input[1] (fp32 data),
+//           else attr.extra, else all dims; keepdims; ReduceMax starts at -inf;
+//           ReduceMean adds x/denom element by element in row-major order
+//           (denom = fp32 product of the reduced dims).  INT8 ReduceMean (the
+//           quantised models' global pool) sums the codes exactly in int32 and
+//           returns (float)sum * (s_x / denom) with the factor formed in fp32.
+//   Softmax reference/activation/softmax.c:5-41   max-shifted expf, divide by
+//           the sum
+//   TopK    reference/tensor/topk.c:5-124   k from input[1]; values and fp32
+//           indices sorted (descending if largest), ties to the smaller index,
+//           equal values at the k-th place keep the earlier indices
+// Device design: reductions run one thread per output element looping over
+// the reduced index space in the reference's order (bit-exact with it); the
+// threads of a warp take adjacent outputs, so NHWC global pooling reads
+// coalesce along C.  Softmax uses a warp per row when the axis is innermost.
+// TopK sorts each row's (value, index) keys with a shared-memory bitonic
+// sort, one block per row.
+#include <string.h>
+
+#include "common.cuh"
+
+namespace spkv2 {
+
+namespace {
+
+struct ReduceDesc {
+  int keep_rank;
+  int64_t keep_dim[kMaxRank];
+  int64_t keep_xstride[kMaxRank];
+  int64_t keep_ystride[kMaxRank];
+  int red_rank;
+  int64_t red_dim[kMaxRank];
+  int64_t red_xstride[kMaxRank];
+  float denom;
+};
+
+struct ReducePlan : NodePlan {
+  ReduceDesc d;
+  bool is_max = false;
+  bool int8_in = false;
+  float int8_factor = 1.0f;
+  int64_t outputs = 0;
+};
+
+template <bool IS_MAX>
+__global__ void reduce_kernel(float *__restrict__ y, const float *__restrict__ x, ReduceDesc d, int64_t outputs,
+                              int64_t red_count) {
+  for (int64_t o = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; o < outputs; o += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = o, xb = 0, yo = 0;
+    for (int k = d.keep_rank - 1; k >= 0; --k) {
+      const int64_t c = rem % d.keep_dim[k];
+      rem /= d.keep_dim[k];
+      xb += c * d.keep_xstride[k];
+      yo += c * d.keep_ystride[k];
+    }
+    float acc = IS_MAX ? -INFINITY : 0.0f;
+    for (int64_t r = 0; r < red_count; ++r) {
+      int64_t rr = r, xo = xb;
+      for (int k = d.red_rank - 1; k >= 0; --k) {
+        xo += (rr % d.red_dim[k]) * d.red_xstride[k];
+        rr /= d.red_dim[k];
+      }
+      const float v = x[xo];
+      if (IS_MAX) {
+        if (v > acc) acc = v;
+      } else {
+        acc += v / d.denom;
+      }
+    }
+    y[yo] = acc;
+  }
+}
+
+__global__ void reduce_mean_i8_kernel(float *__restrict__ y, const int8_t *__restrict__ x, ReduceDesc d,
+                                      int64_t outputs, int64_t red_count, float factor) {
+  for (int64_t o = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; o < outputs; o += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = o, xb = 0, yo = 0;
+    for (int k = d.keep_rank - 1; k >= 0; --k) {
+      const int64_t c = rem % d.keep_dim[k];
+      rem /= d.keep_dim[k];
+      xb += c * d.keep_xstride[k];
+      yo += c * d.keep_ystride[k];
+    }
+    int32_t acc = 0;
+    for (int64_t r = 0; r < red_count; ++r) {
+      int64_t rr = r, xo = xb;
+      for (int k = d.red_rank - 1; k >= 0; --k) {
+        xo += (rr % d.red_dim[k]) * d.red_xstride[k];
+        rr /= d.red_dim[k];
+      }
+      acc += x[xo];
+    }
+    y[yo] = __fmul_rn(float(acc), factor);
+  }
+}
+
+// ---------------- Softmax ----------------
+
+struct SoftmaxPlan : NodePlan {
+  int64_t outer = 1, dim = 1, inner = 1;
+};
+
+__global__ void softmax_rows_kernel(float *__restrict__ y, const float *__restrict__ x, int64_t rows, int64_t dim) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t row = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; row < rows; row += warps) {
+    const float *xr = x + row * dim;
+    float *yr = y + row * dim;
+    float m = -INFINITY;
+    for (int64_t i = lane; i < dim; i += 32) m = fmaxf(m, xr[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+    for (int64_t i = lane; i < dim; i += 32) {
+      const float e = expf(xr[i] - m);
+      yr[i] = e;
+      s += e;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __syncwarp();
+    for (int64_t i = lane; i < dim; i += 32) yr[i] = yr[i] / s;
+  }
+}
+
+__global__ void softmax_strided_kernel(float *__restrict__ y, const float *__restrict__ x, int64_t outer, int64_t dim,
+                                       int64_t inner) {
+  const int64_t total = outer * inner;
+  for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t o = t / inner, in = t % inner;
+    const float *xr = x + o * dim * inner + in;
+    float *yr = y + o * dim * inner + in;
+    float m = -INFINITY;
+    for (int64_t d = 0; d < dim; ++d) m = fmaxf(m, xr[d * inner]);
+    float s = 0.0f;
+    for (int64_t d = 0; d < dim; ++d) {
+      const float e = expf(xr[d * inner] - m);
+      yr[d * inner] = e;
+      s += e;
+    }
+    for (int64_t d = 0; d < dim; ++d) yr[d * inner] = yr[d * inner] / s;
+  }
+}
+
+// ---------------- TopK ----------------
+
+constexpr int kTopkMaxPow2 = 16384;
+
+struct TopkPlan : NodePlan {
+  int64_t outer = 1, dim = 1, inner = 1, k = 0;
+  int largest = 1;
+  int pow2 = 1;
+  int64_t x_axis_stride = 1;
+};
+
+// Unsigned key whose order is the float order; -0 and +0 share a key so they
+// tie (and fall back to the index) as they compare equal in the reference.
+__device__ __forceinline__ uint32_t float_order_key(float v) {
+  const uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void topk_kernel(float *__restrict__ values, float *__restrict__ indices, const float *__restrict__ x,
+                            int64_t dim, int64_t inner, int64_t k, int largest, int pow2) {
+  extern __shared__ unsigned long long keys[];
+  const int64_t row = blockIdx.x;
+  const int64_t o = row / inner, in = row % inner;
+  const float *xr = x + o * dim * inner + in;
+  for (int i = threadIdx.x; i < pow2; i += blockDim.x) {
+    unsigned long long key = ~0ull;
+    if (i < dim) {
+      uint32_t hi = float_order_key(xr[int64_t(i) * inner]);
+      if (largest) hi = ~hi;
+      key = (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(i);
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  for (int size = 2; size <= pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < pow2 / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const unsigned long long a = keys[lo], b = keys[hi];
+        if ((a > b) == ascending) {
+          keys[lo] = b;
+          keys[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
+    const unsigned long long key = keys[j];
+    const uint32_t idx = static_cast<uint32_t>(key & 0xffffffffu);
+    values[(o * k + j) * inner + in] = xr[int64_t(idx) * inner];
+    indices[(o * k + j) * inner + in] = float(idx);
+  }
+}
+
+// Reads a small constant tensor (axes, k) from the package's host weights.
+const float *host_weight_f32(const Spkv2Context *ctx, uint32_t tid, size_t *count) {
+  const Spkv2TensorRecord *r = ctx->tensors[tid].record;
+  if (r->role != SPKV2_ROLE_WEIGHT || r->dtype != SPKV2_DTYPE_FP32) return nullptr;
+  if (r->data_offset + r->size_bytes > ctx->weights_size) return nullptr;
+  *count = elem_count(r);
+  return reinterpret_cast<const float *>(ctx->weights + r->data_offset);
+}
+
+}  // namespace
+
+int reduce_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  const int rank = tx.record->rank;
+  int axes[kMaxRank];
+  int naxes = 0;
+  if (node->input_count > 1) {
+    size_t n = 0;
+    const float *v = host_weight_f32(ctx, node->inputs[1], &n);
+    if (!v) return SPKV2_ERR_UNSUPPORTED;
+    if (n > size_t(kMaxRank)) return -11;
+    for (size_t i = 0; i < n; ++i) axes[naxes++] = int(v[i]) < 0 ? int(v[i]) + rank : int(v[i]);
+  } else if (a.extra_count > 0) {
+    if (a.extra_count > kMaxRank) return -11;
+    for (int i = 0; i < a.extra_count; ++i) axes[naxes++] = a.extra[i] < 0 ? a.extra[i] + rank : a.extra[i];
+  } else {
+    for (int i = 0; i < rank; ++i) axes[naxes++] = i;
+  }
+  auto reduced = [&](int d) {
+    for (int i = 0; i < naxes; ++i)
+      if (axes[i] == d) return true;
+    return false;
+  };
+  const View vx = make_view(tx), vy = make_view(ty);
+  ReducePlan *p = new ReducePlan();
+  ReduceDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  p->is_max = node->op_type == SPKV2_OP_REDUCEMAX;
+  p->int8_in = tx.record->dtype == SPKV2_DTYPE_INT8;
+  if (ty.record->dtype != SPKV2_DTYPE_FP32 || (p->int8_in && p->is_max) ||
+      (!p->int8_in && tx.record->dtype != SPKV2_DTYPE_FP32)) {
+    delete p;
+    return SPKV2_ERR_UNSUPPORTED;
+  }
+  float denom = 1.0f;
+  int yd = 0;
+  for (int xd = 0; xd < rank; ++xd) {
+    if (reduced(xd)) {
+      d.red_dim[d.red_rank] = vx.dim[xd];
+      d.red_xstride[d.red_rank] = vx.stride[xd];
+      d.red_rank++;
+      denom *= float(vx.dim[xd]);
+      if (a.keepdims) yd++;
+    } else {
+      if (yd >= vy.rank) {
+        delete p;
+        return -11;
+      }
+      d.keep_dim[d.keep_rank] = vx.dim[xd];
+      d.keep_xstride[d.keep_rank] = vx.stride[xd];
+      d.keep_ystride[d.keep_rank] = vy.stride[yd];
+      d.keep_rank++;
+      yd++;
+    }
+  }
+  d.denom = denom;
+  p->outputs = 1;
+  for (int k = 0; k < d.keep_rank; ++k) p->outputs *= d.keep_dim[k];
+  if (p->int8_in) {
+    const float *sx = quant_scales(ctx, find_quant_param(ctx, node->inputs[0]));
+    if (!sx) {
+      delete p;
+      return SPKV2_ERR_UNSUPPORTED;
+    }
+    p->int8_factor = sx[0] / denom;  // fp32 division on the host, one rounding
+  }
+  p->variant = p->int8_in ? "reduce_mean_int8" : (p->is_max ? "reduce_max" : "reduce_mean");
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int reduce_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  ReducePlan *p = node_plan<ReducePlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->outputs == 0) return 0;
+  int64_t red = 1;
+  for (int k = 0; k < p->d.red_rank; ++k) red *= p->d.red_dim[k];
+  float *y = reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data);
+  const void *x = ctx->tensors[node->inputs[0]].data;
+  const int g = grid_for(p->outputs, 128);
+  if (p->int8_in)
+    reduce_mean_i8_kernel<<<g, 128, 0, ctx->stream>>>(y, static_cast<const int8_t *>(x), p->d, p->outputs, red,
+                                                      p->int8_factor);
+  else if (p->is_max)
+    reduce_kernel<true><<<g, 128, 0, ctx->stream>>>(y, static_cast<const float *>(x), p->d, p->outputs, red);
+  else
+    reduce_kernel<false><<<g, 128, 0, ctx->stream>>>(y, static_cast<const float *>(x), p->d, p->outputs, red);
+  return cuda_status(cudaGetLastError());
+}
+
+int softmax_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (tx.layout != kRowMajor || ty.layout != kRowMajor) return SPKV2_ERR_UNSUPPORTED;
+  if (tx.record->dtype != SPKV2_DTYPE_FP32) return SPKV2_ERR_UNSUPPORTED;
+  const int rank = tx.record->rank;
+  const int axis = a.axis < 0 ? a.axis + rank : a.axis;
+  if (axis < 0 || axis >= rank) return -11;
+  SoftmaxPlan *p = new SoftmaxPlan();
+  for (int i = 0; i < axis; ++i) p->outer *= tx.record->shape[i];
+  p->dim = tx.record->shape[axis];
+  for (int i = axis + 1; i < rank; ++i) p->inner *= tx.record->shape[i];
+  p->variant = p->inner == 1 ? "softmax_warp_rows" : "softmax_strided";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int softmax_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  SoftmaxPlan *p = node_plan<SoftmaxPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  float *y = reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data);
+  const float *x = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
+  if (p->outer * p->inner == 0 || p->dim == 0) return 0;
+  if (p->inner == 1)
+    softmax_rows_kernel<<<grid_for(p->outer * 32, 256), 256, 0, ctx->stream>>>(y, x, p->outer, p->dim);
+  else
+    softmax_strided_kernel<<<grid_for(p->outer * p->inner, 128), 128, 0, ctx->stream>>>(y, x, p->outer, p->dim,
+                                                                                         p->inner);
+  return cuda_status(cudaGetLastError());
+}
+
+int topk_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 2 || node->output_count < 2) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  if (tx.layout != kRowMajor || tx.record->dtype != SPKV2_DTYPE_FP32) return SPKV2_ERR_UNSUPPORTED;
+  for (int i = 0; i < 2; ++i)
+    if (ctx->tensors[node->outputs[i]].layout != kRowMajor) return SPKV2_ERR_UNSUPPORTED;
+  size_t kn = 0;
+  const float *kv = host_weight_f32(ctx, node->inputs[1], &kn);
+  if (!kv || kn < 1) return SPKV2_ERR_UNSUPPORTED;
+  const int rank = tx.record->rank;
+  const int axis = a.axis < 0 ? a.axis + rank : a.axis;
+  if (axis < 0 || axis >= rank) return -11;
+  TopkPlan *p = new TopkPlan();
+  for (int i = 0; i < axis; ++i) p->outer *= tx.record->shape[i];
+  p->dim = tx.record->shape[axis];
+  for (int i = axis + 1; i < rank; ++i) p->inner *= tx.record->shape[i];
+  p->k = int64_t(size_t(kv[0]));
+  if (p->k > p->dim) p->k = p->dim;
+  p->largest = a.largest;
+  p->pow2 = 1;
+  while (p->pow2 < p->dim) p->pow2 <<= 1;
+  if (p->pow2 > kTopkMaxPow2) {
+    delete p;
+    return SPKV2_ERR_UNSUPPORTED;
+  }
+  const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  p->variant = "topk_bitonic";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int topk_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  TopkPlan *p = node_plan<TopkPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->k == 0 || p->dim == 0) return 0;
+  const int64_t rows = p->outer * p->inner;
+  if (rows == 0) return 0;
+  const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
+  topk_kernel<<<unsigned(rows), 1024, smem, ctx->stream>>>(
+      reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data),
+      reinterpret_cast<float *>(ctx->tensors[node->outputs[1]].data),
+      reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data), p->dim, p->inner, p->k, p->largest,
+      p->pow2);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace spkv2

@@ -1,0 +1,365 @@
+// Concat, Split, Transpose, Tile and GatherElements.
+//
+// Semantics (reference):
+//   Concat  reference/tensor/concat.c:5-30   inputs stacked along `axis`
+//   Split   reference/tensor/split.c:5-30    output sizes from the output
+//           records along `axis`
+//   Transpose reference/shape/transpose.c:3  y[coords] = x[coords permuted by
+//           attr.extra]; with no perm attribute the mapping is the identity
+//   Tile    reference/shape/tile.c            x coord = y coord mod x dim
+//   GatherElements reference/tensor/gather_elements.c:3-25  fp32 indices,
+//           negative indices wrap by the axis size
+// Device design: every kernel walks one tensor in physical order and reaches
+// the others through per-dim strides, so NHWC and NCHW operands mix freely;
+// Concat/Split move four elements per thread when the innermost physical dim
+// allows it.  Concat inputs that the memory plan placed inside the output
+// (sub-region aliases) are copied onto themselves, which is a no-op.
+#include <string.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace spkv2 {
+
+namespace {
+
+constexpr int kMaxParts = 8;
+
+struct PartDesc {
+  int rank;                      // iteration rank (physical order of the big tensor)
+  int64_t dim[kMaxRank];         // big tensor dims in iteration order
+  int64_t big_stride[kMaxRank];  // big tensor strides in iteration order
+  int axis_pos;                  // position of the axis in iteration order
+  int parts;
+  int64_t begin[kMaxParts + 1];  // axis offset of each part
+  int64_t part_stride[kMaxParts][kMaxRank];
+  void *ptr[kMaxParts];
+};
+
+struct PartPlan : NodePlan {
+  PartDesc d;
+  int vec = 1;
+  int esize = 4;
+  int64_t total = 0;
+};
+
+// GATHER (Concat): big = output, parts = inputs.  Split: big = input,
+// parts = outputs.
+template <typename T, int V, bool GATHER>
+__global__ void part_kernel(T *big, PartDesc d, int64_t total) {
+  typedef typename std::conditional<sizeof(T) == 4, float4, char4>::type VT;
+  const int64_t inner = d.dim[d.rank - 1] / V;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i;
+    int64_t coord[kMaxRank];
+    coord[d.rank - 1] = (rem % inner) * V;
+    rem /= inner;
+    for (int k = d.rank - 2; k >= 0; --k) {
+      coord[k] = rem % d.dim[k];
+      rem /= d.dim[k];
+    }
+    const int64_t a = coord[d.axis_pos];
+    int p = 0;
+    while (p + 1 < d.parts && a >= d.begin[p + 1]) ++p;
+    int64_t ob = 0, op = 0;
+    for (int k = 0; k < d.rank; ++k) {
+      ob += coord[k] * d.big_stride[k];
+      op += (k == d.axis_pos ? a - d.begin[p] : coord[k]) * d.part_stride[p][k];
+    }
+    T *part = static_cast<T *>(d.ptr[p]);
+    if (V == 4) {
+      if (GATHER)
+        *reinterpret_cast<VT *>(big + ob) = *reinterpret_cast<const VT *>(part + op);
+      else
+        *reinterpret_cast<VT *>(part + op) = *reinterpret_cast<const VT *>(big + ob);
+    } else {
+      if (GATHER)
+        big[ob] = part[op];
+      else
+        part[op] = big[ob];
+    }
+  }
+}
+
+int prepare_parts(Spkv2Context *ctx, const Spkv2NodeRecord *node, bool concat) {
+  Spkv2AttrRecord attr;
+  int rc = get_attr(ctx, node, &attr);
+  if (rc) return rc;
+  const uint16_t nparts = concat ? node->input_count : node->output_count;
+  if (nparts < 1 || nparts > kMaxParts) return SPKV2_ERR_UNSUPPORTED;
+  const TensorState &big = ctx->tensors[concat ? node->outputs[0] : node->inputs[0]];
+  const int rank = big.record->rank;
+  const int axis = attr.axis < 0 ? attr.axis + rank : attr.axis;
+  if (axis < 0 || axis >= rank) return -11;
+  const View vb = make_view(big);
+  int order[kMaxRank];
+  for (int i = 0; i < rank; ++i) order[i] = i;
+  std::stable_sort(order, order + rank, [&](int a, int b) { return vb.stride[a] > vb.stride[b]; });
+  PartPlan *p = new PartPlan();
+  PartDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  d.rank = rank;
+  d.parts = nparts;
+  for (int j = 0; j < rank; ++j) {
+    d.dim[j] = vb.dim[order[j]];
+    d.big_stride[j] = vb.stride[order[j]];
+    if (order[j] == axis) d.axis_pos = j;
+  }
+  const size_t esize = dtype_size(big.record->dtype);
+  // Four elements per thread need: big innermost stride 1 and extent % 4,
+  // every other stride of every tensor % 4, parts contiguous innermost,
+  // part extents along an innermost axis % 4, 4-element-aligned pointers.
+  bool vec = d.big_stride[rank - 1] == 1 && d.dim[rank - 1] % 4 == 0 &&
+             reinterpret_cast<uintptr_t>(big.data) % (4 * esize) == 0;
+  for (int j = 0; j + 1 < rank; ++j) vec = vec && d.big_stride[j] % 4 == 0;
+  int64_t off = 0;
+  for (int k = 0; k < nparts; ++k) {
+    const TensorState &t = ctx->tensors[concat ? node->inputs[k] : node->outputs[k]];
+    if (t.record->rank != rank || t.record->dtype != big.record->dtype) {
+      delete p;
+      return SPKV2_ERR_UNSUPPORTED;
+    }
+    const View vp = make_view(t);
+    for (int j = 0; j < rank; ++j)
+      if (j != axis && vp.dim[j] != vb.dim[j]) {
+        delete p;
+        return -3;
+      }
+    d.begin[k] = off;
+    off += vp.dim[axis];
+    for (int j = 0; j < rank; ++j) d.part_stride[k][j] = vp.stride[order[j]];
+    vec = vec && d.part_stride[k][rank - 1] == 1 && reinterpret_cast<uintptr_t>(t.data) % (4 * esize) == 0;
+    for (int j = 0; j + 1 < rank; ++j) vec = vec && d.part_stride[k][j] % 4 == 0;
+    if (d.axis_pos == rank - 1) vec = vec && vp.dim[axis] % 4 == 0;
+  }
+  d.begin[nparts] = off;
+  if (off != vb.dim[axis]) {
+    delete p;
+    return -3;
+  }
+  p->vec = vec ? 4 : 1;
+  p->esize = int(esize);
+  p->total = vb.count() / p->vec;
+  p->variant = vec ? (concat ? "concat_vec4" : "split_vec4") : (concat ? "concat" : "split");
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+template <bool GATHER>
+int run_parts(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  PartPlan *p = node_plan<PartPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->total == 0) return 0;
+  PartDesc d = p->d;
+  for (int k = 0; k < d.parts; ++k) d.ptr[k] = ctx->tensors[GATHER ? node->inputs[k] : node->outputs[k]].data;
+  void *big = ctx->tensors[GATHER ? node->outputs[0] : node->inputs[0]].data;
+  const int g = grid_for(p->total, 256);
+  if (p->esize == 1) {
+    if (p->vec == 4)
+      part_kernel<int8_t, 4, GATHER><<<g, 256, 0, ctx->stream>>>(static_cast<int8_t *>(big), d, p->total);
+    else
+      part_kernel<int8_t, 1, GATHER><<<g, 256, 0, ctx->stream>>>(static_cast<int8_t *>(big), d, p->total);
+  } else {
+    if (p->vec == 4)
+      part_kernel<float, 4, GATHER><<<g, 256, 0, ctx->stream>>>(static_cast<float *>(big), d, p->total);
+    else
+      part_kernel<float, 1, GATHER><<<g, 256, 0, ctx->stream>>>(static_cast<float *>(big), d, p->total);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+// ---------------- strided gather copy (Transpose, Tile) ----------------
+
+struct GatherDesc {
+  int rank;
+  int64_t dim[kMaxRank];      // output dims in output physical order
+  int64_t ostride[kMaxRank];  // output strides
+  int64_t istride[kMaxRank];  // input stride per output dim
+  int64_t imod[kMaxRank];     // input coordinate = output coordinate mod imod
+};
+
+struct GatherPlan : NodePlan {
+  GatherDesc d;
+  int esize = 4;
+  int64_t total = 0;
+};
+
+template <typename T>
+__global__ void gather_copy_kernel(T *__restrict__ y, const T *__restrict__ x, GatherDesc d, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i, oy = 0, ox = 0;
+    for (int k = d.rank - 1; k >= 0; --k) {
+      const int64_t c = rem % d.dim[k];
+      rem /= d.dim[k];
+      oy += c * d.ostride[k];
+      ox += (c % d.imod[k]) * d.istride[k];
+    }
+    y[oy] = x[ox];
+  }
+}
+
+// perm[d] = input dim feeding output dim d; tile=true uses the modulus.
+int prepare_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node, const int *perm, bool tile, const char *name) {
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (tx.record->dtype != ty.record->dtype || tx.record->rank != ty.record->rank) return SPKV2_ERR_UNSUPPORTED;
+  const View vx = make_view(tx), vy = make_view(ty);
+  const int rank = vy.rank;
+  int order[kMaxRank];
+  for (int i = 0; i < rank; ++i) order[i] = i;
+  std::stable_sort(order, order + rank, [&](int a, int b) { return vy.stride[a] > vy.stride[b]; });
+  GatherPlan *p = new GatherPlan();
+  GatherDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  d.rank = rank;
+  for (int j = 0; j < rank; ++j) {
+    const int od = order[j];
+    const int id = perm[od];
+    if (id < 0 || id >= rank) {
+      delete p;
+      return -11;
+    }
+    d.dim[j] = vy.dim[od];
+    d.ostride[j] = vy.stride[od];
+    d.istride[j] = vx.stride[id];
+    d.imod[j] = tile ? std::max<int64_t>(vx.dim[id], 1) : std::max<int64_t>(vy.dim[od], 1);
+  }
+  p->esize = int(dtype_size(ty.record->dtype));
+  p->total = vy.count();
+  p->variant = name;
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int run_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  GatherPlan *p = node_plan<GatherPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->total == 0) return 0;
+  void *y = ctx->tensors[node->outputs[0]].data;
+  const void *x = ctx->tensors[node->inputs[0]].data;
+  const int g = grid_for(p->total, 256);
+  if (p->esize == 1)
+    gather_copy_kernel<uint8_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint8_t *>(y), static_cast<const uint8_t *>(x),
+                                                            p->d, p->total);
+  else
+    gather_copy_kernel<uint32_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint32_t *>(y),
+                                                             static_cast<const uint32_t *>(x), p->d, p->total);
+  return cuda_status(cudaGetLastError());
+}
+
+// ---------------- GatherElements ----------------
+
+struct GEDesc {
+  int rank;
+  int axis;
+  int64_t dim[kMaxRank];      // output (= index) dims, logical order
+  int64_t ystride[kMaxRank];
+  int64_t istride[kMaxRank];
+  int64_t dstride[kMaxRank];
+  int64_t axis_dim;
+};
+
+struct GEPlan : NodePlan {
+  GEDesc d;
+  int64_t total = 0;
+};
+
+__global__ void gather_elements_kernel(float *__restrict__ y, const float *__restrict__ data,
+                                       const float *__restrict__ idx, GEDesc d, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i, oy = 0, oi = 0, od = 0;
+    int64_t coord[kMaxRank];
+    for (int k = d.rank - 1; k >= 0; --k) {
+      coord[k] = rem % d.dim[k];
+      rem /= d.dim[k];
+      oy += coord[k] * d.ystride[k];
+      oi += coord[k] * d.istride[k];
+    }
+    int g = int(idx[oi]);
+    if (g < 0) g += int(d.axis_dim);
+    coord[d.axis] = g;
+    for (int k = 0; k < d.rank; ++k) od += coord[k] * d.dstride[k];
+    y[oy] = data[od];
+  }
+}
+
+}  // namespace
+
+int concat_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->output_count < 1) return -3;
+  return prepare_parts(ctx, node, true);
+}
+int concat_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) { return run_parts<true>(ctx, node); }
+
+int split_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 1) return -3;
+  return prepare_parts(ctx, node, false);
+}
+int split_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) { return run_parts<false>(ctx, node); }
+
+int transpose_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  int perm[kMaxRank];
+  const int rank = ctx->tensors[node->outputs[0]].record->rank;
+  for (int i = 0; i < rank; ++i) perm[i] = a.extra_count > 0 ? a.extra[i] : i;
+  return prepare_gather(ctx, node, perm, false, "transpose");
+}
+int transpose_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) { return run_gather(ctx, node); }
+
+int tile_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 1 || node->output_count < 1) return -3;
+  int perm[kMaxRank];
+  for (int i = 0; i < kMaxRank; ++i) perm[i] = i;
+  return prepare_gather(ctx, node, perm, true, "tile");
+}
+int tile_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) { return run_gather(ctx, node); }
+
+int gather_elements_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 2 || node->output_count < 1) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &td = ctx->tensors[node->inputs[0]];
+  const TensorState &ti = ctx->tensors[node->inputs[1]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (td.record->dtype != SPKV2_DTYPE_FP32 || ti.record->dtype != SPKV2_DTYPE_FP32 ||
+      ty.record->dtype != SPKV2_DTYPE_FP32)
+    return SPKV2_ERR_UNSUPPORTED;
+  const int rank = td.record->rank;
+  const int axis = a.axis < 0 ? a.axis + rank : a.axis;
+  if (axis < 0 || axis >= rank || ti.record->rank != rank || ty.record->rank != rank) return -11;
+  const View vd = make_view(td), vi = make_view(ti), vy = make_view(ty);
+  GEPlan *p = new GEPlan();
+  GEDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  d.rank = rank;
+  d.axis = axis;
+  d.axis_dim = vd.dim[axis];
+  for (int k = 0; k < rank; ++k) {
+    d.dim[k] = vi.dim[k];
+    d.ystride[k] = vy.stride[k];
+    d.istride[k] = vi.stride[k];
+    d.dstride[k] = vd.stride[k];
+  }
+  p->total = vi.count();
+  p->variant = "gather_elements";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int gather_elements_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  GEPlan *p = node_plan<GEPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->total == 0) return 0;
+  gather_elements_kernel<<<grid_for(p->total, 256), 256, 0, ctx->stream>>>(
+      reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data),
+      reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data),
+      reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data), p->d, p->total);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace spkv2

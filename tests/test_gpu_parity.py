@@ -1,0 +1,101 @@
+"""GPU parity: the CUDA runtime (through the C-ABI, spkv2_* entry points)
+against the reference SPINNV2 CPU runtime (oracle/_ref, built from the
+reference sources) on the same fused graph and the same seeded inputs.
+
+fp32 tolerance: max-abs 1e-3 and rel 1e-4 on final
+outputs, i.e. np.allclose(gpu, ref, atol=1e-3, rtol=1e-4).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import compile_pair, reference_outputs, seeded_input
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-3, 1e-4
+
+
+def _run_gpu(spk: bytes, inputs, **kw):
+    from spinnv2_b200.runtime import Runtime
+
+    with Runtime(spk, device=0, **kw) as rt:
+        outs = rt.run(*inputs)
+        variants = {rt.package.nodes[i].op_type + ":" + rt.node_variant(i) for i in range(len(rt.package.nodes))}
+    return outs, variants
+
+
+@pytest.mark.parametrize("math", ["spec", "fp32"])
+def test_lenet5_matches_reference(gpu, math):
+    from spinnv2_b200.runtime import MATH_FP32, MATH_SPEC
+
+    spk = compile_pair("lenet5", 1)
+    x = seeded_input((1, 1, 28, 28), "uniform")
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x], math_mode=MATH_FP32 if math == "fp32" else MATH_SPEC)
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+
+
+SWEEP = ["conv7x7s2_3_64_224", "conv3x3_64_56", "conv3x3_128_28", "conv3x3_256_14", "conv3x3_512_7",
+         "conv1x1_256_64_56", "conv1x1_1024_256_14", "conv1x1_2048_512_7", "conv3x3s2_128_128_56", "gemm_2048_1000"]
+
+
+@pytest.mark.parametrize("case", SWEEP)
+@pytest.mark.parametrize("batch", [1, 4])
+def test_sweep_matches_reference(gpu, case, batch):
+    spk = compile_pair(case, batch)
+    from spinnv2_b200.spk import read_spk
+
+    shape = read_spk(spk["cuda_b200"]).inputs[0].shape
+    x = seeded_input(shape)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, _ = _run_gpu(spk["cuda_b200"], [x])
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+
+
+def test_resnet101_bs1_matches_reference(gpu):
+    spk = compile_pair("resnet101", 1)
+    x = seeded_input((1, 3, 224, 224))
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x])
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+    assert int(np.argmax(out[0])) == int(np.argmax(ref))
+
+
+def test_resnet101_bs2_graph_replay_is_stable(gpu):
+    from spinnv2_b200.runtime import Runtime
+
+    spk = compile_pair("resnet101", 2)
+    x = seeded_input((2, 3, 224, 224), seed=7)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    with Runtime(spk["cuda_b200"], device=0, graph=True) as rt:
+        runs = [rt.run(x)[0] for _ in range(4)]  # eager, capture, replay, replay
+    for r in runs:
+        np.testing.assert_allclose(r, ref, atol=ATOL, rtol=RTOL)
+    for r in runs[1:]:
+        np.testing.assert_array_equal(r, runs[0])
+
+
+def test_yolo_style_bs1_matches_reference(gpu):
+    from oracle import harness
+    from spinnv2_b200.runtime import Runtime
+    from spinnv2_b200.spk import read_spk
+
+    spk = compile_pair("yolo_style", 1)
+    x = seeded_input((1, 3, 640, 640), "uniform")
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])
+    pkg = read_spk(spk["cuda_b200"])
+    topk = next(n for n in pkg.nodes if n.op_type == "TopK")
+    with Runtime(spk["cuda_b200"], device=0) as rt:
+        scores, boxes = rt.run(x)
+        idx_gpu = rt.read_tensor(topk.outputs[1])
+    _, env = harness.run_spk(spk["cuda_b200"], [x], keep_all=True)
+    idx_ref = env[topk.outputs[1]]
+    # Scores: sorted top-300 values within tolerance.
+    np.testing.assert_allclose(scores, ref[0], atol=ATOL, rtol=RTOL)
+    # Indices may swap between near-equal scores; compare boxes where they agree.
+    same = idx_gpu == idx_ref
+    assert same.mean() > 0.9
+    np.testing.assert_allclose(boxes[same], env[pkg.outputs[1].id][same], atol=ATOL, rtol=RTOL)
