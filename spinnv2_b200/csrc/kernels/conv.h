@@ -27,6 +27,8 @@ struct ConvGeo {
   float res_scale;      // s_r / s_y          (kConvI8 with residual)
 };
 
+void conv_tc_release(void *state);
+
 struct ConvPlan : NodePlan {
   ConvGeo g{};
   int mode = kConvF32;
@@ -38,7 +40,9 @@ struct ConvPlan : NodePlan {
   const float *bias_f = nullptr;  // fp32 bias (device weights)
   int tc_block_n = 0;      // tcgen05 tile width in output channels
   int tc_kpad = 0;         // padded K of the tcgen05 panels
+  void *tc_state = nullptr;  // tensor map + launch configuration (conv_tc.cu)
   ~ConvPlan() override {
+    if (tc_state) conv_tc_release(tc_state);
     device_free(w_simt);
     device_free(w_tc);
     device_free(bias_q);

@@ -358,6 +358,19 @@ int launch_all(Spkv2Context *ctx) {
   return launch_graph(ctx);
 }
 
+// Reads (and clears) the status word that kernels with bounded waits set on
+// timeout; call after the stream has been synchronised.
+int take_device_status(Spkv2Context *ctx) {
+  int st = 0;
+  if (!ctx->d_status) return 0;
+  if (cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return SPKV2_ERR_CUDA;
+  if (st != 0) {
+    cudaMemset(ctx->d_status, 0, sizeof(int));
+    return SPKV2_ERR_DEVICE_STATUS;
+  }
+  return 0;
+}
+
 int check_runnable(Spkv2Context *ctx) {
   if (!ctx) return -1;
   if (!ctx->prepared) return -5;
@@ -613,6 +626,7 @@ int spkv2_run(Spkv2Context *ctx) {
   }
   if ((rc = stage_outputs(ctx))) return rc;
   if ((rc = cuda_status(cudaStreamSynchronize(ctx->stream)))) return rc;
+  if ((rc = take_device_status(ctx))) return rc;
   ctx->run_count++;
   return 0;
 }
@@ -715,7 +729,8 @@ int spkv2_cuda_run_async(Spkv2Context *ctx) {
 int spkv2_cuda_synchronize(Spkv2Context *ctx) {
   if (!ctx || !ctx->prepared) return SPKV2_ERR_NOT_PREPARED;
   cudaSetDevice(ctx->device);
-  return cuda_status(cudaStreamSynchronize(ctx->stream));
+  int rc = cuda_status(cudaStreamSynchronize(ctx->stream));
+  return rc ? rc : take_device_status(ctx);
 }
 
 int spkv2_cuda_run_nodes(Spkv2Context *ctx, uint32_t first, uint32_t last) {
@@ -725,6 +740,7 @@ int spkv2_cuda_run_nodes(Spkv2Context *ctx, uint32_t first, uint32_t last) {
   cudaSetDevice(ctx->device);
   rc = run_nodes_eager(ctx, first, last, false);
   int src = cuda_status(cudaStreamSynchronize(ctx->stream));
+  if (rc == 0 && src == 0) src = take_device_status(ctx);
   return rc ? rc : src;
 }
 
