@@ -97,6 +97,29 @@ const char *spkv2_cuda_status_string(int code);
  * it; the Python SPK writer calls it for large packages). */
 uint32_t spkv2_fnv1a32(const void *data, size_t size);
 
+/* Allocation-free GEMV: Y[M,N] = alpha * A[M,K] * B[K,N] + bias[N] (bias may
+ * be NULL), all row-major fp32 device pointers, launched asynchronously on
+ * `stream` (a cudaStream_t; NULL = legacy default stream).  This entry point
+ * has no counterpart in the reference runtime.  It is for callers that must
+ * not allocate device memory while they run - inside a CUDA stream capture,
+ * in latency-bound loops where cudaMalloc would synchronise the device, or
+ * in fixed-memory deployments (profiles with allow_runtime_malloc = false).
+ * Its split-K scratch is a static 1 MiB device array that every GPU loading
+ * this library holds until exit; the call itself allocates nothing.
+ *   - M must be 1..8 and ksplit*M*N must fit 262144 floats (ksplit shrinks
+ *     to fit, down to 1); otherwise it returns -14 (scratch overflow).
+ *   - The first call on each device resolves the array's device address
+ *     (cudaGetSymbolAddress) with that device current: make that first call
+ *     before any stream capture begins.
+ *   - All calls on a device share the one scratch array and every call fully
+ *     rewrites the part it reads, so nothing needs clearing between calls;
+ *     calls that overlap on the GPU (different streams, no ordering) race on
+ *     it and must be serialised by the caller.
+ * Returns 0, -1 for bad arguments, -14 for sizes beyond the scratch, or a
+ * CUDA-target error code. */
+int spkv2_cuda_gemv_noalloc(const float *A, const float *B, const float *bias, float *Y,
+                            int M, int K, int N, float alpha, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -134,6 +134,44 @@ __global__ void gemm_naive_kernel(float *__restrict__ Y, const float *__restrict
 
 }  // namespace
 
+// ---------------- allocation-free GEMV entry point ----------------
+//
+// Some callers cannot allocate device memory at call time: code that runs
+// inside a CUDA stream capture (allocation is not a capturable operation),
+// real-time loops where cudaMalloc's implicit device synchronisation would
+// break the latency budget, and deployments built from the fixed-memory
+// target profiles (allow_runtime_malloc = false) whose memory is budgeted
+// ahead of time.  spkv2_cuda_gemv_noalloc serves them: the split-K partial
+// sums live in the file-scope array below, sized once at load time, and the
+// call itself allocates nothing.
+
+namespace {
+
+// 1 MiB of split-K partials: ksplit * M * N must not exceed this many floats.
+constexpr size_t kNoAllocPartials = 262144;
+__device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
+
+constexpr int kMaxDevices = 64;
+float *g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_partials on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address must come
+// from cudaGetSymbolAddress, once per device, with that device current.
+int noalloc_scratch(float **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SPKV2_ERR_NO_DEVICE;
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (err != cudaSuccess || !p) return cuda_status(err == cudaSuccess ? cudaErrorInvalidSymbol : err);
+    g_noalloc_ptr[dev] = static_cast<float *>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace
+
 int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
   if (node->input_count < 2 || node->output_count < 1) return -3;
   if (node->op_type != SPKV2_OP_GEMM) return SPKV2_ERR_UNSUPPORTED;
@@ -197,3 +235,22 @@ int gemm_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
 }
 
 }  // namespace spkv2
+
+extern "C" int spkv2_cuda_gemv_noalloc(const float *A, const float *B, const float *bias, float *Y, int M, int K,
+                                       int N, float alpha, void *stream) {
+  using namespace spkv2;
+  if (!A || !B || !Y || M < 1 || K < 1 || N < 1) return -1;
+  if (M > kGemvMaxM) return -14;  // rows beyond the GEMV kernel's register tile
+  int ksplit = std::max(1, std::min(16, K / 128));
+  while (ksplit > 1 && size_t(ksplit) * M * N > kNoAllocPartials) --ksplit;
+  if (size_t(ksplit) * M * N > kNoAllocPartials) return -14;  // partials exceed the static scratch
+  float *part = nullptr;
+  int rc = noalloc_scratch(&part);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int kpb = int(ceil_div(K, ksplit));
+  dim3 grid(unsigned(ceil_div(N, 32)), unsigned(ksplit));
+  gemv_partial_kernel<<<grid, dim3(32, kGemvWarps), 0, s>>>(part, A, B, M, K, N, kpb);
+  gemv_finish_kernel<<<grid_for(int64_t(M) * N, 256), 256, 0, s>>>(Y, part, bias, M, N, ksplit, alpha);
+  return cuda_status(cudaGetLastError());
+}
