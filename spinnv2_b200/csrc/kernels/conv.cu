@@ -365,7 +365,7 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   }
   p->variant = p->mode == kConvI8 ? "simt_int8" : "simt_fp32";
   if (math != SPKV2_CUDA_MATH_FP32) {
-    rc = conv_tc_prepare(*p, tw.data, ctx->stream);
+    rc = conv_tc_prepare(*p, tw.data, tx.data, ty.data, ctx->stream);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;
       return rc;

@@ -54,7 +54,7 @@ int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res,
 
 // tcgen05 path (conv_tc.cu): returns 0 when the node is eligible and its
 // operand panels were built; SPKV2_ERR_UNSUPPORTED when the shape is not.
-int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, cudaStream_t s);
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s);
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
 
 }  // namespace spkv2

@@ -2,27 +2,36 @@
 // tensor cores, 3xTF32 split for near-fp32 accuracy).
 //
 // GEMM view: rows = output pixels (n, oh, ow), columns = output channels,
-// K = (r, s, c) with c fastest; A rows are gathered from the activation
-// (implicit im2col), B = packed weights [Cout_pad][K_pad] K-major.
+// K = (r, s, c) with c fastest; A rows are the activation gathered on the
+// fly (implicit im2col), B = packed weights [Cout_pad][K_pad] K-major.
 //
 // CTA tile: 128 pixels x BN channels, K step 32 fp32 (one 128-byte swizzle
 // row).  Warp roles (192 threads):
-//   warps 0-3  A producers: each thread gathers 16-byte chunks of 8 rows
-//              (8 threads cover one 128-byte row: coalesced), converts to
-//              TF32 (hi = round-to-nearest TF32, lo = x - hi), stores them in
-//              the 128B-swizzled K-major layout, then run the epilogue
-//              (TMEM lanes 32w..32w+31 = tile rows of warp w).
-//   warp 4     B producer: one thread issues TMA loads (no multicast) of the
-//              weight panels (hi, and lo for 3xTF32).
-//   warp 5     MMA issuer: allocates TMEM, one thread issues tcgen05.mma
-//              (M=128, N=BN, K=8 per instruction) into an fp32 TMEM
-//              accumulator and commits stage releases; frees TMEM at the end.
+//   warps 0-3  A operand, then the epilogue.  How A reaches shared memory:
+//                AMODE 2 (1x1, stride 1, NHWC, C % 32 == 0): TMA tile load;
+//                AMODE 1 (NHWC, C % 4 == 0): cp.async 16-byte gathers with
+//                  zero-fill for padding, completion signalled on the stage
+//                  mbarrier (many loads in flight per thread);
+//                AMODE 0 (anything else, e.g. NCHW graph input, C = 3):
+//                  per-element gathers through registers.
+//              For AMODE 1/2 the same warps then convert the landed tile in
+//              place, one stage behind the loads: TF32 hi = round-to-nearest,
+//              lo = x - hi (3xTF32), written in the 128B-swizzled K-major
+//              layout the MMA descriptors describe.
+//              Epilogue: TMEM lanes 32w..32w+31 (= tile rows of warp w) ->
+//              registers -> bias, residual, Relu/SiLU -> either a TMA store
+//              staged through shared memory (NHWC outputs) or direct stores.
+//   warp 4     TMA producer (one thread): weight panels (hi, and lo for
+//              3xTF32) and, in AMODE 2, the A tile.  No multicast.
+//   warp 5     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
+//              K=8) into an fp32 TMEM accumulator and commits stage
+//              releases to mbarriers.
 // 3xTF32: acc += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (three MMAs per K step).
-// Pipelines use mbarriers; every wait is bounded (about a second of clock
-// cycles) and on timeout the CTA records an error in the context status word
-// and winds down without further waits on the failed barrier.
+// Every mbarrier wait is bounded (about a second of clock cycles); on timeout
+// the CTA records a code in the context's status word and winds down.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "conv.h"
@@ -92,6 +101,28 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 16-byte async copy global -> shared; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on `bar` once all of this thread's prior cp.async copies landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -139,10 +170,8 @@ struct TcParams {
   int Kpad;      // K rounded up to a multiple of 32
   int Npad;      // Cout rounded up to a multiple of BN
   int num_kb;    // Kpad / 32
-  int split3;    // 1: 3xTF32, 0: TF32
 };
 
-// Shared memory per stage: A_hi, [A_lo], B_hi, [B_lo]; each 1024-aligned.
 template <int BN, bool SPLIT3>
 struct StageBytes {
   static constexpr int A = kBM * 128;
@@ -150,11 +179,34 @@ struct StageBytes {
   static constexpr int value = (SPLIT3 ? 2 : 1) * (A + B);
 };
 
-// AVEC: activation NHWC with C % 4 == 0 (16-byte chunk gathers); otherwise
-// per-element gathers through the generic strides.
-template <int BN, int STAGES, bool SPLIT3, bool AVEC>
+// Row / chunk mapping shared by the A loads and the conversion pass: thread t
+// handles 16-byte chunk (t & 7) of rows i*16 + (t >> 3), i = 0..7.
+__device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
+  return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <bool SPLIT3>
+__device__ __forceinline__ void convert_stage(uint8_t *a_hi, uint8_t *a_lo, int tid) {
+  const int chunk = tid & 7, rsub = tid >> 3;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t off = swz_off(i * 16 + rsub, chunk);
+    const float4 v = *reinterpret_cast<const float4 *>(a_hi + off);
+    float4 hi;
+    hi.x = tf32_rna(v.x);
+    hi.y = tf32_rna(v.y);
+    hi.z = tf32_rna(v.z);
+    hi.w = tf32_rna(v.w);
+    *reinterpret_cast<float4 *>(a_hi + off) = hi;
+    if (SPLIT3)
+      *reinterpret_cast<float4 *>(a_lo + off) = make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w);
+  }
+}
+
+template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const float *__restrict__ x,
+    conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap ymap, const float *__restrict__ x,
                    const float *__restrict__ bias, const float *__restrict__ res, float *__restrict__ y, TcParams tp,
                    int *status) {
   extern __shared__ uint8_t smem_raw[];
@@ -162,7 +214,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int A_BYTES = StageBytes<BN, SPLIT3>::A;
   constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
   constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
-  __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], done_bar;
+  constexpr bool CONVERT = (AMODE == 1) || (AMODE == 2 && SPLIT3);
+  __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], done_bar;
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
 
@@ -174,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 128 + 1);
+      mbar_init(&raw_bar[s], AMODE == 2 ? 1 : 128 + 1);
+      mbar_init(&full_bar[s], 128);
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&done_bar, 1);
@@ -193,86 +247,115 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_base_holder;
 
   if (warp < 4) {
-    // ------------------------------------------------------------ A producer
-    const int chunk = tid & 7;   // 16-byte chunk of the 128-byte row
-    const int rsub = tid >> 3;   // 0..15: row within a group of 16
-    int rn[8], rih[8], riw[8];
-    bool rvalid[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t p = m0 + i * 16 + rsub;
-      rvalid[i] = p < g.P;
-      const int64_t pp = rvalid[i] ? p : 0;
-      const int ow = int(pp % g.OW);
-      const int64_t t = pp / g.OW;
-      rih[i] = int(t % g.OH) * g.sh - g.ph;
-      riw[i] = ow * g.sw - g.pw;
-      rn[i] = int(t / g.OH);
-    }
-    for (int kb = 0; kb < tp.num_kb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (!mbar_wait(&empty_bar[s], ph ^ 1, &abort_flag, status, 1)) break;
-      uint8_t *a_hi = smem + s * STAGE;
-      uint8_t *a_lo = a_hi + A_BYTES;
-      float4 v[8];
-      const int k0 = kb * kBK + chunk * 4;
-      if (AVEC) {
-        // The 4 channels of this chunk share one filter tap (C % 4 == 0).
-        const bool kval = k0 < g.K;
-        const int tap = k0 / g.Cg, c = k0 - tap * g.Cg;
-        const int r = tap / g.KW, sx = tap - r * g.KW;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int ih = rih[i] + r * g.dh, iw = riw[i] + sx * g.dw;
-          const bool ok = kval && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-          v[i] = ok ? __ldg(reinterpret_cast<const float4 *>(x + ((int64_t(rn[i]) * g.H + ih) * g.W + iw) * g.C + c))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      } else {
-        int er[4], es[4], ec[4];
-        bool ek[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k = k0 + e;
-          ek[e] = k < g.K;
-          const int tap = k / g.Cg;
-          ec[e] = k - tap * g.Cg;
-          er[e] = tap / g.KW;
-          es[e] = tap - er[e] * g.KW;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float f[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int ih = rih[i] + er[e] * g.dh, iw = riw[i] + es[e] * g.dw;
-            const bool ok = ek[e] && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-            f[e] = ok ? __ldg(x + rn[i] * g.xs[0] + ec[e] * g.xs[1] + ih * g.xs[2] + iw * g.xs[3]) : 0.f;
-          }
-          v[i] = make_float4(f[0], f[1], f[2], f[3]);
+    // ------------------------------------------------------------ A operand
+    const int chunk = tid & 7;
+    const int rsub = tid >> 3;
+    if (AMODE == 2) {
+      if (CONVERT) {
+        for (int kb = 0; kb < tp.num_kb; ++kb) {
+          const int s = kb % STAGES;
+          if (!mbar_wait(&raw_bar[s], (kb / STAGES) & 1, &abort_flag, status, 5)) break;
+          uint8_t *a_hi = smem + s * STAGE;
+          convert_stage<SPLIT3>(a_hi, a_hi + A_BYTES, tid);
+          fence_proxy_async();
+          mbar_arrive(&full_bar[s]);
         }
       }
+    } else {
+      int rn[8], rih[8], riw[8];
+      bool rvalid[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int row = i * 16 + rsub;
-        const uint32_t off = row * 128 + ((chunk ^ (row & 7)) << 4);
-        float4 hi, lo;
-        hi.x = tf32_rna(v[i].x);
-        hi.y = tf32_rna(v[i].y);
-        hi.z = tf32_rna(v[i].z);
-        hi.w = tf32_rna(v[i].w);
-        *reinterpret_cast<float4 *>(a_hi + off) = hi;
-        if (SPLIT3) {
-          lo.x = v[i].x - hi.x;
-          lo.y = v[i].y - hi.y;
-          lo.z = v[i].z - hi.z;
-          lo.w = v[i].w - hi.w;
-          *reinterpret_cast<float4 *>(a_lo + off) = lo;
+        const int64_t p = m0 + i * 16 + rsub;
+        rvalid[i] = p < g.P;
+        const int64_t pp = rvalid[i] ? p : 0;
+        const int ow = int(pp % g.OW);
+        const int64_t t = pp / g.OW;
+        rih[i] = int(t % g.OH) * g.sh - g.ph;
+        riw[i] = ow * g.sw - g.pw;
+        rn[i] = int(t / g.OH);
+      }
+      bool ok = true;
+      for (int kb = 0; kb < tp.num_kb && ok; ++kb) {
+        const int s = kb % STAGES;
+        ok = mbar_wait(&empty_bar[s], ((kb / STAGES) & 1) ^ 1, &abort_flag, status, 1);
+        if (!ok) break;
+        uint8_t *a_hi = smem + s * STAGE;
+        const int k0 = kb * kBK + chunk * 4;
+        if (AMODE == 1) {
+          // The 4 channels of this chunk share one filter tap (C % 4 == 0).
+          const bool kval = k0 < g.K;
+          const int tap = k0 / g.Cg, c = k0 - tap * g.Cg;
+          const int r = tap / g.KW, sx = tap - r * g.KW;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int ih = rih[i] + r * g.dh, iw = riw[i] + sx * g.dw;
+            const bool in = kval && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+            const float *src = in ? x + ((int64_t(rn[i]) * g.H + ih) * g.W + iw) * g.C + c : x;
+            cp_async16(a_hi + swz_off(i * 16 + rsub, chunk), src, in ? 16u : 0u);
+          }
+          cp_async_arrive(&raw_bar[s]);
+          // Convert the previous stage while this one's copies are in flight.
+          if (kb > 0) {
+            const int ps = (kb - 1) % STAGES;
+            ok = mbar_wait(&raw_bar[ps], ((kb - 1) / STAGES) & 1, &abort_flag, status, 6);
+            if (!ok) break;
+            uint8_t *p_hi = smem + ps * STAGE;
+            convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, tid);
+            fence_proxy_async();
+            mbar_arrive(&full_bar[ps]);
+          }
+        } else {
+          float4 v[8];
+          int er[4], es[4], ec[4];
+          bool ek[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = k0 + e;
+            ek[e] = k < g.K;
+            const int tap = k / g.Cg;
+            ec[e] = k - tap * g.Cg;
+            er[e] = tap / g.KW;
+            es[e] = tap - er[e] * g.KW;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float f[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int ih = rih[i] + er[e] * g.dh, iw = riw[i] + es[e] * g.dw;
+              const bool in = ek[e] && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+              f[e] = in ? __ldg(x + rn[i] * g.xs[0] + ec[e] * g.xs[1] + ih * g.xs[2] + iw * g.xs[3]) : 0.f;
+            }
+            v[i] = make_float4(f[0], f[1], f[2], f[3]);
+          }
+          uint8_t *a_lo = a_hi + A_BYTES;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t off = swz_off(i * 16 + rsub, chunk);
+            float4 hi;
+            hi.x = tf32_rna(v[i].x);
+            hi.y = tf32_rna(v[i].y);
+            hi.z = tf32_rna(v[i].z);
+            hi.w = tf32_rna(v[i].w);
+            *reinterpret_cast<float4 *>(a_hi + off) = hi;
+            if (SPLIT3)
+              *reinterpret_cast<float4 *>(a_lo + off) =
+                  make_float4(v[i].x - hi.x, v[i].y - hi.y, v[i].z - hi.z, v[i].w - hi.w);
+          }
+          fence_proxy_async();
+          mbar_arrive(&raw_bar[s]);
         }
       }
-      fence_proxy_async();
-      mbar_arrive(&full_bar[s]);
+      if (AMODE == 1 && ok && tp.num_kb > 0) {
+        const int kb = tp.num_kb - 1, ps = kb % STAGES;
+        if (mbar_wait(&raw_bar[ps], (kb / STAGES) & 1, &abort_flag, status, 6)) {
+          uint8_t *p_hi = smem + ps * STAGE;
+          convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, tid);
+          fence_proxy_async();
+          mbar_arrive(&full_bar[ps]);
+        }
+      }
     }
     // ------------------------------------------------------------ epilogue
     if (mbar_wait(&done_bar, 0, &abort_flag, status, 4)) {
@@ -289,68 +372,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
-      const bool yvec = g.ys[1] == 1 && (g.M % 4) == 0;
       const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
+      // Staging for the TMA store: two 32x32 fp32 buffers per warp, reusing
+      // the (now idle) operand stages.
+      uint8_t *stage_buf = smem + warp * 8192;
 #pragma unroll 1
       for (int cb = 0; cb < BN; cb += 32) {
         uint32_t acc[32];
         tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(cb), acc);
         const int c0 = n0 + cb;
-        if (!pv || c0 >= g.M) continue;
+        if (c0 >= g.M) continue;  // whole chunk in the channel padding (warp-uniform)
         float vals[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) vals[j] = __uint_as_float(acc[j]);
         const int cn = min(32, g.M - c0);
-        if (cn == 32 && yvec && (!g.has_res || rvec)) {
+        if (cn == 32 && (!g.has_res || rvec)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
-            float4 rr = g.has_res ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
-                                  : make_float4(0, 0, 0, 0);
-            float4 o;
-            o.x = apply_act(vals[j] + b.x + rr.x, g.act);
-            o.y = apply_act(vals[j + 1] + b.y + rr.y, g.act);
-            o.z = apply_act(vals[j + 2] + b.z + rr.z, g.act);
-            o.w = apply_act(vals[j + 3] + b.w + rr.w, g.act);
-            *reinterpret_cast<float4 *>(y + ybase + c0 + j) = o;
+            const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
+            const float4 rr = (g.has_res && pv) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
+                                                : make_float4(0, 0, 0, 0);
+            vals[j] = apply_act(__uint_as_float(acc[j]) + b.x + rr.x, g.act);
+            vals[j + 1] = apply_act(__uint_as_float(acc[j + 1]) + b.y + rr.y, g.act);
+            vals[j + 2] = apply_act(__uint_as_float(acc[j + 2]) + b.z + rr.z, g.act);
+            vals[j + 3] = apply_act(__uint_as_float(acc[j + 3]) + b.w + rr.w, g.act);
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            float v = __uint_as_float(acc[j]);
             if (j < cn) {
               const int c = c0 + j;
-              float v = vals[j];
               if (g.has_bias) v += __ldg(bias + c);
-              if (g.has_res) v += __ldg(res + rbase + int64_t(c) * g.rs[1]);
-              y[ybase + int64_t(c) * g.ys[1]] = apply_act(v, g.act);
+              if (g.has_res && pv) v += __ldg(res + rbase + int64_t(c) * g.rs[1]);
+              v = apply_act(v, g.act);
             }
+            vals[j] = v;
+          }
+        }
+        if (EPI_TMA) {
+          uint8_t *buf = stage_buf + ((cb >> 5) & 1) * 4096;
+          if (cb >= 64 && lane == 0) tma_store_wait_read1();  // the buffer's previous store has read it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4 *>(buf + swz_off(lane, j)) =
+                make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2], vals[4 * j + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0 && m0 + warp * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + warp * 32), buf);
+        } else if (pv) {
+          if (cn == 32 && g.ys[1] == 1 && (g.M % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4 *>(y + ybase + c0 + j) =
+                  make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < cn) y[ybase + int64_t(c0 + j) * g.ys[1]] = vals[j];
           }
         }
       }
+      if (EPI_TMA && lane == 0) tma_store_wait_all();
     }
   } else if (warp == 4) {
-    // ------------------------------------------------------------ B producer (TMA)
+    // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE == 2 ? A_BYTES : 0);
       for (int kb = 0; kb < tp.num_kb; ++kb) {
         const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1, &abort_flag, status, 2)) break;
-        uint8_t *b_hi = smem + s * STAGE + (SPLIT3 ? 2 : 1) * A_BYTES;
-        mbar_arrive_expect_tx(&full_bar[s], (SPLIT3 ? 2 : 1) * B_BYTES);
-        tma_load_2d(b_hi, &wmap, kb * kBK, n0, &full_bar[s]);
-        if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &full_bar[s]);
+        if (!mbar_wait(&empty_bar[s], ((kb / STAGES) & 1) ^ 1, &abort_flag, status, 2)) break;
+        uint8_t *a_hi = smem + s * STAGE;
+        uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
+        mbar_arrive_expect_tx(&raw_bar[s], bytes);
+        tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
+        if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
+        if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
       }
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-      bool ok = true;
-      for (int kb = 0; kb < tp.num_kb && ok; ++kb) {
+      constexpr uint32_t idesc =
+          (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+      for (int kb = 0; kb < tp.num_kb; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
-        ok = mbar_wait(&full_bar[s], ph, &abort_flag, status, 3);
-        if (!ok) break;
+        if (!mbar_wait(CONVERT ? &full_bar[s] : &raw_bar[s], ph, &abort_flag, status, 3)) break;
         tc_fence_after();
         uint8_t *a_hi = smem + s * STAGE;
         uint8_t *a_lo = a_hi + A_BYTES;
@@ -418,102 +525,133 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// 2-D fp32 tensor map, 128-byte swizzle: dims {inner, outer}, row pitch in
+// elements, box {32, box_rows}.
+bool encode_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_rows) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch * sizeof(float)};
+  const cuuint32_t box[2] = {uint32_t(kBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct TcState {
-  CUtensorMap map;
+  CUtensorMap wmap, amap, ymap;
   TcParams tp;
   int bn = 128;
   int stages = 2;
   bool split3 = true;
-  bool avec = true;
+  int amode = 0;
+  bool epi_tma = false;
   size_t smem = 0;
   bool set_attr_only = false;  // dispatch only sets the kernel's smem attribute
 };
 
-template <int BN, int STAGES, bool SPLIT3, bool AVEC>
+template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI>
 int launch_cfg(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
                cudaStream_t s) {
-  auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AVEC>;
+  auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AMODE, EPI>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   const int64_t mt = ceil_div(st.tp.g.P, kBM);
   const int64_t blocks = mt * (st.tp.Npad / BN);
   if (blocks > 0x7fffffffLL) return SPKV2_ERR_UNSUPPORTED;
-  kern<<<unsigned(blocks), kThreads, st.smem, s>>>(st.map, x, bias, res, y, st.tp, status);
+  kern<<<unsigned(blocks), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
   return cuda_status(cudaGetLastError());
 }
 
 template <int BN, int STAGES, bool SPLIT3>
-int launch_avec(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
-                cudaStream_t s) {
-  return st.avec ? launch_cfg<BN, STAGES, SPLIT3, true>(st, x, y, bias, res, status, s)
-                 : launch_cfg<BN, STAGES, SPLIT3, false>(st, x, y, bias, res, status, s);
+int launch_modes(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
+                 cudaStream_t s) {
+  if (st.epi_tma) {
+    switch (st.amode) {
+      case 2: return launch_cfg<BN, STAGES, SPLIT3, 2, true>(st, x, y, bias, res, status, s);
+      case 1: return launch_cfg<BN, STAGES, SPLIT3, 1, true>(st, x, y, bias, res, status, s);
+      default: return launch_cfg<BN, STAGES, SPLIT3, 0, true>(st, x, y, bias, res, status, s);
+    }
+  }
+  switch (st.amode) {
+    case 2: return launch_cfg<BN, STAGES, SPLIT3, 2, false>(st, x, y, bias, res, status, s);
+    case 1: return launch_cfg<BN, STAGES, SPLIT3, 1, false>(st, x, y, bias, res, status, s);
+    default: return launch_cfg<BN, STAGES, SPLIT3, 0, false>(st, x, y, bias, res, status, s);
+  }
+}
+
+int stages_for(int bn, bool split3) {
+  const int stage = (split3 ? 2 : 1) * (kBM * 128 + bn * 128);
+  return std::min(4, (200 * 1024) / stage);
 }
 
 }  // namespace
 
-// Eligible: fp32 in/out, group 1, output channels >= 16.  Tile width BN is
-// the smallest of {32, 64, 128, 256}... covering Cout, capped at 128 (256 for
-// Cout >= 512 in TF32 mode).
-int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, cudaStream_t s) {
+// Eligible: fp32 in and out, group 1, Cout >= 16, 3xTF32 or TF32 math.
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s) {
   const ConvGeo &g = p.g;
   if (p.mode != kConvF32 || g.groups != 1 || g.M < 16) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
   if (!encode_fn()) return SPKV2_ERR_UNSUPPORTED;
   TcState *st = new TcState();
+  memset(&st->wmap, 0, sizeof(st->wmap));
+  memset(&st->amap, 0, sizeof(st->amap));
+  memset(&st->ymap, 0, sizeof(st->ymap));
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
-  st->bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128;
-  st->stages = st->split3 ? (st->bn == 128 ? 3 : 4) : 4;
-  st->avec = g.xs[1] == 1 && g.C % 4 == 0;
+  int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128;
+  if (!st->split3 && g.M >= 256) bn = 256;
+  if (const char *e = getenv("SPKV2_TC_BN")) {
+    const int v = atoi(e);
+    if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
+  }
+  st->bn = bn;
+  st->stages = stages_for(bn, st->split3);
+  const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
+  const bool c32 = g.C % 32 == 0;
+  if (nhwc_in && c32 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
+      reinterpret_cast<uintptr_t>(x_dev) % 16 == 0)
+    st->amode = 2;
+  else if (nhwc_in && g.C % 4 == 0 && reinterpret_cast<uintptr_t>(x_dev) % 16 == 0)
+    st->amode = 1;
+  else
+    st->amode = 0;
+  const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
+  st->epi_tma = nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
   tp.g = g;
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);
-  tp.Npad = int(ceil_div(g.M, st->bn) * st->bn);
+  tp.Npad = int(ceil_div(g.M, bn) * bn);
   tp.num_kb = tp.Kpad / kBK;
-  tp.split3 = st->split3 ? 1 : 0;
   const int parts = st->split3 ? 2 : 1;
-  const size_t wbytes = size_t(parts) * tp.Npad * tp.Kpad * sizeof(float);
-  float *wtc = static_cast<float *>(device_alloc(wbytes));
+  float *wtc = static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));
   if (!wtc) {
     delete st;
     return SPKV2_ERR_DEVICE_ALLOC;
   }
   pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(wtc, static_cast<const float *>(w_raw_dev),
-                                                                           g, tp.Npad, tp.Kpad, tp.split3);
+                                                                           g, tp.Npad, tp.Kpad, st->split3 ? 1 : 0);
   int rc = cuda_status(cudaGetLastError());
-  if (rc) {
+  bool ok = rc == 0 && encode_2d(&st->wmap, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(bn));
+  if (ok && st->amode == 2) ok = encode_2d(&st->amap, x_dev, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
+  if (ok && st->epi_tma) ok = encode_2d(&st->ymap, y_dev, uint64_t(g.M), uint64_t(g.P), uint64_t(g.M), 32);
+  if (!ok) {
     device_free(wtc);
     delete st;
-    return rc;
+    return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  // Weight panel tensor map: dims {Kpad, parts*Npad}, box {32, BN}, 128B swizzle.
-  const cuuint64_t dims[2] = {cuuint64_t(tp.Kpad), cuuint64_t(parts) * cuuint64_t(tp.Npad)};
-  const cuuint64_t strides[1] = {cuuint64_t(tp.Kpad) * sizeof(float)};
-  const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(st->bn)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult cr = encode_fn()(&st->map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, wtc, dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) {
-    device_free(wtc);
-    delete st;
-    return SPKV2_ERR_UNSUPPORTED;
-  }
-  const int stage_bytes = parts * (kBM * 128 + st->bn * 128);
-  st->smem = size_t(st->stages) * stage_bytes + 1024;
-  // Keep at most two CTAs per SM so their TMEM allocations (<= 256 columns
-  // each) always fit in the 512 columns.
-  st->smem = std::max<size_t>(st->smem, 80 * 1024);
+  st->smem = size_t(st->stages) * size_t(parts) * (kBM * 128 + bn * 128) + 1024;
+  // At most one CTA per SM: TMEM (<= 256 columns) is never contended.
+  st->smem = std::max<size_t>(st->smem, 120 * 1024);
   p.w_tc = wtc;
   p.tc_state = st;
-  // Opt the chosen kernel into its dynamic shared memory on this device.
+  p.tc_block_n = bn;
+  p.tc_kpad = tp.Kpad;
   st->set_attr_only = true;
   rc = conv_tc_launch(p, nullptr, nullptr, nullptr, nullptr, s);
   st->set_attr_only = false;
   if (rc) return rc;
-  p.tc_block_n = st->bn;
-  p.tc_kpad = tp.Kpad;
-  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(st->bn) +
-              (st->avec ? "_vec" : "_gather");
+  static const char *amodes[] = {"gather", "cpasync", "tma"};
+  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) + "_" +
+              amodes[st->amode] + (st->epi_tma ? "_tmastore" : "");
   return 0;
 }
 
@@ -527,15 +665,17 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   const float *bias = p.bias_f;
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_avec<32, 4, true>(st, xf, yf, bias, rf, status, s);
-      case 64: return launch_avec<64, 4, true>(st, xf, yf, bias, rf, status, s);
-      default: return launch_avec<128, 3, true>(st, xf, yf, bias, rf, status, s);
+      case 32: return launch_modes<32, 4, true>(st, xf, yf, bias, rf, status, s);
+      case 64: return launch_modes<64, 4, true>(st, xf, yf, bias, rf, status, s);
+      case 256: return launch_modes<256, 2, true>(st, xf, yf, bias, rf, status, s);
+      default: return launch_modes<128, 3, true>(st, xf, yf, bias, rf, status, s);
     }
   }
   switch (st.bn) {
-    case 32: return launch_avec<32, 4, false>(st, xf, yf, bias, rf, status, s);
-    case 64: return launch_avec<64, 4, false>(st, xf, yf, bias, rf, status, s);
-    default: return launch_avec<128, 4, false>(st, xf, yf, bias, rf, status, s);
+    case 32: return launch_modes<32, 4, false>(st, xf, yf, bias, rf, status, s);
+    case 64: return launch_modes<64, 4, false>(st, xf, yf, bias, rf, status, s);
+    case 256: return launch_modes<256, 4, false>(st, xf, yf, bias, rf, status, s);
+    default: return launch_modes<128, 4, false>(st, xf, yf, bias, rf, status, s);
   }
 }
 
