@@ -1,32 +1,34 @@
 // tcgen05 implicit-GEMM convolution for sm_100a (fp32 activations, TF32
-// tensor cores, 3xTF32 split for near-fp32 accuracy).
+// tensor cores, 3xTF32 split for near-fp32 accuracy).  Also serves Gemm as a
+// 1x1 convolution over [M,1,1,K].
 //
 // GEMM view: rows = output pixels (n, oh, ow), columns = output channels,
 // K = (r, s, c) with c fastest; A rows are the activation gathered on the
 // fly (implicit im2col), B = packed weights [Cout_pad][K_pad] K-major.
 //
-// CTA tile: 128 pixels x BN channels, K step 32 fp32 (one 128-byte swizzle
-// row).  Warp roles (192 threads):
-//   warps 0-3  A operand, then the epilogue.  How A reaches shared memory:
-//                AMODE 2 (1x1, stride 1, NHWC, C % 32 == 0): TMA tile load;
-//                AMODE 1 (NHWC, C % 4 == 0): cp.async 16-byte gathers with
-//                  zero-fill for padding, completion signalled on the stage
-//                  mbarrier (many loads in flight per thread);
-//                AMODE 0 (anything else, e.g. NCHW graph input, C = 3):
-//                  per-element gathers through registers.
-//              For AMODE 1/2 the same warps then convert the landed tile in
-//              place, one stage behind the loads: TF32 hi = round-to-nearest,
-//              lo = x - hi (3xTF32), written in the 128B-swizzled K-major
-//              layout the MMA descriptors describe.
-//              Epilogue: TMEM lanes 32w..32w+31 (= tile rows of warp w) ->
-//              registers -> bias, residual, Relu/SiLU -> either a TMA store
-//              staged through shared memory (NHWC outputs) or direct stores.
-//   warp 4     TMA producer (one thread): weight panels (hi, and lo for
-//              3xTF32) and, in AMODE 2, the A tile.  No multicast.
-//   warp 5     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
-//              K=8) into an fp32 TMEM accumulator and commits stage
-//              releases to mbarriers.
+// Persistent kernel: one CTA per SM walks output tiles (128 pixels x BN
+// channels) in a static round-robin.  Warp roles (320 threads):
+//   warps 0-3  epilogue: TMEM lanes 32w..32w+31 (= tile rows of warp w) ->
+//              registers -> bias, residual, Relu/SiLU -> TMA store staged
+//              through shared memory (NHWC outputs) or direct stores.  The
+//              accumulator is double-buffered in TMEM (2 x BN columns), so
+//              the epilogue of tile i overlaps the mainloop of tile i+1.
+//   warps 4-7  A operand.  AMODE 2 (1x1, stride 1, NHWC, C % 32 == 0): TMA
+//              tile loads (issued by warp 8); AMODE 1 (NHWC, C % 4 == 0):
+//              cp.async 16-byte gathers, zero-fill for padding, completion on
+//              the stage mbarrier; AMODE 0 (generic strides): per-element
+//              gathers through registers.  For AMODE 1/2 the warps convert the
+//              landed tile in place, one stage behind the loads: TF32 hi =
+//              round-to-nearest, lo = x - hi (3xTF32), in the 128B-swizzled
+//              K-major layout the MMA descriptors describe.
+//   warp 8     TMA producer (one thread): weight panels (hi, and lo for
+//              3xTF32), and the A tile in AMODE 2.  No multicast.
+//   warp 9     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
+//              K=8) and commits stage releases and finished accumulators.
 // 3xTF32: acc += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (three MMAs per K step).
+// Inputs that are not dense NHWC with C % 4 == 0 (the NCHW graph input of a
+// network's first conv, C = 3) are first re-laid out by a small kernel into a
+// plan-owned NHWC buffer with C rounded up to 4, then take AMODE 1.
 // Every mbarrier wait is bounded (about a second of clock cycles); on timeout
 // the CTA records a code in the context's status word and winds down.
 #include <cuda.h>
@@ -42,7 +44,8 @@ namespace {
 
 constexpr int kBM = 128;          // tile rows (pixels) = UMMA M
 constexpr int kBK = 32;           // fp32 elements per K step = 128 bytes
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 buffers x 32x32 fp32
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
 
 // ---------------------------------------------------------------- PTX helpers
@@ -166,10 +169,12 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 // ---------------------------------------------------------------- kernel
 struct TcParams {
-  ConvGeo g;
-  int Kpad;      // K rounded up to a multiple of 32
-  int Npad;      // Cout rounded up to a multiple of BN
-  int num_kb;    // Kpad / 32
+  ConvGeo g;       // GEMM-side geometry (C may be the padded channel count)
+  int Kpad;        // K rounded up to a multiple of 32
+  int Npad;        // Cout rounded up to a multiple of BN
+  int num_kb;      // Kpad / 32
+  int n_tiles;     // Npad / BN
+  int64_t tiles;   // m_tiles * n_tiles
 };
 
 template <int BN, bool SPLIT3>
@@ -180,14 +185,14 @@ struct StageBytes {
 };
 
 // Row / chunk mapping shared by the A loads and the conversion pass: thread t
-// handles 16-byte chunk (t & 7) of rows i*16 + (t >> 3), i = 0..7.
+// (0..127) handles 16-byte chunk (t & 7) of rows i*16 + (t >> 3), i = 0..7.
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
 template <bool SPLIT3>
-__device__ __forceinline__ void convert_stage(uint8_t *a_hi, uint8_t *a_lo, int tid) {
-  const int chunk = tid & 7, rsub = tid >> 3;
+__device__ __forceinline__ void convert_stage(uint8_t *a_hi, uint8_t *a_lo, int t) {
+  const int chunk = t & 7, rsub = t >> 3;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t off = swz_off(i * 16 + rsub, chunk);
@@ -215,15 +220,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
   constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
   constexpr bool CONVERT = (AMODE == 1) || (AMODE == 2 && SPLIT3);
-  __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], done_bar;
+  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
 
   const ConvGeo &g = tp.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_tiles = tp.Npad / BN;
-  const int n0 = (blockIdx.x % n_tiles) * BN;  // channel tile fastest: pixel tile shared in L2
-  const int64_t m0 = int64_t(blockIdx.x / n_tiles) * kBM;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -231,12 +234,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], 128);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&done_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 128);
+    }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  constexpr uint32_t kTmemCols = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_holder)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -247,21 +252,116 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_base_holder;
 
   if (warp < 4) {
-    // ------------------------------------------------------------ A operand
-    const int chunk = tid & 7;
-    const int rsub = tid >> 3;
-    if (AMODE == 2) {
-      if (CONVERT) {
-        for (int kb = 0; kb < tp.num_kb; ++kb) {
-          const int s = kb % STAGES;
-          if (!mbar_wait(&raw_bar[s], (kb / STAGES) & 1, &abort_flag, status, 5)) break;
-          uint8_t *a_hi = smem + s * STAGE;
-          convert_stage<SPLIT3>(a_hi, a_hi + A_BYTES, tid);
+    // ------------------------------------------------------------ epilogue
+    uint8_t *stage_buf = smem + STAGES * STAGE + warp * 8192;
+    const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
+    uint32_t sc = 0;  // TMA-store chunks issued by this warp
+    int ti = 0;
+    for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x, ++ti) {
+      const int n0 = int(t % tp.n_tiles) * BN;
+      const int64_t m0 = (t / tp.n_tiles) * kBM;
+      const int ab = ti & 1;
+      if (!mbar_wait(&accf_bar[ab], (ti >> 1) & 1, &abort_flag, status, 4)) break;
+      tc_fence_after();
+      const int row = warp * 32 + lane;
+      const int64_t p = m0 + row;
+      const bool pv = p < g.P;
+      int n = 0, oh = 0, ow = 0;
+      if (pv) {
+        ow = int(p % g.OW);
+        const int64_t q = p / g.OW;
+        oh = int(q % g.OH);
+        n = int(q / g.OH);
+      }
+      const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
+      const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
+#pragma unroll 1
+      for (int cb = 0; cb < BN; cb += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(ab * BN + cb), acc);
+        if (cb + 32 >= BN) {
+          // All of this tile's accumulator has been read: hand the buffer back.
+          tc_fence_before();
+          mbar_arrive(&acce_bar[ab]);
+        }
+        const int c0 = n0 + cb;
+        if (c0 >= g.M) continue;  // channel padding (warp-uniform)
+        float vals[32];
+        const int cn = min(32, g.M - c0);
+        if (cn == 32 && (!g.has_res || rvec)) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
+            const float4 rr = (g.has_res && pv) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
+                                                : make_float4(0, 0, 0, 0);
+            vals[j] = apply_act(__uint_as_float(acc[j]) + b.x + rr.x, g.act);
+            vals[j + 1] = apply_act(__uint_as_float(acc[j + 1]) + b.y + rr.y, g.act);
+            vals[j + 2] = apply_act(__uint_as_float(acc[j + 2]) + b.z + rr.z, g.act);
+            vals[j + 3] = apply_act(__uint_as_float(acc[j + 3]) + b.w + rr.w, g.act);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float v = __uint_as_float(acc[j]);
+            if (j < cn) {
+              const int c = c0 + j;
+              if (g.has_bias) v += __ldg(bias + c);
+              if (g.has_res && pv) v += __ldg(res + rbase + int64_t(c) * g.rs[1]);
+              v = apply_act(v, g.act);
+            }
+            vals[j] = v;
+          }
+        }
+        if (EPI_TMA) {
+          uint8_t *buf = stage_buf + (sc & 1) * 4096;
+          if (sc >= 2 && lane == 0) tma_store_wait_read1();  // previous store from this buffer has read it
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4 *>(buf + swz_off(lane, j)) =
+                make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2], vals[4 * j + 3]);
           fence_proxy_async();
-          mbar_arrive(&full_bar[s]);
+          __syncwarp();
+          if (lane == 0 && m0 + warp * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + warp * 32), buf);
+          ++sc;
+        } else if (pv) {
+          if (cn == 32 && g.ys[1] == 1 && (g.M % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4 *>(y + ybase + c0 + j) =
+                  make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < cn) y[ybase + int64_t(c0 + j) * g.ys[1]] = vals[j];
+          }
         }
       }
-    } else {
+    }
+    if (EPI_TMA && lane == 0) tma_store_wait_all();
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ A operand
+    const int at = tid - 128;
+    const int chunk = at & 7;
+    const int rsub = at >> 3;
+    uint32_t it = 0;  // global K-step counter (stage ring position)
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+      const int64_t m0 = (t / tp.n_tiles) * kBM;
+      if (AMODE == 2) {
+        if (CONVERT) {
+          for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
+            const int s = it % STAGES;
+            ok = mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5);
+            if (!ok) break;
+            uint8_t *a_hi = smem + s * STAGE;
+            convert_stage<SPLIT3>(a_hi, a_hi + A_BYTES, at);
+            fence_proxy_async();
+            mbar_arrive(&full_bar[s]);
+          }
+        }
+        continue;
+      }
       int rn[8], rih[8], riw[8];
       bool rvalid[8];
 #pragma unroll
@@ -270,15 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         rvalid[i] = p < g.P;
         const int64_t pp = rvalid[i] ? p : 0;
         const int ow = int(pp % g.OW);
-        const int64_t t = pp / g.OW;
-        rih[i] = int(t % g.OH) * g.sh - g.ph;
+        const int64_t q = pp / g.OW;
+        rih[i] = int(q % g.OH) * g.sh - g.ph;
         riw[i] = ow * g.sw - g.pw;
-        rn[i] = int(t / g.OH);
+        rn[i] = int(q / g.OH);
       }
-      bool ok = true;
-      for (int kb = 0; kb < tp.num_kb && ok; ++kb) {
-        const int s = kb % STAGES;
-        ok = mbar_wait(&empty_bar[s], ((kb / STAGES) & 1) ^ 1, &abort_flag, status, 1);
+      for (int kb = 0; kb < tp.num_kb && ok; ++kb, ++it) {
+        const int s = it % STAGES;
+        ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 1);
         if (!ok) break;
         uint8_t *a_hi = smem + s * STAGE;
         const int k0 = kb * kBK + chunk * 4;
@@ -295,13 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             cp_async16(a_hi + swz_off(i * 16 + rsub, chunk), src, in ? 16u : 0u);
           }
           cp_async_arrive(&raw_bar[s]);
-          // Convert the previous stage while this one's copies are in flight.
-          if (kb > 0) {
-            const int ps = (kb - 1) % STAGES;
-            ok = mbar_wait(&raw_bar[ps], ((kb - 1) / STAGES) & 1, &abort_flag, status, 6);
+          // Convert the previous K step while this one's copies are in flight.
+          if (it > 0) {
+            const uint32_t pit = it - 1;
+            const int ps = pit % STAGES;
+            ok = mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6);
             if (!ok) break;
             uint8_t *p_hi = smem + ps * STAGE;
-            convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, tid);
+            convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, at);
             fence_proxy_async();
             mbar_arrive(&full_bar[ps]);
           }
@@ -347,106 +447,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&raw_bar[s]);
         }
       }
-      if (AMODE == 1 && ok && tp.num_kb > 0) {
-        const int kb = tp.num_kb - 1, ps = kb % STAGES;
-        if (mbar_wait(&raw_bar[ps], (kb / STAGES) & 1, &abort_flag, status, 6)) {
-          uint8_t *p_hi = smem + ps * STAGE;
-          convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, tid);
-          fence_proxy_async();
-          mbar_arrive(&full_bar[ps]);
-        }
+    }
+    if (AMODE == 1 && ok && it > 0) {
+      const uint32_t pit = it - 1;
+      const int ps = pit % STAGES;
+      if (mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6)) {
+        uint8_t *p_hi = smem + ps * STAGE;
+        convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, at);
+        fence_proxy_async();
+        mbar_arrive(&full_bar[ps]);
       }
     }
-    // ------------------------------------------------------------ epilogue
-    if (mbar_wait(&done_bar, 0, &abort_flag, status, 4)) {
-      tc_fence_after();
-      const int row = warp * 32 + lane;
-      const int64_t p = m0 + row;
-      const bool pv = p < g.P;
-      int n = 0, oh = 0, ow = 0;
-      if (pv) {
-        ow = int(p % g.OW);
-        const int64_t t = p / g.OW;
-        oh = int(t % g.OH);
-        n = int(t / g.OH);
-      }
-      const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
-      const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
-      const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
-      // Staging for the TMA store: two 32x32 fp32 buffers per warp, reusing
-      // the (now idle) operand stages.
-      uint8_t *stage_buf = smem + warp * 8192;
-#pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 32) {
-        uint32_t acc[32];
-        tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(cb), acc);
-        const int c0 = n0 + cb;
-        if (c0 >= g.M) continue;  // whole chunk in the channel padding (warp-uniform)
-        float vals[32];
-        const int cn = min(32, g.M - c0);
-        if (cn == 32 && (!g.has_res || rvec)) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
-            const float4 rr = (g.has_res && pv) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
-                                                : make_float4(0, 0, 0, 0);
-            vals[j] = apply_act(__uint_as_float(acc[j]) + b.x + rr.x, g.act);
-            vals[j + 1] = apply_act(__uint_as_float(acc[j + 1]) + b.y + rr.y, g.act);
-            vals[j + 2] = apply_act(__uint_as_float(acc[j + 2]) + b.z + rr.z, g.act);
-            vals[j + 3] = apply_act(__uint_as_float(acc[j + 3]) + b.w + rr.w, g.act);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float v = __uint_as_float(acc[j]);
-            if (j < cn) {
-              const int c = c0 + j;
-              if (g.has_bias) v += __ldg(bias + c);
-              if (g.has_res && pv) v += __ldg(res + rbase + int64_t(c) * g.rs[1]);
-              v = apply_act(v, g.act);
-            }
-            vals[j] = v;
-          }
-        }
-        if (EPI_TMA) {
-          uint8_t *buf = stage_buf + ((cb >> 5) & 1) * 4096;
-          if (cb >= 64 && lane == 0) tma_store_wait_read1();  // the buffer's previous store has read it
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float4 *>(buf + swz_off(lane, j)) =
-                make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2], vals[4 * j + 3]);
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0 && m0 + warp * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + warp * 32), buf);
-        } else if (pv) {
-          if (cn == 32 && g.ys[1] == 1 && (g.M % 4) == 0) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4 *>(y + ybase + c0 + j) =
-                  make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < cn) y[ybase + int64_t(c0 + j) * g.ys[1]] = vals[j];
-          }
-        }
-      }
-      if (EPI_TMA && lane == 0) tma_store_wait_all();
-    }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE == 2 ? A_BYTES : 0);
-      for (int kb = 0; kb < tp.num_kb; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(&empty_bar[s], ((kb / STAGES) & 1) ^ 1, &abort_flag, status, 2)) break;
-        uint8_t *a_hi = smem + s * STAGE;
-        uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
-        mbar_arrive_expect_tx(&raw_bar[s], bytes);
-        tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
-        if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
-        if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+        const int n0 = int(t % tp.n_tiles) * BN;
+        const int64_t m0 = (t / tp.n_tiles) * kBM;
+        for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 2);
+          if (!ok) break;
+          uint8_t *a_hi = smem + s * STAGE;
+          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
+          mbar_arrive_expect_tx(&raw_bar[s], bytes);
+          tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
+          if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
+          if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
+        }
       }
     }
   } else {
@@ -454,62 +485,102 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc =
           (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-      for (int kb = 0; kb < tp.num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(CONVERT ? &full_bar[s] : &raw_bar[s], ph, &abort_flag, status, 3)) break;
+      uint32_t it = 0;
+      int ti = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x, ++ti) {
+        const int ab = ti & 1;
+        ok = mbar_wait(&acce_bar[ab], ((ti >> 1) & 1) ^ 1, &abort_flag, status, 7);
+        if (!ok) break;
         tc_fence_after();
-        uint8_t *a_hi = smem + s * STAGE;
-        uint8_t *a_lo = a_hi + A_BYTES;
-        uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
-        uint8_t *b_lo = b_hi + B_BYTES;
-        const uint64_t dah = smem_desc(a_hi), dbh = smem_desc(b_hi);
-        const uint64_t dal = smem_desc(a_lo), dbl = smem_desc(b_lo);
+        const uint32_t dtm = tmem + uint32_t(ab * BN);
+        for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          ok = mbar_wait(CONVERT ? &full_bar[s] : &raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 3);
+          if (!ok) break;
+          tc_fence_after();
+          uint8_t *a_hi = smem + s * STAGE;
+          uint8_t *a_lo = a_hi + A_BYTES;
+          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
+          uint8_t *b_lo = b_hi + B_BYTES;
+          const uint64_t dah = smem_desc(a_hi), dbh = smem_desc(b_hi);
+          const uint64_t dal = smem_desc(a_lo), dbl = smem_desc(b_lo);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-          if (SPLIT3) {
-            mma_tf32(tmem, dal + step, dbh + step, idesc, first);
-            mma_tf32(tmem, dah + step, dbl + step, idesc, 1u);
-            mma_tf32(tmem, dah + step, dbh + step, idesc, 1u);
-          } else {
-            mma_tf32(tmem, dah + step, dbh + step, idesc, first);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            if (SPLIT3) {
+              mma_tf32(dtm, dal + step, dbh + step, idesc, first);
+              mma_tf32(dtm, dah + step, dbl + step, idesc, 1u);
+              mma_tf32(dtm, dah + step, dbh + step, idesc, 1u);
+            } else {
+              mma_tf32(dtm, dah + step, dbh + step, idesc, first);
+            }
           }
+          mma_commit(&empty_bar[s]);
         }
-        mma_commit(&empty_bar[s]);
+        if (ok) mma_commit(&accf_bar[ab]);
       }
-      mma_commit(&done_bar);
-      // MMAs must be complete before TMEM is freed, also on the abort path.
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&done_bar, 0) && clock64() - t0 < kWaitCycles) {
+      // Every issued MMA must finish before TMEM is freed (also on abort):
+      // a last commit, then a bounded wait on it.
+      if (ti > 0) {
+        const int last = (ti - 1) & 1;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&accf_bar[last], ((ti - 1) >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+        }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
 // ---------------------------------------------------------------- weights
-// [part][Npad][Kpad], k = (r*KW + s)*Cg + c; part 0 = TF32(rna) of w,
-// part 1 = w - part 0 (3xTF32 only); zero padding.
-__global__ void pack_tc_kernel(float *__restrict__ dst, const float *__restrict__ w, ConvGeo g, int Npad, int Kpad,
-                               int split3) {
+// [part][Npad][Kpad] with k = (r*KW + s)*Cg + c over the GEMM channel count
+// Cg (which may be padded above the weight's Cw); part 0 = TF32(rna) of w,
+// part 1 = w - part 0 (3xTF32 only); zero padding.  w_kn: the weights are a
+// [K][Cout] matrix (Gemm B with transB = 0) instead of OIHW.
+__global__ void pack_tc_kernel(float *__restrict__ dst, const float *__restrict__ w, ConvGeo g, int Cw, int Npad,
+                               int Kpad, int split3, int w_kn) {
   const int64_t total = int64_t(Npad) * Kpad;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int m = int(i / Kpad), k = int(i % Kpad);
     float v = 0.f;
     if (m < g.M && k < g.K) {
       const int c = k % g.Cg, rs = k / g.Cg, s = rs % g.KW, r = rs / g.KW;
-      v = w[((int64_t(m) * g.Cg + c) * g.KH + r) * g.KW + s];
+      if (c < Cw) v = w_kn ? w[int64_t(c) * g.M + m] : w[((int64_t(m) * Cw + c) * g.KH + r) * g.KW + s];
     }
     const float hi = tf32_rna(v);
     dst[i] = hi;
     if (split3) dst[total + i] = v - hi;
+  }
+}
+
+// Any 4-D fp32 view (strides xs) -> dense NHWC with C4 >= C channels
+// (zero-filled); one thread per (pixel, 4-channel group), so for an NCHW
+// source the loads coalesce along pixels and the stores are 16 bytes.
+__global__ void to_nhwc4_kernel(float *__restrict__ dst, const float *__restrict__ x, int N, int C, int H, int W,
+                                int C4, int64_t xs0, int64_t xs1, int64_t xs2, int64_t xs3) {
+  const int G = C4 / 4;
+  const int64_t total = int64_t(N) * H * W * G;
+  const int64_t HW = int64_t(H) * W;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t pix = i % (int64_t(N) * HW);
+    const int grp = int(i / (int64_t(N) * HW));
+    const int w = int(pix % W);
+    const int h = int((pix / W) % H);
+    const int n = int(pix / HW);
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = grp * 4 + e;
+      v[e] = c < C ? x[n * xs0 + c * xs1 + h * xs2 + w * xs3] : 0.f;
+    }
+    *reinterpret_cast<float4 *>(dst + pix * C4 + grp * 4) = make_float4(v[0], v[1], v[2], v[3]);
   }
 }
 
@@ -546,7 +617,11 @@ struct TcState {
   int amode = 0;
   bool epi_tma = false;
   size_t smem = 0;
+  int grid = 148;
   bool set_attr_only = false;  // dispatch only sets the kernel's smem attribute
+  float *staged_x = nullptr;   // NHWC4 copy of an input that needs relayout
+  ConvGeo src;                 // geometry of the original input (relayout source)
+  ~TcState() { device_free(staged_x); }
 };
 
 template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI>
@@ -555,10 +630,7 @@ int launch_cfg(const TcState &st, const float *x, float *y, const float *bias, c
   auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AMODE, EPI>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  const int64_t mt = ceil_div(st.tp.g.P, kBM);
-  const int64_t blocks = mt * (st.tp.Npad / BN);
-  if (blocks > 0x7fffffffLL) return SPKV2_ERR_UNSUPPORTED;
-  kern<<<unsigned(blocks), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
+  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
   return cuda_status(cudaGetLastError());
 }
 
@@ -579,41 +651,59 @@ int launch_modes(const TcState &st, const float *x, float *y, const float *bias,
   }
 }
 
-int stages_for(int bn, bool split3) {
-  const int stage = (split3 ? 2 : 1) * (kBM * 128 + bn * 128);
-  return std::min(4, (200 * 1024) / stage);
+// Pipeline depth per (BN, split): stages + epilogue staging fit in 227 KB.
+constexpr int stages_of(int bn, bool split3) {
+  return split3 ? (bn == 32 ? 4 : bn == 64 ? 4 : bn == 128 ? 3 : 2) : (bn == 32 ? 6 : bn == 64 ? 6 : bn == 128 ? 6 : 4);
 }
 
 }  // namespace
 
 // Eligible: fp32 in and out, group 1, Cout >= 16, 3xTF32 or TF32 math.
-int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s) {
-  const ConvGeo &g = p.g;
-  if (p.mode != kConvF32 || g.groups != 1 || g.M < 16) return SPKV2_ERR_UNSUPPORTED;
+int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
+                       cudaStream_t s) {
+  const ConvGeo &g0 = p.g;
+  if (p.mode != kConvF32 || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
   if (!encode_fn()) return SPKV2_ERR_UNSUPPORTED;
   TcState *st = new TcState();
   memset(&st->wmap, 0, sizeof(st->wmap));
   memset(&st->amap, 0, sizeof(st->amap));
   memset(&st->ymap, 0, sizeof(st->ymap));
+  st->src = g0;
+  ConvGeo g = g0;
+  const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
+  const bool aligned_in = reinterpret_cast<uintptr_t>(x_dev) % 16 == 0;
+  if (!(nhwc_in && g.C % 4 == 0 && aligned_in)) {
+    // Re-lay the input out as dense NHWC with C rounded up to 4.
+    const int C4 = int(ceil_div(g.C, 4) * 4);
+    st->staged_x = static_cast<float *>(device_alloc(size_t(g.N) * g.H * g.W * C4 * sizeof(float) + 256));
+    if (!st->staged_x) {
+      delete st;
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+    g.C = g.Cg = C4;
+    g.K = g.KH * g.KW * C4;
+    g.xs[0] = int64_t(g.H) * g.W * C4;
+    g.xs[1] = 1;
+    g.xs[2] = int64_t(g.W) * C4;
+    g.xs[3] = C4;
+    x_dev = st->staged_x;
+    p.launches = 2;
+  }
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
   int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128;
-  if (!st->split3 && g.M >= 256) bn = 256;
+  if (g.M >= 256) bn = 256;
+  if (st->split3 && bn == 256) bn = 128;
   if (const char *e = getenv("SPKV2_TC_BN")) {
     const int v = atoi(e);
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
   }
   st->bn = bn;
-  st->stages = stages_for(bn, st->split3);
-  const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
-  const bool c32 = g.C % 32 == 0;
-  if (nhwc_in && c32 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
-      reinterpret_cast<uintptr_t>(x_dev) % 16 == 0)
+  st->stages = stages_of(bn, st->split3);
+  if (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
     st->amode = 2;
-  else if (nhwc_in && g.C % 4 == 0 && reinterpret_cast<uintptr_t>(x_dev) % 16 == 0)
-    st->amode = 1;
   else
-    st->amode = 0;
+    st->amode = 1;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   st->epi_tma = nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
@@ -621,16 +711,23 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);
   tp.Npad = int(ceil_div(g.M, bn) * bn);
   tp.num_kb = tp.Kpad / kBK;
+  tp.n_tiles = tp.Npad / bn;
+  tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  st->grid = int(std::min<int64_t>(tp.tiles, sms));
   const int parts = st->split3 ? 2 : 1;
   float *wtc = static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));
   if (!wtc) {
     delete st;
     return SPKV2_ERR_DEVICE_ALLOC;
   }
-  pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(wtc, static_cast<const float *>(w_raw_dev),
-                                                                           g, tp.Npad, tp.Kpad, st->split3 ? 1 : 0);
+  pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
+      wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0);
   int rc = cuda_status(cudaGetLastError());
-  bool ok = rc == 0 && encode_2d(&st->wmap, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(bn));
+  bool ok = rc == 0 && encode_2d(&st->wmap, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad),
+                                 uint32_t(bn));
   if (ok && st->amode == 2) ok = encode_2d(&st->amap, x_dev, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
   if (ok && st->epi_tma) ok = encode_2d(&st->ymap, y_dev, uint64_t(g.M), uint64_t(g.P), uint64_t(g.M), 32);
   if (!ok) {
@@ -638,9 +735,7 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  st->smem = size_t(st->stages) * size_t(parts) * (kBM * 128 + bn * 128) + 1024;
-  // At most one CTA per SM: TMEM (<= 256 columns) is never contended.
-  st->smem = std::max<size_t>(st->smem, 120 * 1024);
+  st->smem = size_t(st->stages) * size_t(parts) * (kBM * 128 + bn * 128) + kStagingBytes + 1024;
   p.w_tc = wtc;
   p.tc_state = st;
   p.tc_block_n = bn;
@@ -651,8 +746,12 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
   if (rc) return rc;
   static const char *amodes[] = {"gather", "cpasync", "tma"};
   p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) + "_" +
-              amodes[st->amode] + (st->epi_tma ? "_tmastore" : "");
+              amodes[st->amode] + (st->epi_tma ? "_tmastore" : "") + (st->staged_x ? "_relayout" : "");
   return 0;
+}
+
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s) {
+  return conv_tc_prepare_ex(p, w_raw_dev, x_dev, y_dev, false, s);
 }
 
 void conv_tc_release(void *state) { delete static_cast<TcState *>(state); }
@@ -660,22 +759,32 @@ void conv_tc_release(void *state) { delete static_cast<TcState *>(state); }
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s) {
   const TcState &st = *static_cast<const TcState *>(p.tc_state);
   const float *xf = static_cast<const float *>(x);
+  if (st.staged_x && !st.set_attr_only) {
+    const ConvGeo &o = st.src;
+    const int C4 = st.tp.g.C;
+    const int64_t total = int64_t(o.N) * o.H * o.W * (C4 / 4);
+    to_nhwc4_kernel<<<grid_for(total, 256), 256, 0, s>>>(st.staged_x, xf, o.N, o.C, o.H, o.W, C4, o.xs[0], o.xs[1],
+                                                        o.xs[2], o.xs[3]);
+    int rc = cuda_status(cudaGetLastError());
+    if (rc) return rc;
+    xf = st.staged_x;
+  }
   float *yf = static_cast<float *>(y);
   const float *rf = static_cast<const float *>(res);
   const float *bias = p.bias_f;
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_modes<32, 4, true>(st, xf, yf, bias, rf, status, s);
-      case 64: return launch_modes<64, 4, true>(st, xf, yf, bias, rf, status, s);
-      case 256: return launch_modes<256, 2, true>(st, xf, yf, bias, rf, status, s);
-      default: return launch_modes<128, 3, true>(st, xf, yf, bias, rf, status, s);
+      case 32: return launch_modes<32, stages_of(32, true), true>(st, xf, yf, bias, rf, status, s);
+      case 64: return launch_modes<64, stages_of(64, true), true>(st, xf, yf, bias, rf, status, s);
+      case 256: return launch_modes<256, stages_of(256, true), true>(st, xf, yf, bias, rf, status, s);
+      default: return launch_modes<128, stages_of(128, true), true>(st, xf, yf, bias, rf, status, s);
     }
   }
   switch (st.bn) {
-    case 32: return launch_modes<32, 4, false>(st, xf, yf, bias, rf, status, s);
-    case 64: return launch_modes<64, 4, false>(st, xf, yf, bias, rf, status, s);
-    case 256: return launch_modes<256, 4, false>(st, xf, yf, bias, rf, status, s);
-    default: return launch_modes<128, 4, false>(st, xf, yf, bias, rf, status, s);
+    case 32: return launch_modes<32, stages_of(32, false), false>(st, xf, yf, bias, rf, status, s);
+    case 64: return launch_modes<64, stages_of(64, false), false>(st, xf, yf, bias, rf, status, s);
+    case 256: return launch_modes<256, stages_of(256, false), false>(st, xf, yf, bias, rf, status, s);
+    default: return launch_modes<128, stages_of(128, false), false>(st, xf, yf, bias, rf, status, s);
   }
 }
 

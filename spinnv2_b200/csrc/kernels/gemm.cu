@@ -11,7 +11,7 @@
 //   with transposes        - one thread per output, strided loads.
 #include <string.h>
 
-#include "common.cuh"
+#include "conv.h"
 
 namespace spkv2 {
 
@@ -19,6 +19,7 @@ namespace {
 
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvWarps = 8;
+constexpr int kTcMinRows = 16;  // from this many rows a Gemm runs as a tcgen05 1x1 conv
 
 struct GemmPlan : NodePlan {
   int M = 0, K = 0, N = 0;
@@ -26,7 +27,11 @@ struct GemmPlan : NodePlan {
   float alpha = 1.0f;
   int ksplit = 1;
   float *partials = nullptr;  // [ksplit][M][N] for the GEMV path
-  ~GemmPlan() override { device_free(partials); }
+  ConvPlan *tc = nullptr;     // Y = A * B + bias as a 1x1 conv over [M,1,1,K]
+  ~GemmPlan() override {
+    device_free(partials);
+    delete tc;
+  }
 };
 
 // grid (ceil(N/32), ksplit); block 32 x kGemvWarps.  Each block reduces its
@@ -203,6 +208,36 @@ int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     p->variant = "gemv_splitk_fp32";
   } else if (!p->trans_a && !p->trans_b) {
     p->variant = "sgemm_tile64_fp32";
+    const int math = ctx->math_mode == SPKV2_CUDA_MATH_SPEC ? SPKV2_CUDA_MATH_3XTF32 : ctx->math_mode;
+    if (p->M >= kTcMinRows && p->alpha == 1.0f && math != SPKV2_CUDA_MATH_FP32) {
+      // A [M,K] row-major is an NHWC [M,1,1,K] activation; Y [M,N] likewise.
+      ConvPlan *c = new ConvPlan();
+      ConvGeo &g = c->g;
+      g.N = p->M, g.C = p->K, g.H = g.W = 1, g.M = p->N, g.OH = g.OW = 1;
+      g.KH = g.KW = 1, g.sh = g.sw = 1, g.ph = g.pw = 0, g.dh = g.dw = 1;
+      g.groups = 1, g.Cg = p->K, g.Mg = p->N, g.K = p->K, g.P = p->M;
+      g.xs[0] = p->K, g.xs[1] = 1, g.xs[2] = p->K, g.xs[3] = p->K;
+      g.ys[0] = p->N, g.ys[1] = 1, g.ys[2] = p->N, g.ys[3] = p->N;
+      g.act = 0;
+      g.has_bias = node->input_count > 2 ? 1 : 0;
+      g.has_res = 0;
+      c->mode = kConvF32;
+      c->math = math;
+      c->bias_f = g.has_bias ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
+      if (g.has_bias && elem_count(ctx->tensors[node->inputs[2]].record) != size_t(p->N)) g.has_bias = 0;
+      const int trc = conv_tc_prepare_ex(*c, tb.data, ta.data, ty.data, true, ctx->stream);
+      if (trc == 0) {
+        p->tc = c;
+        p->launches = c->launches;
+        p->variant = "gemm_as_" + c->variant;
+      } else {
+        delete c;
+        if (trc != SPKV2_ERR_UNSUPPORTED) {
+          delete p;
+          return trc;
+        }
+      }
+    }
   } else {
     p->variant = "gemm_naive_fp32";
   }
@@ -218,6 +253,7 @@ int gemm_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   const float *A = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
   const float *B = reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data);
   const float *bias = node->input_count > 2 ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
+  if (p->tc) return conv_tc_launch(*p->tc, A, Y, nullptr, ctx->d_status, ctx->stream);
   if (p->partials) {
     const int kpb = int(ceil_div(p->K, p->ksplit));
     dim3 grid(unsigned(ceil_div(p->N, 32)), unsigned(p->ksplit));

@@ -99,3 +99,41 @@ def test_yolo_style_bs1_matches_reference(gpu):
     same = idx_gpu == idx_ref
     assert same.mean() > 0.9
     np.testing.assert_allclose(boxes[same], env[pkg.outputs[1].id][same], atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("rows", [16, 64, 100])
+def test_gemm_rows_on_tensor_cores_match_reference(gpu, rows):
+    spk = compile_pair("gemm_2048_1000", rows)
+    x = seeded_input((rows, 2048))
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x])
+    assert any("gemm_as_tc_3xtf32" in v for v in variants), variants
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("case", ["conv7x7s2_3_64_224", "conv1x1_256_64_56", "conv3x3_512_7", "conv3x3s2_128_128_56"])
+def test_sweep_batch32_matches_reference(gpu, case):
+    from spinnv2_b200.spk import read_spk
+
+    spk = compile_pair(case, 32)
+    x = seeded_input(read_spk(spk["cuda_b200"]).inputs[0].shape)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, _ = _run_gpu(spk["cuda_b200"], [x])
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+
+
+def test_resnet101_tf32_mode_is_close(gpu):
+    """Plain TF32 (10-bit mantissa products) is the fast mode, not the parity
+    mode: it must keep the top-1 class and stay within 2e-3 absolute on the
+    softmax outputs of ResNet-101."""
+    from spinnv2_b200.runtime import MATH_TF32
+
+    spk = compile_pair("resnet101", 2)
+    x = seeded_input((2, 3, 224, 224), seed=11)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x], math_mode=MATH_TF32)
+    assert any("tc_tf32" in v for v in variants)
+    err = float(np.max(np.abs(out[0] - ref)))
+    print("tf32 resnet101 max abs", err)
+    assert err < 2e-3
+    np.testing.assert_array_equal(np.argmax(out[0], axis=1), np.argmax(ref, axis=1))
