@@ -208,7 +208,7 @@ __device__ __forceinline__ void convert_stage(uint8_t *a_hi, uint8_t *a_lo, int 
   }
 }
 
-template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI_TMA>
+template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI_TMA, bool PROMOTE>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap ymap, const float *__restrict__ x,
@@ -256,13 +256,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *stage_buf = smem + STAGES * STAGE + warp * 8192;
     const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
     uint32_t sc = 0;  // TMA-store chunks issued by this warp
-    int ti = 0;
-    for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x, ++ti) {
+    uint32_t gi = 0;  // accumulator hand-offs consumed (per tile, or per K step when promoting)
+    for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * kBM;
-      const int ab = ti & 1;
-      if (!mbar_wait(&accf_bar[ab], (ti >> 1) & 1, &abort_flag, status, 4)) break;
-      tc_fence_after();
+      const int ab = gi & 1;
+      // PROMOTE: every K step's partial product lands in one of two TMEM
+      // buffers and is added here into fp32 registers with round-to-nearest,
+      // so no accumulator chain in the tensor core is longer than one K step.
+      float racc[PROMOTE ? BN : 1];
+      bool failed = false;
+      if (PROMOTE) {
+#pragma unroll
+        for (int j = 0; j < (PROMOTE ? BN : 1); ++j) racc[j] = 0.f;
+        for (int kb = 0; kb < tp.num_kb; ++kb, ++gi) {
+          const int pb = gi & 1;
+          if (!mbar_wait(&accf_bar[pb], (gi >> 1) & 1, &abort_flag, status, 4)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int cb = 0; cb < BN; cb += 32) {
+            uint32_t part[32];
+            tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(pb * BN + cb), part);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) racc[(cb + j) % (PROMOTE ? BN : 1)] += __uint_as_float(part[j]);
+          }
+          tc_fence_before();
+          mbar_arrive(&acce_bar[pb]);
+        }
+      } else {
+        failed = !mbar_wait(&accf_bar[ab], (gi >> 1) & 1, &abort_flag, status, 4);
+        if (!failed) tc_fence_after();
+      }
+      if (failed) break;
       const int row = warp * 32 + lane;
       const int64_t p = m0 + row;
       const bool pv = p < g.P;
@@ -275,14 +303,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
-#pragma unroll 1
+#pragma unroll
       for (int cb = 0; cb < BN; cb += 32) {
         uint32_t acc[32];
-        tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(ab * BN + cb), acc);
-        if (cb + 32 >= BN) {
-          // All of this tile's accumulator has been read: hand the buffer back.
-          tc_fence_before();
-          mbar_arrive(&acce_bar[ab]);
+        if (PROMOTE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(racc[(cb + j) % (PROMOTE ? BN : 1)]);
+        } else {
+          tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(ab * BN + cb), acc);
+          if (cb + 32 >= BN) {
+            // All of this tile's accumulator has been read: hand the buffer back.
+            tc_fence_before();
+            mbar_arrive(&acce_bar[ab]);
+            ++gi;
+          }
         }
         const int c0 = n0 + cb;
         if (c0 >= g.M) continue;  // channel padding (warp-uniform)
@@ -486,15 +520,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc =
           (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
       uint32_t it = 0;
-      int ti = 0;
+      uint32_t gi = 0;  // accumulator hand-offs issued (per tile, or per K step when promoting)
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x, ++ti) {
-        const int ab = ti & 1;
-        ok = mbar_wait(&acce_bar[ab], ((ti >> 1) & 1) ^ 1, &abort_flag, status, 7);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t dtm = tmem + uint32_t(ab * BN);
+      int ab = 0;
+      uint32_t dtm = tmem;
+      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+        if (!PROMOTE) {
+          ab = gi & 1;
+          ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
+          if (!ok) break;
+          tc_fence_after();
+          dtm = tmem + uint32_t(ab * BN);
+        }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
+          if (PROMOTE) {
+            ab = gi & 1;
+            ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
+            if (!ok) break;
+            tc_fence_after();
+            dtm = tmem + uint32_t(ab * BN);
+          }
           const int s = it % STAGES;
           ok = mbar_wait(CONVERT ? &full_bar[s] : &raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 3);
           if (!ok) break;
@@ -508,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-            const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+            const uint32_t first = ((PROMOTE || kb == 0) && kk == 0) ? 0u : 1u;
             if (SPLIT3) {
               mma_tf32(dtm, dal + step, dbh + step, idesc, first);
               mma_tf32(dtm, dah + step, dbl + step, idesc, 1u);
@@ -518,15 +563,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           mma_commit(&empty_bar[s]);
+          if (PROMOTE) {
+            mma_commit(&accf_bar[ab]);
+            ++gi;
+          }
         }
-        if (ok) mma_commit(&accf_bar[ab]);
+        if (!PROMOTE && ok) {
+          mma_commit(&accf_bar[ab]);
+          ++gi;
+        }
       }
       // Every issued MMA must finish before TMEM is freed (also on abort):
-      // a last commit, then a bounded wait on it.
-      if (ti > 0) {
-        const int last = (ti - 1) & 1;
+      // a bounded wait on the last accumulator hand-off.
+      if (gi > 0) {
+        const int last = (gi - 1) & 1;
         const long long t0 = clock64();
-        while (!mbar_try_wait(&accf_bar[last], ((ti - 1) >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+        while (!mbar_try_wait(&accf_bar[last], ((gi - 1) >> 1) & 1) && clock64() - t0 < kWaitCycles) {
         }
       }
     }
@@ -627,7 +679,7 @@ struct TcState {
 template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI>
 int launch_cfg(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
                cudaStream_t s) {
-  auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AMODE, EPI>;
+  auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AMODE, EPI, SPLIT3>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
