@@ -175,6 +175,7 @@ struct TcParams {
   int num_kb;      // Kpad / 32
   int n_tiles;     // Npad / BN
   int64_t tiles;   // m_tiles * n_tiles
+  int group;       // K steps per TMEM partial when promoting (3xTF32)
 };
 
 template <int BN, bool SPLIT3>
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (PROMOTE) {
 #pragma unroll
         for (int j = 0; j < (PROMOTE ? BN : 1); ++j) racc[j] = 0.f;
-        for (int kb = 0; kb < tp.num_kb; ++kb, ++gi) {
+        for (int kb = 0; kb < tp.num_kb; kb += tp.group, ++gi) {
           const int pb = gi & 1;
           if (!mbar_wait(&accf_bar[pb], (gi >> 1) & 1, &abort_flag, status, 4)) {
             failed = true;
@@ -428,9 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             cp_async16(a_hi + swz_off(i * 16 + rsub, chunk), src, in ? 16u : 0u);
           }
           cp_async_arrive(&raw_bar[s]);
-          // Convert the previous K step while this one's copies are in flight.
-          if (it > 0) {
-            const uint32_t pit = it - 1;
+          // Convert the K step issued STAGES-1 steps ago, keeping that many
+          // steps of gathers in flight.  No deadlock: stage it % STAGES frees
+          // once step it-STAGES is consumed, and that step was converted at
+          // iteration it-1.
+          if (it >= uint32_t(STAGES - 1)) {
+            const uint32_t pit = it - (STAGES - 1);
             const int ps = pit % STAGES;
             ok = mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6);
             if (!ok) break;
@@ -482,10 +486,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (AMODE == 1 && ok && it > 0) {
-      const uint32_t pit = it - 1;
-      const int ps = pit % STAGES;
-      if (mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6)) {
+    if (AMODE == 1 && ok) {
+      // Drain: convert the last STAGES-1 issued K steps, oldest first.
+      const uint32_t first = it > uint32_t(STAGES - 1) ? it - (STAGES - 1) : 0;
+      for (uint32_t pit = first; pit < it && ok; ++pit) {
+        const int ps = pit % STAGES;
+        ok = mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6);
+        if (!ok) break;
         uint8_t *p_hi = smem + ps * STAGE;
         convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, at);
         fence_proxy_async();
@@ -533,7 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           dtm = tmem + uint32_t(ab * BN);
         }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
-          if (PROMOTE) {
+          const bool group_start = PROMOTE && kb % tp.group == 0;
+          const bool group_end = PROMOTE && (kb % tp.group == tp.group - 1 || kb == tp.num_kb - 1);
+          if (group_start) {
             ab = gi & 1;
             ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
             if (!ok) break;
@@ -553,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-            const uint32_t first = ((PROMOTE || kb == 0) && kk == 0) ? 0u : 1u;
+            const uint32_t first = ((PROMOTE ? group_start : kb == 0) && kk == 0) ? 0u : 1u;
             if (SPLIT3) {
               mma_tf32(dtm, dal + step, dbh + step, idesc, first);
               mma_tf32(dtm, dah + step, dbl + step, idesc, 1u);
@@ -563,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           mma_commit(&empty_bar[s]);
-          if (PROMOTE) {
+          if (group_end) {
             mma_commit(&accf_bar[ab]);
             ++gi;
           }
@@ -765,6 +774,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.num_kb = tp.Kpad / kBK;
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
+  tp.group = 1;
+  if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
