@@ -106,4 +106,19 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
+// apply_act over a register array, branching once: inside an element loop
+// the compiler may if-convert the switch and evaluate the SiLU expf and
+// divide for every element whatever `act` is.
+template <int N>
+__device__ __forceinline__ void apply_act_n(float (&v)[N], int act) {
+  if (act == 1) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+  } else if (act == 2) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = v[j] / (1.0f + expf(-v[j]));
+  }
+}
+__device__ __forceinline__ void apply_act32(float (&v)[32], int act) { apply_act_n<32>(v, act); }
+
 }  // namespace spkv2

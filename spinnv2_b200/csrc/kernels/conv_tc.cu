@@ -10,25 +10,35 @@
 // channels) in a static round-robin.  Warp roles (320 threads):
 //   warps 0-3  epilogue: TMEM lanes 32w..32w+31 (= tile rows of warp w) ->
 //              registers -> bias, residual, Relu/SiLU -> TMA store staged
-//              through shared memory (NHWC outputs) or direct stores.  The
-//              accumulator is double-buffered in TMEM (2 x BN columns), so
-//              the epilogue of tile i overlaps the mainloop of tile i+1.
-//   warps 4-7  A operand.  AMODE 2 (1x1, stride 1, NHWC, C % 32 == 0): TMA
-//              tile loads (issued by warp 8); AMODE 1 (NHWC, C % 4 == 0):
-//              cp.async 16-byte gathers, zero-fill for padding, completion on
-//              the stage mbarrier; AMODE 0 (generic strides): per-element
-//              gathers through registers.  For AMODE 1/2 the warps convert the
-//              landed tile in place, one stage behind the loads: TF32 hi =
-//              round-to-nearest, lo = x - hi (3xTF32), in the 128B-swizzled
-//              K-major layout the MMA descriptors describe.
+//              through shared memory (NHWC outputs) or direct stores.  TMEM
+//              holds two accumulator buffers, so the epilogue overlaps the
+//              next tile's mainloop.
+//   warps 4-7  A operand.  AMODE 2 (1x1, stride 1, C % 32 == 0): the A tile
+//              arrives by TMA (issued by warp 8) straight into the operand
+//              stage and, for 3xTF32, is split there in place.  AMODE 1 (any
+//              other conv): each thread gathers its 16-byte chunks with
+//              cp.async (zero-fill for padding) into a landing ring of LAND
+//              slots, LAND-1 K steps ahead of the MMA, and later converts ITS
+//              OWN chunks into the operand stage, so a per-thread
+//              cp.async.wait_group is the only synchronisation the landing
+//              needs and a slow MMA never stalls the gathers.
+//              Conversion: TF32 hi = round-to-nearest, lo = x - hi (3xTF32),
+//              in the 128B-swizzled K-major layout the MMA descriptors
+//              describe.
 //   warp 8     TMA producer (one thread): weight panels (hi, and lo for
 //              3xTF32), and the A tile in AMODE 2.  No multicast.
 //   warp 9     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
 //              K=8) and commits stage releases and finished accumulators.
 // 3xTF32: acc += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (three MMAs per K step).
-// Inputs that are not dense NHWC with C % 4 == 0 (the NCHW graph input of a
-// network's first conv, C = 3) are first re-laid out by a small kernel into a
-// plan-owned NHWC buffer with C rounded up to 4, then take AMODE 1.
+// The tensor core's fp32 accumulation truncates, which over long K chains
+// biases the sum (the error grows linearly with K).  In 3xTF32 mode each
+// group of `group` K steps therefore accumulates into its own TMEM buffer,
+// and the epilogue warps add each finished partial into a third TMEM region
+// of running sums with round-to-nearest fp32 adds ("promotion"), so the MMA
+// of the next group overlaps the add of this one.
+// Inputs that are not dense NHWC with C % 4 == 0 (a network's NCHW graph
+// input, C = 3) are first re-laid out into a plan-owned NHWC buffer with C
+// rounded up to 4.
 // Every mbarrier wait is bounded (about a second of clock cycles); on timeout
 // the CTA records a code in the context's status word and winds down.
 #include <cuda.h>
@@ -44,6 +54,7 @@ namespace {
 
 constexpr int kBM = 128;          // tile rows (pixels) = UMMA M
 constexpr int kBK = 32;           // fp32 elements per K step = 128 bytes
+constexpr int kABytes = kBM * 128;
 constexpr int kThreads = 320;
 constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 buffers x 32x32 fp32
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
@@ -120,10 +131,10 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
 }
-
-// Arrive on `bar` once all of this thread's prior cp.async copies landed.
-__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -161,6 +172,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -180,9 +204,8 @@ struct TcParams {
 
 template <int BN, bool SPLIT3>
 struct StageBytes {
-  static constexpr int A = kBM * 128;
   static constexpr int B = BN * 128;
-  static constexpr int value = (SPLIT3 ? 2 : 1) * (A + B);
+  static constexpr int value = (SPLIT3 ? 2 : 1) * (kABytes + B);
 };
 
 // Row / chunk mapping shared by the A loads and the conversion pass: thread t
@@ -191,25 +214,27 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// Converts thread t's chunks of an fp32 A tile at `src` into TF32 hi (and lo)
+// at dst_hi / dst_lo; src may equal dst_hi (in place).
 template <bool SPLIT3>
-__device__ __forceinline__ void convert_stage(uint8_t *a_hi, uint8_t *a_lo, int t) {
+__device__ __forceinline__ void convert_tile(const uint8_t *src, uint8_t *dst_hi, uint8_t *dst_lo, int t) {
   const int chunk = t & 7, rsub = t >> 3;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t off = swz_off(i * 16 + rsub, chunk);
-    const float4 v = *reinterpret_cast<const float4 *>(a_hi + off);
+    const float4 v = *reinterpret_cast<const float4 *>(src + off);
     float4 hi;
     hi.x = tf32_rna(v.x);
     hi.y = tf32_rna(v.y);
     hi.z = tf32_rna(v.z);
     hi.w = tf32_rna(v.w);
-    *reinterpret_cast<float4 *>(a_hi + off) = hi;
+    *reinterpret_cast<float4 *>(dst_hi + off) = hi;
     if (SPLIT3)
-      *reinterpret_cast<float4 *>(a_lo + off) = make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w);
+      *reinterpret_cast<float4 *>(dst_lo + off) = make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w);
   }
 }
 
-template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI_TMA, bool PROMOTE>
+template <int BN, int STAGES, int LAND, bool SPLIT3, int AMODE, bool EPI_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap ymap, const float *__restrict__ x,
@@ -217,11 +242,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                    int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int A_BYTES = StageBytes<BN, SPLIT3>::A;
   constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
   constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
-  constexpr bool CONVERT = (AMODE == 1) || (AMODE == 2 && SPLIT3);
-  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
+  // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
+  // always for gathers, and for TMA-loaded tiles when they must be split.
+  // A TF32 TMA tile goes to the tensor core as loaded (the hardware ignores
+  // the low 13 mantissa bits).
+  constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
+  // TMEM: two accumulator buffers (MMA / epilogue overlap) + the promoted
+  // sums for 3xTF32, rounded up to a power of two >= 32 columns.
+  constexpr int kCols = (SPLIT3 ? 3 : 2) * BN;
+  constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
+  static_assert(kCols <= 512, "accumulators exceed TMEM");
+  uint8_t *land = smem + STAGES * STAGE;    // AMODE 1 landing ring
+  uint8_t *staging = land + LAND * kABytes;  // epilogue TMA-store staging
   __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
@@ -231,9 +265,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&raw_bar[s], AMODE == 2 ? 1 : 128 + 1);
-      mbar_init(&full_bar[s], 128);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&raw_bar[s], 1);     // TMA producer's arrive.expect_tx (+ transaction bytes)
+      mbar_init(&full_bar[s], 128);  // A warps, after converting
+      mbar_init(&empty_bar[s], 1);   // MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
@@ -254,44 +288,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp < 4) {
     // ------------------------------------------------------------ epilogue
-    uint8_t *stage_buf = smem + STAGES * STAGE + warp * 8192;
+    uint8_t *stage_buf = staging + warp * 8192;
     const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
     uint32_t sc = 0;  // TMA-store chunks issued by this warp
-    uint32_t gi = 0;  // accumulator hand-offs consumed (per tile, or per K step when promoting)
+    uint32_t gi = 0;  // accumulator hand-offs consumed (one per K group)
+    const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
+    const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
+    const uint32_t tsum = trow + uint32_t(2 * BN);               // promoted sums (3xTF32)
     for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * kBM;
-      const int ab = gi & 1;
-      // PROMOTE: every K step's partial product lands in one of two TMEM
-      // buffers and is added here into fp32 registers with round-to-nearest,
-      // so no accumulator chain in the tensor core is longer than one K step.
-      float racc[PROMOTE ? BN : 1];
+      // All K groups but the last: add the group's partial into the sums
+      // (round-to-nearest fp32 adds) and hand the partial buffer back.
       bool failed = false;
-      if (PROMOTE) {
-#pragma unroll
-        for (int j = 0; j < (PROMOTE ? BN : 1); ++j) racc[j] = 0.f;
-        for (int kb = 0; kb < tp.num_kb; kb += tp.group, ++gi) {
-          const int pb = gi & 1;
-          if (!mbar_wait(&accf_bar[pb], (gi >> 1) & 1, &abort_flag, status, 4)) {
-            failed = true;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int cb = 0; cb < BN; cb += 32) {
-            uint32_t part[32];
-            tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(pb * BN + cb), part);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) racc[(cb + j) % (PROMOTE ? BN : 1)] += __uint_as_float(part[j]);
-          }
-          tc_fence_before();
-          mbar_arrive(&acce_bar[pb]);
+      for (int gidx = 0; gidx + 1 < ngroups; ++gidx, ++gi) {
+        const int pb = gi & 1;
+        if (!mbar_wait(&accf_bar[pb], (gi >> 1) & 1, &abort_flag, status, 4)) {
+          failed = true;
+          break;
         }
-      } else {
-        failed = !mbar_wait(&accf_bar[ab], (gi >> 1) & 1, &abort_flag, status, 4);
-        if (!failed) tc_fence_after();
+        tc_fence_after();
+#pragma unroll 1
+        for (int cb = 0; cb < BN; cb += 32) {
+          uint32_t part[32];
+          tmem_ld32(trow + uint32_t(pb * BN + cb), part);
+          if (gidx > 0) {
+            uint32_t sum[32];
+            tmem_ld32(tsum + uint32_t(cb), sum);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) part[j] = __float_as_uint(__uint_as_float(part[j]) + __uint_as_float(sum[j]));
+          }
+          tmem_st32(tsum + uint32_t(cb), part);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&acce_bar[pb]);
       }
       if (failed) break;
+      const int ab = gi & 1;
+      if (!mbar_wait(&accf_bar[ab], (gi >> 1) & 1, &abort_flag, status, 4)) break;
+      tc_fence_after();
       const int row = warp * 32 + lane;
       const int64_t p = m0 + row;
       const bool pv = p < g.P;
@@ -304,23 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
-#pragma unroll
-      for (int cb = 0; cb < BN; cb += 32) {
-        uint32_t acc[32];
-        if (PROMOTE) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(racc[(cb + j) % (PROMOTE ? BN : 1)]);
-        } else {
-          tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(ab * BN + cb), acc);
-          if (cb + 32 >= BN) {
-            // All of this tile's accumulator has been read: hand the buffer back.
-            tc_fence_before();
-            mbar_arrive(&acce_bar[ab]);
-            ++gi;
-          }
-        }
+      // Bias, residual, activation and store of accumulator columns
+      // cb..cb+31 of this thread's row.
+      auto store_chunk = [&](int cb, const uint32_t(&acc)[32]) {
         const int c0 = n0 + cb;
-        if (c0 >= g.M) continue;  // channel padding (warp-uniform)
+        if (c0 >= g.M) return;  // channel padding (warp-uniform)
         float vals[32];
         const int cn = min(32, g.M - c0);
         if (cn == 32 && (!g.has_res || rvec)) {
@@ -329,10 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
             const float4 rr = (g.has_res && pv) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
                                                 : make_float4(0, 0, 0, 0);
-            vals[j] = apply_act(__uint_as_float(acc[j]) + b.x + rr.x, g.act);
-            vals[j + 1] = apply_act(__uint_as_float(acc[j + 1]) + b.y + rr.y, g.act);
-            vals[j + 2] = apply_act(__uint_as_float(acc[j + 2]) + b.z + rr.z, g.act);
-            vals[j + 3] = apply_act(__uint_as_float(acc[j + 3]) + b.w + rr.w, g.act);
+            vals[j] = __uint_as_float(acc[j]) + b.x + rr.x;
+            vals[j + 1] = __uint_as_float(acc[j + 1]) + b.y + rr.y;
+            vals[j + 2] = __uint_as_float(acc[j + 2]) + b.z + rr.z;
+            vals[j + 3] = __uint_as_float(acc[j + 3]) + b.w + rr.w;
           }
         } else {
 #pragma unroll
@@ -342,11 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int c = c0 + j;
               if (g.has_bias) v += __ldg(bias + c);
               if (g.has_res && pv) v += __ldg(res + rbase + int64_t(c) * g.rs[1]);
-              v = apply_act(v, g.act);
             }
             vals[j] = v;
           }
         }
+        apply_act32(vals, g.act);  // one uniform branch per chunk
         if (EPI_TMA) {
           uint8_t *buf = stage_buf + (sc & 1) * 4096;
           if (sc >= 2 && lane == 0) tma_store_wait_read1();  // previous store from this buffer has read it
@@ -371,138 +395,109 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (j < cn) y[ybase + int64_t(c0 + j) * g.ys[1]] = vals[j];
           }
         }
+      };
+      // Last K group: partial (+ sums) -> bias/residual/activation -> store.
+#pragma unroll 1
+      for (int cb = 0; cb < BN; cb += 32) {
+        uint32_t acc[32];
+        tmem_ld32(trow + uint32_t(ab * BN + cb), acc);
+        if (ngroups > 1) {
+          uint32_t sum[32];
+          tmem_ld32(tsum + uint32_t(cb), sum);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(sum[j]));
+        }
+        if (cb + 32 >= BN) {
+          // All of this tile's accumulator has been read: hand the buffer back.
+          tc_fence_before();
+          mbar_arrive(&acce_bar[ab]);
+          ++gi;
+        }
+        store_chunk(cb, acc);
       }
     }
     if (EPI_TMA && lane == 0) tma_store_wait_all();
   } else if (warp < 8) {
     // ------------------------------------------------------------ A operand
     const int at = tid - 128;
-    const int chunk = at & 7;
-    const int rsub = at >> 3;
-    uint32_t it = 0;  // global K-step counter (stage ring position)
+    uint32_t it = 0;  // global K-step counter
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
-      const int64_t m0 = (t / tp.n_tiles) * kBM;
-      if (AMODE == 2) {
-        if (CONVERT) {
+    if constexpr (AMODE == 2) {
+      if (CONVERT) {  // 3xTF32: split the TMA-landed tile in place
+        for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
           for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             ok = mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5);
             if (!ok) break;
             uint8_t *a_hi = smem + s * STAGE;
-            convert_stage<SPLIT3>(a_hi, a_hi + A_BYTES, at);
+            convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
             fence_proxy_async();
             mbar_arrive(&full_bar[s]);
           }
         }
-        continue;
       }
-      int rn[8], rih[8], riw[8];
-      bool rvalid[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int64_t p = m0 + i * 16 + rsub;
-        rvalid[i] = p < g.P;
-        const int64_t pp = rvalid[i] ? p : 0;
-        const int ow = int(pp % g.OW);
-        const int64_t q = pp / g.OW;
-        rih[i] = int(q % g.OH) * g.sh - g.ph;
-        riw[i] = ow * g.sw - g.pw;
-        rn[i] = int(q / g.OH);
-      }
-      for (int kb = 0; kb < tp.num_kb && ok; ++kb, ++it) {
-        const int s = it % STAGES;
-        ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 1);
-        if (!ok) break;
+    } else {
+      const int chunk = at & 7;
+      const int rsub = at >> 3;
+      // Converts K step `pit` from its landing slot into its operand stage
+      // once the MMA has released that stage.
+      auto finish = [&](uint32_t pit) -> bool {
+        const int s = pit % STAGES;
+        if (!mbar_wait(&empty_bar[s], ((pit / STAGES) & 1) ^ 1, &abort_flag, status, 1)) return false;
         uint8_t *a_hi = smem + s * STAGE;
-        const int k0 = kb * kBK + chunk * 4;
-        if (AMODE == 1) {
-          // The 4 channels of this chunk share one filter tap (C % 4 == 0).
+        convert_tile<SPLIT3>(land + (pit % LAND) * kABytes, a_hi, a_hi + kABytes, at);
+        fence_proxy_async();
+        mbar_arrive(&full_bar[s]);
+        return true;
+      };
+      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+        const int64_t m0 = (t / tp.n_tiles) * kBM;
+        int rn[8], rih[8], riw[8];
+        bool rvalid[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int64_t p = m0 + i * 16 + rsub;
+          rvalid[i] = p < g.P;
+          const int64_t pp = rvalid[i] ? p : 0;
+          const int ow = int(pp % g.OW);
+          const int64_t q = pp / g.OW;
+          rih[i] = int(q % g.OH) * g.sh - g.ph;
+          riw[i] = ow * g.sw - g.pw;
+          rn[i] = int(q / g.OH);
+        }
+        for (int kb = 0; kb < tp.num_kb && ok; ++kb, ++it) {
+          // Gather K step `it` into landing slot it % LAND.  That slot's
+          // previous step (it - LAND) was converted one iteration ago by this
+          // same thread, which reads only the chunks it loads.
+          uint8_t *slot = land + (it % LAND) * kABytes;
+          const int k0 = kb * kBK + chunk * 4;
           const bool kval = k0 < g.K;
-          const int tap = k0 / g.Cg, c = k0 - tap * g.Cg;
+          const int tap = k0 / g.Cg, c = k0 - tap * g.Cg;  // 4 channels of one tap (C % 4 == 0)
           const int r = tap / g.KW, sx = tap - r * g.KW;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int ih = rih[i] + r * g.dh, iw = riw[i] + sx * g.dw;
             const bool in = kval && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
             const float *src = in ? x + ((int64_t(rn[i]) * g.H + ih) * g.W + iw) * g.C + c : x;
-            cp_async16(a_hi + swz_off(i * 16 + rsub, chunk), src, in ? 16u : 0u);
+            cp_async16(slot + swz_off(i * 16 + rsub, chunk), src, in ? 16u : 0u);
           }
-          cp_async_arrive(&raw_bar[s]);
-          // Convert the K step issued STAGES-1 steps ago, keeping that many
-          // steps of gathers in flight.  No deadlock: stage it % STAGES frees
-          // once step it-STAGES is consumed, and that step was converted at
-          // iteration it-1.
-          if (it >= uint32_t(STAGES - 1)) {
-            const uint32_t pit = it - (STAGES - 1);
-            const int ps = pit % STAGES;
-            ok = mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6);
-            if (!ok) break;
-            uint8_t *p_hi = smem + ps * STAGE;
-            convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, at);
-            fence_proxy_async();
-            mbar_arrive(&full_bar[ps]);
+          cp_async_commit();
+          if (it >= uint32_t(LAND - 1)) {
+            cp_async_wait<LAND - 1>();  // step it-(LAND-1) has landed
+            ok = finish(it - (LAND - 1));
           }
-        } else {
-          float4 v[8];
-          int er[4], es[4], ec[4];
-          bool ek[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int k = k0 + e;
-            ek[e] = k < g.K;
-            const int tap = k / g.Cg;
-            ec[e] = k - tap * g.Cg;
-            er[e] = tap / g.KW;
-            es[e] = tap - er[e] * g.KW;
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float f[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int ih = rih[i] + er[e] * g.dh, iw = riw[i] + es[e] * g.dw;
-              const bool in = ek[e] && rvalid[i] && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
-              f[e] = in ? __ldg(x + rn[i] * g.xs[0] + ec[e] * g.xs[1] + ih * g.xs[2] + iw * g.xs[3]) : 0.f;
-            }
-            v[i] = make_float4(f[0], f[1], f[2], f[3]);
-          }
-          uint8_t *a_lo = a_hi + A_BYTES;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t off = swz_off(i * 16 + rsub, chunk);
-            float4 hi;
-            hi.x = tf32_rna(v[i].x);
-            hi.y = tf32_rna(v[i].y);
-            hi.z = tf32_rna(v[i].z);
-            hi.w = tf32_rna(v[i].w);
-            *reinterpret_cast<float4 *>(a_hi + off) = hi;
-            if (SPLIT3)
-              *reinterpret_cast<float4 *>(a_lo + off) =
-                  make_float4(v[i].x - hi.x, v[i].y - hi.y, v[i].z - hi.z, v[i].w - hi.w);
-          }
-          fence_proxy_async();
-          mbar_arrive(&raw_bar[s]);
         }
       }
-    }
-    if (AMODE == 1 && ok) {
-      // Drain: convert the last STAGES-1 issued K steps, oldest first.
-      const uint32_t first = it > uint32_t(STAGES - 1) ? it - (STAGES - 1) : 0;
-      for (uint32_t pit = first; pit < it && ok; ++pit) {
-        const int ps = pit % STAGES;
-        ok = mbar_wait(&raw_bar[ps], (pit / STAGES) & 1, &abort_flag, status, 6);
-        if (!ok) break;
-        uint8_t *p_hi = smem + ps * STAGE;
-        convert_stage<SPLIT3>(p_hi, p_hi + A_BYTES, at);
-        fence_proxy_async();
-        mbar_arrive(&full_bar[ps]);
+      cp_async_wait<0>();  // nothing of ours in flight past this point
+      if (ok) {
+        const uint32_t first = it > uint32_t(LAND - 1) ? it - (LAND - 1) : 0;
+        for (uint32_t pit = first; pit < it && ok; ++pit) ok = finish(pit);
       }
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE == 2 ? A_BYTES : 0);
+      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE == 2 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
@@ -513,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 2);
           if (!ok) break;
           uint8_t *a_hi = smem + s * STAGE;
-          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
+          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
           mbar_arrive_expect_tx(&raw_bar[s], bytes);
           tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
           if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
@@ -527,21 +522,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc =
           (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
       uint32_t it = 0;
-      uint32_t gi = 0;  // accumulator hand-offs issued (per tile, or per K step when promoting)
+      uint32_t gi = 0;  // accumulator hand-offs issued (one per K group)
       bool ok = true;
       int ab = 0;
       uint32_t dtm = tmem;
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
-        if (!PROMOTE) {
-          ab = gi & 1;
-          ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
-          if (!ok) break;
-          tc_fence_after();
-          dtm = tmem + uint32_t(ab * BN);
-        }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
-          const bool group_start = PROMOTE && kb % tp.group == 0;
-          const bool group_end = PROMOTE && (kb % tp.group == tp.group - 1 || kb == tp.num_kb - 1);
+          const bool group_start = kb % tp.group == 0;
+          const bool group_end = kb % tp.group == tp.group - 1 || kb == tp.num_kb - 1;
           if (group_start) {
             ab = gi & 1;
             ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
@@ -550,19 +538,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             dtm = tmem + uint32_t(ab * BN);
           }
           const int s = it % STAGES;
-          ok = mbar_wait(CONVERT ? &full_bar[s] : &raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 3);
+          const uint32_t ph = (it / STAGES) & 1;
+          // B (and, in AMODE 2, A) lands by TMA on raw_bar; a converted A
+          // tile is signalled on full_bar (in AMODE 2 only after the A warps
+          // saw raw_bar themselves).
+          ok = (AMODE == 2 && CONVERT) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
+          if (ok && CONVERT) ok = mbar_wait(&full_bar[s], ph, &abort_flag, status, 3);
           if (!ok) break;
           tc_fence_after();
           uint8_t *a_hi = smem + s * STAGE;
-          uint8_t *a_lo = a_hi + A_BYTES;
-          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * A_BYTES;
+          uint8_t *a_lo = a_hi + kABytes;
+          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
           uint8_t *b_lo = b_hi + B_BYTES;
           const uint64_t dah = smem_desc(a_hi), dbh = smem_desc(b_hi);
           const uint64_t dal = smem_desc(a_lo), dbl = smem_desc(b_lo);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-            const uint32_t first = ((PROMOTE ? group_start : kb == 0) && kk == 0) ? 0u : 1u;
+            const uint32_t first = (group_start && kk == 0) ? 0u : 1u;
             if (SPLIT3) {
               mma_tf32(dtm, dal + step, dbh + step, idesc, first);
               mma_tf32(dtm, dah + step, dbl + step, idesc, 1u);
@@ -576,10 +569,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&accf_bar[ab]);
             ++gi;
           }
-        }
-        if (!PROMOTE && ok) {
-          mma_commit(&accf_bar[ab]);
-          ++gi;
         }
       }
       // Every issued MMA must finish before TMEM is freed (also on abort):
@@ -669,13 +658,30 @@ bool encode_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t oute
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Pipeline shape per (BN, split, A mode): operand stages and landing slots,
+// sized so stages + landing ring + epilogue staging fit in 227 KB.
+struct PipeShape {
+  int stages, land;
+};
+constexpr PipeShape pipe_shape(int bn, bool split3, int amode) {
+  return amode == 2 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
+                              : PipeShape{bn == 256 ? 4 : 6, 0})
+                    : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
+                              : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
+}
+
+size_t smem_bytes(int bn, bool split3, int amode) {
+  const PipeShape ps = pipe_shape(bn, split3, amode);
+  return size_t(ps.stages) * size_t(split3 ? 2 : 1) * (kABytes + bn * 128) + size_t(ps.land) * kABytes +
+         kStagingBytes + 1024;
+}
+
 struct TcState {
   CUtensorMap wmap, amap, ymap;
   TcParams tp;
   int bn = 128;
-  int stages = 2;
   bool split3 = true;
-  int amode = 0;
+  int amode = 1;
   bool epi_tma = false;
   size_t smem = 0;
   int grid = 148;
@@ -685,36 +691,25 @@ struct TcState {
   ~TcState() { device_free(staged_x); }
 };
 
-template <int BN, int STAGES, bool SPLIT3, int AMODE, bool EPI>
+template <int BN, bool SPLIT3, int AMODE, bool EPI>
 int launch_cfg(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
                cudaStream_t s) {
-  auto kern = conv_tc_kernel<BN, STAGES, SPLIT3, AMODE, EPI, SPLIT3>;
+  constexpr PipeShape ps = pipe_shape(BN, SPLIT3, AMODE);
+  auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
   return cuda_status(cudaGetLastError());
 }
 
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, bool SPLIT3>
 int launch_modes(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
                  cudaStream_t s) {
-  if (st.epi_tma) {
-    switch (st.amode) {
-      case 2: return launch_cfg<BN, STAGES, SPLIT3, 2, true>(st, x, y, bias, res, status, s);
-      case 1: return launch_cfg<BN, STAGES, SPLIT3, 1, true>(st, x, y, bias, res, status, s);
-      default: return launch_cfg<BN, STAGES, SPLIT3, 0, true>(st, x, y, bias, res, status, s);
-    }
-  }
-  switch (st.amode) {
-    case 2: return launch_cfg<BN, STAGES, SPLIT3, 2, false>(st, x, y, bias, res, status, s);
-    case 1: return launch_cfg<BN, STAGES, SPLIT3, 1, false>(st, x, y, bias, res, status, s);
-    default: return launch_cfg<BN, STAGES, SPLIT3, 0, false>(st, x, y, bias, res, status, s);
-  }
-}
-
-// Pipeline depth per (BN, split): stages + epilogue staging fit in 227 KB.
-constexpr int stages_of(int bn, bool split3) {
-  return split3 ? (bn == 32 ? 4 : bn == 64 ? 4 : bn == 128 ? 3 : 2) : (bn == 32 ? 6 : bn == 64 ? 6 : bn == 128 ? 6 : 4);
+  if (st.epi_tma)
+    return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, true>(st, x, y, bias, res, status, s)
+                         : launch_cfg<BN, SPLIT3, 1, true>(st, x, y, bias, res, status, s);
+  return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, false>(st, x, y, bias, res, status, s)
+                       : launch_cfg<BN, SPLIT3, 1, false>(st, x, y, bias, res, status, s);
 }
 
 }  // namespace
@@ -752,19 +747,18 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     p.launches = 2;
   }
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
+  st->amode = (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0) ? 2 : 1;
+  // Tile width: the smallest that covers Cout up to 128; 256 for wide TF32
+  // layers.  3xTF32 keeps 128: two partial buffers plus the promoted sums
+  // take 3 x BN TMEM columns, and TMEM has 512.
   int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128;
-  if (g.M >= 256) bn = 256;
-  if (st->split3 && bn == 256) bn = 128;
+  if (g.M >= 256 && !st->split3) bn = 256;
   if (const char *e = getenv("SPKV2_TC_BN")) {
     const int v = atoi(e);
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
   }
+  if (st->split3 && bn == 256) bn = 128;
   st->bn = bn;
-  st->stages = stages_of(bn, st->split3);
-  if (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
-    st->amode = 2;
-  else
-    st->amode = 1;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   st->epi_tma = nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
@@ -774,8 +768,12 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.num_kb = tp.Kpad / kBK;
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
-  tp.group = 1;
-  if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
+  // 3xTF32 promotes every `group` K steps; TF32 hands off once per tile.
+  tp.group = tp.num_kb;
+  if (st->split3) {
+    tp.group = 2;
+    if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
+  }
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -798,7 +796,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  st->smem = size_t(st->stages) * size_t(parts) * (kBM * 128 + bn * 128) + kStagingBytes + 1024;
+  st->smem = smem_bytes(bn, st->split3, st->amode);
   p.w_tc = wtc;
   p.tc_state = st;
   p.tc_block_n = bn;
@@ -807,9 +805,9 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   rc = conv_tc_launch(p, nullptr, nullptr, nullptr, nullptr, s);
   st->set_attr_only = false;
   if (rc) return rc;
-  static const char *amodes[] = {"gather", "cpasync", "tma"};
-  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) + "_" +
-              amodes[st->amode] + (st->epi_tma ? "_tmastore" : "") + (st->staged_x ? "_relayout" : "");
+  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) +
+              (st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
+              (st->staged_x ? "_relayout" : "");
   return 0;
 }
 
@@ -837,17 +835,16 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   const float *bias = p.bias_f;
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_modes<32, stages_of(32, true), true>(st, xf, yf, bias, rf, status, s);
-      case 64: return launch_modes<64, stages_of(64, true), true>(st, xf, yf, bias, rf, status, s);
-      case 256: return launch_modes<256, stages_of(256, true), true>(st, xf, yf, bias, rf, status, s);
-      default: return launch_modes<128, stages_of(128, true), true>(st, xf, yf, bias, rf, status, s);
+      case 32: return launch_modes<32, true>(st, xf, yf, bias, rf, status, s);
+      case 64: return launch_modes<64, true>(st, xf, yf, bias, rf, status, s);
+      default: return launch_modes<128, true>(st, xf, yf, bias, rf, status, s);
     }
   }
   switch (st.bn) {
-    case 32: return launch_modes<32, stages_of(32, false), false>(st, xf, yf, bias, rf, status, s);
-    case 64: return launch_modes<64, stages_of(64, false), false>(st, xf, yf, bias, rf, status, s);
-    case 256: return launch_modes<256, stages_of(256, false), false>(st, xf, yf, bias, rf, status, s);
-    default: return launch_modes<128, stages_of(128, false), false>(st, xf, yf, bias, rf, status, s);
+    case 32: return launch_modes<32, false>(st, xf, yf, bias, rf, status, s);
+    case 64: return launch_modes<64, false>(st, xf, yf, bias, rf, status, s);
+    case 256: return launch_modes<256, false>(st, xf, yf, bias, rf, status, s);
+    default: return launch_modes<128, false>(st, xf, yf, bias, rf, status, s);
   }
 }
 
