@@ -1,6 +1,6 @@
 #!/usr/bin/env python
-"""Throughput benchmark of the SPINNV2 B200 CUDA target (BASELINE.json metric:
-ResNet-101 img/s at batch 64 per GPU on 1/2/4/8 B200).
+"""Throughput benchmark of the SPINNV2 B200 CUDA target: ResNet-101 img/s at
+batch 64 per GPU on 1/2/4/8 B200.
 
 One step = one ResNet-101 v1.5 forward pass (fp32 activations, 3xTF32 conv
 math by default) over a batch of 64 synthetic N(0,1) 3x224x224 images with
