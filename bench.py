@@ -97,39 +97,6 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_setup(n_gpus: int):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    return world, rank, local
-
-
-def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-
-
-def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
 def conv_flops(pkg) -> tuple[float, list[int]]:
     total, ids = 0.0, []
     for n in pkg.nodes:
@@ -163,8 +130,8 @@ def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps:
     return {"value": batch / per, "step_s": per, "steps": len(times), "times": times}
 
 
-def run_reference_arm(args, world: int, rank: int) -> None:
-    if rank != 0:
+def run_reference_arm(args, group) -> None:
+    if group.rank != 0:
         return
     sample = min(args.batch, args.reference_sample)
     threads = os.cpu_count() or 1
@@ -187,8 +154,10 @@ def run_reference_arm(args, world: int, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_gpu_arm(args, world: int, rank: int, local: int) -> None:
+def run_gpu_arm(args, group) -> None:
     import torch
+
+    world, rank, local = group.world, group.rank, group.local_rank
 
     from spinnv2_b200.compiler import pipeline
     from spinnv2_b200.runtime import MATH_3XTF32, MATH_FP32, MATH_SPEC, MATH_TF32, Runtime
@@ -213,7 +182,7 @@ def run_gpu_arm(args, world: int, rank: int, local: int) -> None:
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    barrier(world)
+    group.barrier()
     torch.cuda.synchronize()
     evs = []
     with torch.cuda.stream(stream):
@@ -226,11 +195,11 @@ def run_gpu_arm(args, world: int, rank: int, local: int) -> None:
             evs.append((s, e))
     rt.synchronize()
     torch.cuda.synchronize()
-    barrier(world)
+    group.barrier()
     clocks = sampler.stop()
     step_ms = [s.elapsed_time(e) for s, e in evs]
     local_total_ms = sum(step_ms)
-    total_ms = max_over_ranks(local_total_ms, world)
+    total_ms = group.max(local_total_ms)
     ms_per_step = total_ms / args.steps
     value = world * args.batch * args.steps / (total_ms / 1000.0)
 
@@ -252,11 +221,11 @@ def run_gpu_arm(args, world: int, rank: int, local: int) -> None:
     rt2.bind_output(0, h_out.data_ptr())
     for _ in range(max(args.warmup, 2)):
         rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
-    barrier(world)
+    group.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_s = group.max(time.perf_counter() - t0)
     e2e_value = world * args.batch * args.steps / e2e_s
     launches = rt.launches_per_run() * args.steps
     rt2.close()
@@ -306,17 +275,22 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_setup(args.gpus)
+    from spinnv2_b200.shard import RankGroup
+
+    if args.impl == "reference":
+        # Host cores only, rank 0 alone: no process group is needed.
+        env = os.environ
+        group = RankGroup(int(env.get("WORLD_SIZE", "1")), int(env.get("RANK", "0")), int(env.get("LOCAL_RANK", "0")),
+                          None)
+    else:
+        group = RankGroup.from_env(backend="nccl", timeout_s=300)
     try:
         if args.impl == "reference":
-            run_reference_arm(args, world, rank)
+            run_reference_arm(args, group)
         else:
-            run_gpu_arm(args, world, rank, local)
+            run_gpu_arm(args, group)
     finally:
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
+        group.close()
 
 
 if __name__ == "__main__":
