@@ -108,6 +108,13 @@ def conv_flops(pkg) -> tuple[float, list[int]]:
     return total, ids
 
 
+def use_all_host_threads() -> None:
+    """OpenMP threads for the reference CPU runtime: every host core (torchrun
+    exports OMP_NUM_THREADS=1 to its workers), unless SPKV2_REF_THREADS says
+    otherwise.  Set before the reference library is first loaded."""
+    os.environ["OMP_NUM_THREADS"] = os.environ.get("SPKV2_REF_THREADS", str(os.cpu_count() or 1))
+
+
 def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
     """Reference CPU runtime (oracle/_ref) img/s on a bounded sample."""
     from oracle import refrt
@@ -134,8 +141,7 @@ def run_reference_arm(args, group) -> None:
     if group.rank != 0:
         return
     sample = min(args.batch, args.reference_sample)
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    use_all_host_threads()
     res = cpu_reference_throughput(args.config, sample, seconds=1e9, max_steps=args.warmup + args.steps)
     timed = res["times"][args.warmup:] or res["times"]
     ms = 1000.0 * sum(timed) / len(timed)
@@ -251,8 +257,7 @@ def run_gpu_arm(args, group) -> None:
                          "peak_basis": f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"},
         }
         if world == 1 and not args.no_cpu_baseline:
-            threads = os.cpu_count() or 1
-            os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+            use_all_host_threads()
             cb = cpu_reference_throughput(args.config, 1, seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": cb["value"], "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
                                     "kind": "reference",
