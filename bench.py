@@ -35,6 +35,13 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "ResNet-101 img/s (bs64 per GPU)"
+
+
+def metric_name(args) -> str:
+    """The fp32 headline metric, or the INT8 ResNet-50 line (--int8)."""
+    if args.int8:
+        return f"ResNet-50 INT8 img/s (bs{args.batch} per GPU)"
+    return METRIC
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -97,10 +104,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def conv_flops(pkg) -> tuple[float, list[int]]:
+def conv_flops(pkg, int8_only: bool = False) -> tuple[float, list[int]]:
+    """2 x MACs of the (int8) convs of one step, and their node ids."""
     total, ids = 0.0, []
     for n in pkg.nodes:
-        if n.op_type == "Conv":
+        if n.op_type == "Conv" and (not int8_only or pkg.tensors[n.inputs[1]].np_dtype == np.int8):
             w = pkg.tensors[n.inputs[1]].shape
             y = pkg.tensors[n.outputs[0]].shape
             total += 2.0 * y[0] * y[1] * y[2] * y[3] * w[1] * w[2] * w[3]
@@ -113,6 +121,29 @@ def use_all_host_threads() -> None:
     exports OMP_NUM_THREADS=1 to its workers), unless SPKV2_REF_THREADS says
     otherwise.  Set before the reference library is first loaded."""
     os.environ["OMP_NUM_THREADS"] = os.environ.get("SPKV2_REF_THREADS", str(os.cpu_count() or 1))
+
+
+def cpu_oracle_int8_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
+    """INT8 CPU baseline: the reference's INT8 conv kernel is ARM-dotprod only
+    (on x86 it falls back to the fp32 loop over int8 bytes), so the INT8
+    baseline is the oracle's C restatement of the INT8 contract (OpenMP over
+    output channels) running the same package, timed on a bounded sample."""
+    from oracle import harness
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.spk import read_spk
+
+    spk = pipeline.compile_config(config, batch, targets=("cuda_b200",), int8=True)["cuda_b200"]
+    pkg = read_spk(spk)
+    x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+    harness.run_spk(pkg, [x])
+    times = []
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds and (max_steps is None or len(times) < max_steps):
+        t0 = time.perf_counter()
+        harness.run_spk(pkg, [x])
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    return {"value": batch / per, "step_s": per, "steps": len(times), "times": times}
 
 
 def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
@@ -142,19 +173,23 @@ def run_reference_arm(args, group) -> None:
         return
     sample = min(args.batch, args.reference_sample)
     use_all_host_threads()
-    res = cpu_reference_throughput(args.config, sample, seconds=1e9, max_steps=args.warmup + args.steps)
+    timer = cpu_oracle_int8_throughput if args.int8 else cpu_reference_throughput
+    res = timer(args.config, sample, seconds=1e9, max_steps=args.warmup + args.steps)
     timed = res["times"][args.warmup:] or res["times"]
     ms = 1000.0 * sum(timed) / len(timed)
     value = sample / (ms / 1000.0)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": metric_name(args), "value": value, "unit": "img/s", "n_gpus": args.gpus,
         "steps": len(timed), "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config} fp32 forward, batch {args.batch}", "model": args.config,
-                   "global_batch": args.batch, "sample_batch_per_step": sample, "runtime": "reference cpu_generic "
-                   "(AVX2/FMA, OpenMP), BNNS token removed from the profile"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.int8 else "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config} {'int8' if args.int8 else 'fp32'} forward, batch {args.batch}",
+                   "model": args.config, "global_batch": args.batch, "sample_batch_per_step": sample,
+                   "runtime": ("INT8 oracle (C restatement of the INT8 contract, OpenMP); the reference INT8 kernel "
+                               "is ARM-dotprod only") if args.int8 else
+                   "reference cpu_generic (AVX2/FMA, OpenMP), BNNS token removed from the profile"},
         "cpu_baseline": {"value": value, "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
-                         "kind": "reference", "sample": f"{sample} images per step, {len(timed)} steps"},
+                         "kind": "port" if args.int8 else "reference",
+                         "sample": f"{sample} images per step, {len(timed)} steps"},
         "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -170,7 +205,7 @@ def run_gpu_arm(args, group) -> None:
 
     math_mode = {"spec": MATH_SPEC, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32, "fp32": MATH_FP32}[args.math]
     torch.cuda.set_device(local)
-    spk = pipeline.compile_config(args.config, args.batch, targets=("cuda_b200",), seed=0)["cuda_b200"]
+    spk = pipeline.compile_config(args.config, args.batch, targets=("cuda_b200",), seed=0, int8=args.int8)["cuda_b200"]
     rt = Runtime(spk, device=local, math_mode=math_mode, graph=True)
     pkg = rt.package
     in_t, out_t = pkg.inputs[0], pkg.outputs[0]
@@ -210,12 +245,17 @@ def run_gpu_arm(args, group) -> None:
     value = world * args.batch * args.steps / (total_ms / 1000.0)
 
     # ---- roofline of the conv kernels (per-node events) ----
-    flops, conv_ids = conv_flops(pkg)
+    flops, conv_ids = conv_flops(pkg, int8_only=args.int8)
     prof = np.stack([rt.profile_nodes() for _ in range(3)])
     node_ms = prof.mean(axis=0)
     conv_ms = float(node_ms[conv_ids].sum())
     pk, basis = peaks()
-    tf32_peak = pk["bf16_tflops"] / 2.0
+    if args.int8:
+        peak, peak_unit = pk["bf16_tflops"] * 2.0, "TOPS"
+        peak_basis = f"INT8 dense = bf16 {basis} {pk['bf16_tflops']} x 2 (derived)"
+    else:
+        peak, peak_unit = pk["bf16_tflops"] / 2.0, "TFLOP/s"
+        peak_basis = f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"
     achieved = flops / (conv_ms / 1000.0) / 1e12
     variants = sorted({rt.node_variant(i) for i in conv_ids})
 
@@ -238,11 +278,12 @@ def run_gpu_arm(args, group) -> None:
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args), "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config} v1.5 forward, batch {args.batch} per GPU, 224x224, fp32 "
-                                   f"activations, conv math {args.math}",
+            "vs_baseline": None, "dtype": "int8" if args.int8 else "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config} v1.5 forward, batch {args.batch} per GPU, 224x224, " + (
+                           "int8 activations between convs (fp32 first conv and head)" if args.int8 else
+                           f"fp32 activations, conv math {args.math}"),
                        "model": args.config, "global_batch": args.batch * world, "per_gpu_batch": args.batch,
                        "seq_len": None, "parallelism": f"batch-sharded x{world}, no collectives",
                        "l2": "flushed between steps (256 MiB write)", "conv_variants": variants},
@@ -250,17 +291,17 @@ def run_gpu_arm(args, group) -> None:
             "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(np.prod(out_t.shape) * 4)},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-                         "frac": achieved / tf32_peak, "traffic": None,
-                         "kernel": "all Conv launches of one step", "flops_per_step": flops,
-                         "conv_ms_per_step": conv_ms,
-                         "peak_basis": f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": peak_unit,
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": ("all int8 Conv launches" if args.int8 else "all Conv launches") + " of one step",
+                         "flops_per_step": flops, "conv_ms_per_step": conv_ms, "peak_basis": peak_basis},
         }
         if world == 1 and not args.no_cpu_baseline:
             use_all_host_threads()
-            cb = cpu_reference_throughput(args.config, 1, seconds=args.cpu_seconds)
+            timer = cpu_oracle_int8_throughput if args.int8 else cpu_reference_throughput
+            cb = timer(args.config, 1, seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": cb["value"], "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
-                                    "kind": "reference",
+                                    "kind": "port" if args.int8 else "reference",
                                     "sample": f"batch 1, {cb['steps']} runs over ~{args.cpu_seconds:.0f} s"}
         print(json.dumps(line), flush=True)
     rt.close()
@@ -278,6 +319,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--reference-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--int8", action="store_true", help="INT8 quantised network (use with --config resnet50)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     from spinnv2_b200.shard import RankGroup

@@ -121,4 +121,12 @@ __device__ __forceinline__ void apply_act_n(float (&v)[N], int act) {
 }
 __device__ __forceinline__ void apply_act32(float (&v)[32], int act) { apply_act_n<32>(v, act); }
 
+// int8 requantisation rounding: round half to even, clamp to [lo, 127].
+__device__ __forceinline__ int8_t sat_rne_i8(float v, int lo) {
+  int q = __float2int_rn(v);
+  q = q < lo ? lo : q;
+  q = q > 127 ? 127 : q;
+  return int8_t(q);
+}
+
 }  // namespace spkv2

@@ -40,13 +40,6 @@ __global__ void pack_simt_kernel(T *__restrict__ dst, const T *__restrict__ w, C
   }
 }
 
-__device__ __forceinline__ int8_t sat_rne_i8(float v, int lo) {
-  int q = __float2int_rn(v);  // round half to even
-  q = q < lo ? lo : q;
-  q = q > 127 ? 127 : q;
-  return int8_t(q);
-}
-
 constexpr int kBM = 64, kBN = 64, kBK = 16;
 
 // A-operand element (pixel p, reduction index k) of the implicit GEMM.
@@ -129,10 +122,12 @@ __global__ void __launch_bounds__(256) conv_simt_f32_kernel(const float *__restr
 
 // INT8 implicit GEMM on CUDA cores (exact int32 accumulation) with the
 // requantising epilogue.
+// OUT32: int32 output acc + b_q (no requantisation).
+template <bool OUT32>
 __global__ void __launch_bounds__(256) conv_simt_i8_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ wp,
                                                            const int32_t *__restrict__ bias_q,
                                                            const float *__restrict__ scale_m,
-                                                           const int8_t *__restrict__ res, int8_t *__restrict__ y,
+                                                           const int8_t *__restrict__ res, void *__restrict__ yv,
                                                            ConvGeo g) {
   __shared__ int32_t As[kBK][kBM + 4];
   __shared__ int32_t Bs[kBK][kBN + 4];
@@ -174,10 +169,15 @@ __global__ void __launch_bounds__(256) conv_simt_i8_kernel(const int8_t *__restr
       if (ml >= g.Mg) continue;
       const int m = grp * g.Mg + ml;
       const int32_t a = acc[i][j] + (g.has_bias ? bias_q[m] : 0);
+      const int64_t yo = n * g.ys[0] + m * g.ys[1] + oh * g.ys[2] + ow * g.ys[3];
+      if (OUT32) {
+        static_cast<int32_t *>(yv)[yo] = a;
+        continue;
+      }
       float v = __fmul_rn(float(a), scale_m[m]);
       if (g.has_res)
         v = __fadd_rn(v, __fmul_rn(float(res[n * g.rs[0] + m * g.rs[1] + oh * g.rs[2] + ow * g.rs[3]]), g.res_scale));
-      y[n * g.ys[0] + m * g.ys[1] + oh * g.ys[2] + ow * g.ys[3]] = sat_rne_i8(v, lo);
+      static_cast<int8_t *>(yv)[yo] = sat_rne_i8(v, lo);
     }
   }
 }
@@ -214,9 +214,14 @@ int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res,
                                                               static_cast<const float *>(res), y, g);
       break;
     case kConvI8:
-      conv_simt_i8_kernel<<<grid, 256, 0, s>>>(static_cast<const int8_t *>(x), static_cast<const int8_t *>(p.w_simt),
-                                               p.bias_q, p.scale_m, static_cast<const int8_t *>(res),
-                                               static_cast<int8_t *>(y), g);
+      conv_simt_i8_kernel<false><<<grid, 256, 0, s>>>(static_cast<const int8_t *>(x),
+                                                      static_cast<const int8_t *>(p.w_simt), p.bias_q, p.scale_m,
+                                                      static_cast<const int8_t *>(res), y, g);
+      break;
+    case kConvI8ToI32:
+      conv_simt_i8_kernel<true><<<grid, 256, 0, s>>>(static_cast<const int8_t *>(x),
+                                                     static_cast<const int8_t *>(p.w_simt), p.bias_q, nullptr,
+                                                     nullptr, y, g);
       break;
     default: return SPKV2_ERR_UNSUPPORTED;
   }
@@ -275,53 +280,65 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     p->mode = kConvF32ToI8;
   else if (dx == SPKV2_DTYPE_INT8 && dw == SPKV2_DTYPE_INT8 && dy == SPKV2_DTYPE_INT8)
     p->mode = kConvI8;
+  else if (dx == SPKV2_DTYPE_INT8 && dw == SPKV2_DTYPE_INT8 && dy == SPKV2_DTYPE_INT32)
+    p->mode = kConvI8ToI32;
   else {
     delete p;
     return SPKV2_ERR_UNSUPPORTED;
   }
+  const bool int_acc = p->mode == kConvI8 || p->mode == kConvI8ToI32;
   bool ok = true;
   if (g.has_bias) {
     const TensorState &tb = ctx->tensors[node->inputs[2]];
-    const uint16_t want = p->mode == kConvI8 ? SPKV2_DTYPE_INT32 : SPKV2_DTYPE_FP32;
+    const uint16_t want = int_acc ? SPKV2_DTYPE_INT32 : SPKV2_DTYPE_FP32;
     if (tb.record->dtype != want || elem_count(tb.record) != size_t(g.M)) ok = false;
-    p->bias_f = reinterpret_cast<const float *>(tb.data);
+    if (!int_acc) p->bias_f = reinterpret_cast<const float *>(tb.data);
   }
   if (g.has_res) {
     const uint16_t want = p->mode == kConvI8 ? SPKV2_DTYPE_INT8 : SPKV2_DTYPE_FP32;
-    if (ctx->tensors[node->inputs[3]].record->dtype != want) ok = false;
+    if (ctx->tensors[node->inputs[3]].record->dtype != want || p->mode == kConvI8ToI32) ok = false;
   }
   if (p->mode == kConvF32ToI8) {
     const float sy = per_tensor_scale(ctx, node->outputs[0], &ok);
     g.out_scale_inv = 1.0f / sy;
   }
-  if (p->mode == kConvI8) {
-    if (g.act == 2) ok = false;  // SiLU has no int8 requant form
+  if (int_acc && g.act == 2) ok = false;  // SiLU has no int8 requant form
+  if (p->mode == kConvI8ToI32 && g.act != 0) ok = false;
+  // Per-channel int32 bias and requant multipliers, padded to a multiple of
+  // 32 channels (zeros) so the epilogue may read whole 16-byte vectors.
+  const size_t mpad = size_t(ceil_div(g.M, 32) * 32);
+  if (ok && int_acc && g.has_bias) {
+    p->bias_q = static_cast<int32_t *>(device_alloc(sizeof(int32_t) * mpad));
+    if (!p->bias_q) {
+      delete p;
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+    cudaMemsetAsync(p->bias_q, 0, sizeof(int32_t) * mpad, ctx->stream);
+    cudaMemcpyAsync(p->bias_q, ctx->tensors[node->inputs[2]].data, sizeof(int32_t) * size_t(g.M),
+                    cudaMemcpyDeviceToDevice, ctx->stream);
+  }
+  if (ok && p->mode == kConvI8) {
     const float sx = per_tensor_scale(ctx, node->inputs[0], &ok);
     const float sy = per_tensor_scale(ctx, node->outputs[0], &ok);
     const Spkv2QuantParamRecord *wq = find_quant_param(ctx, node->inputs[1]);
     const float *sw = quant_scales(ctx, wq);
     if (!sw || wq->num_channels != uint32_t(g.M)) ok = false;
     if (ok) {
-      std::vector<float> m(size_t(g.M));
+      std::vector<float> m(mpad, 0.0f);
       for (int c = 0; c < g.M; ++c) {
         const float t = sx * sw[c];
         m[size_t(c)] = t / sy;
       }
-      p->scale_m = static_cast<float *>(device_alloc(sizeof(float) * size_t(g.M)));
+      p->scale_m = static_cast<float *>(device_alloc(sizeof(float) * mpad));
       if (!p->scale_m) {
         delete p;
         return SPKV2_ERR_DEVICE_ALLOC;
       }
-      cudaMemcpyAsync(p->scale_m, m.data(), sizeof(float) * size_t(g.M), cudaMemcpyHostToDevice, ctx->stream);
-      if (g.has_bias) p->bias_q = nullptr, p->bias_f = nullptr;
-      if (g.has_bias) {
-        p->bias_q = static_cast<int32_t *>(device_alloc(sizeof(int32_t) * size_t(g.M)));
-        if (!p->bias_q) {
-          delete p;
-          return SPKV2_ERR_DEVICE_ALLOC;
-        }
-        cudaMemcpyAsync(p->bias_q, ctx->tensors[node->inputs[2]].data, sizeof(int32_t) * size_t(g.M),
-                        cudaMemcpyDeviceToDevice, ctx->stream);
+      cudaMemcpyAsync(p->scale_m, m.data(), sizeof(float) * mpad, cudaMemcpyHostToDevice, ctx->stream);
+      // The host vector must outlive the copy.
+      if ((rc = cuda_status(cudaStreamSynchronize(ctx->stream)))) {
+        delete p;
+        return rc;
       }
       if (g.has_res) {
         const float sr = per_tensor_scale(ctx, node->inputs[3], &ok);
@@ -344,32 +361,35 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   }
   p->math = math;
 
-  // Packed weights for the CUDA-core kernel (also the fallback of every
-  // shape the tensor-core kernel does not take).
-  const size_t esz = p->mode == kConvI8 ? 1 : 4;
-  p->w_simt = device_alloc(size_t(g.M) * g.K * esz);
-  if (!p->w_simt) {
-    delete p;
-    return SPKV2_ERR_DEVICE_ALLOC;
-  }
-  const int64_t total = int64_t(g.M) * g.K;
-  if (esz == 1)
-    pack_simt_kernel<int8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
-        static_cast<int8_t *>(p->w_simt), reinterpret_cast<const int8_t *>(tw.data), g);
-  else
-    pack_simt_kernel<float><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
-        static_cast<float *>(p->w_simt), reinterpret_cast<const float *>(tw.data), g);
-  if ((rc = cuda_status(cudaGetLastError()))) {
-    delete p;
-    return rc;
-  }
-  p->variant = p->mode == kConvI8 ? "simt_int8" : "simt_fp32";
+  // Tensor-core path first; the CUDA-core kernel takes every shape it
+  // declines (and every conv in FP32 math mode).
   if (math != SPKV2_CUDA_MATH_FP32) {
-    rc = conv_tc_prepare(*p, tw.data, tx.data, ty.data, ctx->stream);
+    rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ctx->stream)
+                 : conv_tc_prepare(*p, tw.data, tx.data, ty.data, ctx->stream);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;
       return rc;
     }
+  }
+  if (!p->w_tc) {
+    const size_t esz = int_acc ? 1 : 4;
+    p->w_simt = device_alloc(size_t(g.M) * g.K * esz);
+    if (!p->w_simt) {
+      delete p;
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+    const int64_t total = int64_t(g.M) * g.K;
+    if (esz == 1)
+      pack_simt_kernel<int8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+          static_cast<int8_t *>(p->w_simt), reinterpret_cast<const int8_t *>(tw.data), g);
+    else
+      pack_simt_kernel<float><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
+          static_cast<float *>(p->w_simt), reinterpret_cast<const float *>(tw.data), g);
+    if ((rc = cuda_status(cudaGetLastError()))) {
+      delete p;
+      return rc;
+    }
+    p->variant = int_acc ? (p->mode == kConvI8ToI32 ? "simt_int8_i32out" : "simt_int8") : "simt_fp32";
   }
   set_node_plan(ctx, node, p);
   return 0;
@@ -382,7 +402,9 @@ int conv_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   const void *x = ctx->tensors[node->inputs[0]].data;
   void *y = ctx->tensors[node->outputs[0]].data;
   const void *res = p->g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
-  if (p->w_tc) return conv_tc_launch(*p, x, y, res, ctx->d_status, ctx->stream);
+  if (p->w_tc)
+    return p->tc_i8 ? conv_tc_i8_launch(*p, x, y, res, ctx->d_status, ctx->stream)
+                    : conv_tc_launch(*p, x, y, res, ctx->d_status, ctx->stream);
   return conv_simt_launch(*p, x, y, res, ctx->stream);
 }
 

@@ -10,6 +10,7 @@ enum ConvMode : int {
   kConvF32 = 0,     // fp32 x, fp32 w -> fp32 y
   kConvF32ToI8 = 1, // fp32 x, fp32 w -> int8 y   (quantising epilogue)
   kConvI8 = 2,      // int8 x, int8 w -> int8 y   (int32 acc, requantised)
+  kConvI8ToI32 = 3, // int8 x, int8 w -> int32 y  (acc + int32 bias, no requantisation)
 };
 
 // Geometry and epilogue parameters, passed by value to the kernels.
@@ -28,6 +29,7 @@ struct ConvGeo {
 };
 
 void conv_tc_release(void *state);
+void conv_tc_i8_release(void *state);
 
 struct ConvPlan : NodePlan {
   ConvGeo g{};
@@ -40,9 +42,10 @@ struct ConvPlan : NodePlan {
   const float *bias_f = nullptr;  // fp32 bias (device weights)
   int tc_block_n = 0;      // tcgen05 tile width in output channels
   int tc_kpad = 0;         // padded K of the tcgen05 panels
-  void *tc_state = nullptr;  // tensor map + launch configuration (conv_tc.cu)
+  void *tc_state = nullptr;  // tensor maps + launch configuration (conv_tc.cu / conv_tc_i8.cu)
+  bool tc_i8 = false;        // tc_state belongs to the kind::i8 kernel
   ~ConvPlan() override {
-    if (tc_state) conv_tc_release(tc_state);
+    if (tc_state) tc_i8 ? conv_tc_i8_release(tc_state) : conv_tc_release(tc_state);
     device_free(w_simt);
     device_free(w_tc);
     device_free(bias_q);
@@ -59,5 +62,9 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
                        cudaStream_t s);
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
+
+// tcgen05 kind::i8 path (conv_tc_i8.cu) for kConvI8 / kConvI8ToI32.
+int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaStream_t s);
+int conv_tc_i8_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
 
 }  // namespace spkv2

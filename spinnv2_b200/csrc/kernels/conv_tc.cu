@@ -47,149 +47,19 @@
 #include <string.h>
 
 #include "conv.h"
+#include "tcgen05.cuh"
 
 namespace spkv2 {
 
 namespace {
+
+using namespace tc;
 
 constexpr int kBM = 128;          // tile rows (pixels) = UMMA M
 constexpr int kBK = 32;           // fp32 elements per K step = 128 bytes
 constexpr int kABytes = kBM * 128;
 constexpr int kThreads = 320;
 constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 buffers x 32x32 fp32
-constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
-
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
-                   smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false on timeout or when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
-                                          int code) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      *abort_flag = 1;
-      if (status) atomicExch(status, code);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(smem_u32(src))
-               : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-__device__ __forceinline__ void tma_store_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// 16-byte async copy global -> shared; src_bytes = 0 writes zeros.
-__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, 128B-swizzled operand: SBO = 1024 B between 8-row groups,
-// LBO = 16 B (unused for swizzled K-major), descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t smem_desc(const void *p) {
-  const uint64_t addr = smem_u32(p);
-  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 
 // ---------------------------------------------------------------- kernel
 struct TcParams {
@@ -200,6 +70,7 @@ struct TcParams {
   int n_tiles;     // Npad / BN
   int64_t tiles;   // m_tiles * n_tiles
   int group;       // K steps per TMEM partial when promoting (3xTF32)
+  int out_i8;      // quantise the output: y = clamp(rne(act(v) * (1 / s_y)), -128, 127)
 };
 
 template <int BN, bool SPLIT3>
@@ -371,6 +242,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         apply_act32(vals, g.act);  // one uniform branch per chunk
+        if (tp.out_i8) {
+          // fp32 conv with an int8 output (the first conv of an INT8 network).
+          if (!pv) return;
+          int8_t *y8 = reinterpret_cast<int8_t *>(y);
+          if (cn == 32 && g.ys[1] == 1 && (g.M % 16) == 0) {
+            uint32_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint32_t b = 0;
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                b |= (uint32_t(sat_rne_i8(__fmul_rn(vals[4 * j + e], g.out_scale_inv), -128)) & 0xffu) << (8 * e);
+              w[j] = b;
+            }
+            *reinterpret_cast<uint4 *>(y8 + ybase + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4 *>(y8 + ybase + c0 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < cn) y8[ybase + int64_t(c0 + j) * g.ys[1]] = int8_t(sat_rne_i8(__fmul_rn(vals[j], g.out_scale_inv), -128));
+          }
+          return;
+        }
         if (EPI_TMA) {
           uint8_t *buf = stage_buf + (sc & 1) * 4096;
           if (sc >= 2 && lane == 0) tma_store_wait_read1();  // previous store from this buffer has read it
@@ -634,30 +528,6 @@ __global__ void to_nhwc4_kernel(float *__restrict__ dst, const float *__restrict
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D fp32 tensor map, 128-byte swizzle: dims {inner, outer}, row pitch in
-// elements, box {32, box_rows}.
-bool encode_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_rows) {
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {pitch * sizeof(float)};
-  const cuuint32_t box[2] = {uint32_t(kBK), box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // Pipeline shape per (BN, split, A mode): operand stages and landing slots,
 // sized so stages + landing ring + epilogue staging fit in 227 KB.
 struct PipeShape {
@@ -688,28 +558,43 @@ struct TcState {
   bool set_attr_only = false;  // dispatch only sets the kernel's smem attribute
   float *staged_x = nullptr;   // NHWC4 copy of an input that needs relayout
   ConvGeo src;                 // geometry of the original input (relayout source)
+  const void *amap_base = nullptr, *ymap_base = nullptr;  // pointers the A / Y maps were encoded for
   ~TcState() { device_free(staged_x); }
 };
 
+bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
+  const ConvGeo &g = st.tp.g;
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
+}
+
+bool encode_y(const TcState &st, CUtensorMap *map, const void *y) {
+  const ConvGeo &g = st.tp.g;
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, uint64_t(g.M), uint64_t(g.P), uint64_t(g.M), 32);
+}
+
+struct Maps {
+  CUtensorMap a, y;
+};
+
 template <int BN, bool SPLIT3, int AMODE, bool EPI>
-int launch_cfg(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
-               cudaStream_t s) {
+int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
+               int *status, cudaStream_t s) {
   constexpr PipeShape ps = pipe_shape(BN, SPLIT3, AMODE);
   auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, st.amap, st.ymap, x, bias, res, y, st.tp, status);
+  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status);
   return cuda_status(cudaGetLastError());
 }
 
 template <int BN, bool SPLIT3>
-int launch_modes(const TcState &st, const float *x, float *y, const float *bias, const float *res, int *status,
-                 cudaStream_t s) {
+int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
+                 int *status, cudaStream_t s) {
   if (st.epi_tma)
-    return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, true>(st, x, y, bias, res, status, s)
-                         : launch_cfg<BN, SPLIT3, 1, true>(st, x, y, bias, res, status, s);
-  return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, false>(st, x, y, bias, res, status, s)
-                       : launch_cfg<BN, SPLIT3, 1, false>(st, x, y, bias, res, status, s);
+    return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, status, s)
+                         : launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, status, s);
+  return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, status, s)
+                       : launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, status, s);
 }
 
 }  // namespace
@@ -718,7 +603,7 @@ int launch_modes(const TcState &st, const float *x, float *y, const float *bias,
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
                        cudaStream_t s) {
   const ConvGeo &g0 = p.g;
-  if (p.mode != kConvF32 || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
+  if ((p.mode != kConvF32 && p.mode != kConvF32ToI8) || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
   if (!encode_fn()) return SPKV2_ERR_UNSUPPORTED;
   TcState *st = new TcState();
@@ -760,7 +645,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   if (st->split3 && bn == 256) bn = 128;
   st->bn = bn;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
-  st->epi_tma = nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
+  st->epi_tma = p.mode == kConvF32 && nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
   tp.g = g;
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);
@@ -769,6 +654,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
   // 3xTF32 promotes every `group` K steps; TF32 hands off once per tile.
+  tp.out_i8 = p.mode == kConvF32ToI8 ? 1 : 0;
   tp.group = tp.num_kb;
   if (st->split3) {
     tp.group = 2;
@@ -787,10 +673,12 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
       wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0);
   int rc = cuda_status(cudaGetLastError());
-  bool ok = rc == 0 && encode_2d(&st->wmap, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad),
+  bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad),
                                  uint32_t(bn));
-  if (ok && st->amode == 2) ok = encode_2d(&st->amap, x_dev, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
-  if (ok && st->epi_tma) ok = encode_2d(&st->ymap, y_dev, uint64_t(g.M), uint64_t(g.P), uint64_t(g.M), 32);
+  if (ok && st->amode == 2) ok = encode_a(*st, &st->amap, x_dev);
+  if (ok && st->epi_tma) ok = encode_y(*st, &st->ymap, y_dev);
+  st->amap_base = x_dev;
+  st->ymap_base = y_dev;
   if (!ok) {
     device_free(wtc);
     delete st;
@@ -833,18 +721,25 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   float *yf = static_cast<float *>(y);
   const float *rf = static_cast<const float *>(res);
   const float *bias = p.bias_f;
+  // Tensor maps follow the tensors: a graph input or output rebound to
+  // another device buffer since prepare gets freshly encoded maps.
+  Maps mp{st.amap, st.ymap};
+  if (!st.set_attr_only) {
+    if (st.amode == 2 && !st.staged_x && xf != st.amap_base && !encode_a(st, &mp.a, xf)) return SPKV2_ERR_UNSUPPORTED;
+    if (st.epi_tma && yf != st.ymap_base && !encode_y(st, &mp.y, yf)) return SPKV2_ERR_UNSUPPORTED;
+  }
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_modes<32, true>(st, xf, yf, bias, rf, status, s);
-      case 64: return launch_modes<64, true>(st, xf, yf, bias, rf, status, s);
-      default: return launch_modes<128, true>(st, xf, yf, bias, rf, status, s);
+      case 32: return launch_modes<32, true>(st, mp, xf, yf, bias, rf, status, s);
+      case 64: return launch_modes<64, true>(st, mp, xf, yf, bias, rf, status, s);
+      default: return launch_modes<128, true>(st, mp, xf, yf, bias, rf, status, s);
     }
   }
   switch (st.bn) {
-    case 32: return launch_modes<32, false>(st, xf, yf, bias, rf, status, s);
-    case 64: return launch_modes<64, false>(st, xf, yf, bias, rf, status, s);
-    case 256: return launch_modes<256, false>(st, xf, yf, bias, rf, status, s);
-    default: return launch_modes<128, false>(st, xf, yf, bias, rf, status, s);
+    case 32: return launch_modes<32, false>(st, mp, xf, yf, bias, rf, status, s);
+    case 64: return launch_modes<64, false>(st, mp, xf, yf, bias, rf, status, s);
+    case 256: return launch_modes<256, false>(st, mp, xf, yf, bias, rf, status, s);
+    default: return launch_modes<128, false>(st, mp, xf, yf, bias, rf, status, s);
   }
 }
 
