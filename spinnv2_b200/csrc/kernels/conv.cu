@@ -364,7 +364,8 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   // Tensor-core path first; the CUDA-core kernel takes every shape it
   // declines (and every conv in FP32 math mode).
   if (math != SPKV2_CUDA_MATH_FP32) {
-    rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ctx->stream)
+    const void *r_dev = g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
+    rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream)
                  : conv_tc_prepare(*p, tw.data, tx.data, ty.data, ctx->stream);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;

@@ -64,7 +64,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
 
 // tcgen05 kind::i8 path (conv_tc_i8.cu) for kConvI8 / kConvI8ToI32.
-int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaStream_t s);
+int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const void *y_dev, const void *r_dev,
+                       cudaStream_t s);
 int conv_tc_i8_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
 
 }  // namespace spkv2

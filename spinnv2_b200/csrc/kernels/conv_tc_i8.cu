@@ -11,16 +11,26 @@
 //
 // GEMM view as in conv_tc.cu: rows = output pixels, columns = output
 // channels, K = (r, s, c) with c fastest; one K step = 128 int8 = 128 bytes,
-// four MMAs of K = 32.  Persistent kernel, one CTA per SM, 320 threads:
-//   warps 0-3  epilogue (TMEM lanes 32w..32w+31, double-buffered accumulator)
-//   warps 4-7  A gathers (AMODE 1): 16-byte cp.async chunks (16 channels of
-//              one tap, zero-fill for padding) straight into the operand
-//              stage.  Each thread signals step it-(STAGES-1) (its own
-//              copies landed: cp.async.wait_group, proxy fence, mbarrier
-//              arrive) BEFORE it waits for the stage of step it to free up,
-//              so the MMA never waits on that wait.
-//   warp 8     TMA producer: weight panel B, and A in AMODE 2 (1x1 stride 1).
-//   warp 9     TMEM allocation and the single-thread MMA issuer.
+// four MMAs of K = 32.  Persistent kernel, one CTA per SM, 320 threads.
+// A operand modes:
+//   AMODE 3  im2col TMA (C % 128 == 0, square kernel): one tensor-map load
+//            per K step brings 128 output pixels x 128 channels of one
+//            filter tap, padding and image edges zero-filled by the TMA unit.
+//   AMODE 2  tiled TMA (1x1, stride 1, no padding).
+//   AMODE 1  cp.async gathers by warps 4-7 (C % 16 == 0), 16 channels of one
+//            tap per 16-byte chunk, straight into the operand stage; each
+//            thread publishes step it-(STAGES-1) (wait_group, proxy fence,
+//            mbarrier arrive) before it waits for the stage of step it.
+// Warp roles: warp 8 TMA producer (weights, and A in AMODE 2/3), warp 9 TMEM
+// allocation and the single-thread MMA issuer, epilogue warps 0-3 (AMODE 1)
+// or 0-7 (AMODE 2/3: warps w and w+4 share TMEM lanes 32(w%4).. and split
+// the tile's columns).  TMEM holds two accumulator buffers, so a tile's
+// epilogue overlaps the next tile's MMAs.
+// Epilogue with dense NHWC int8 output: each warp's 32 rows x CW columns go
+// through a shared-memory tile: the residual tile (if any) is TMA-loaded
+// into it when the warp starts the tile (before it waits for the
+// accumulator), the requantised bytes overwrite it, and one TMA store writes
+// it out.  Other outputs (strided, int32) use per-thread stores.
 // Every wait is bounded; on timeout the CTA records a code in the status
 // word and winds down.
 #include <stdlib.h>
@@ -45,25 +55,41 @@ struct I8Params {
   int Kpad, Npad, num_kb, n_tiles;
   int64_t tiles;
   int out_i32;  // 1: int32 output (acc + b_q), no requantisation
+  int epi_tma;  // 1: NHWC int8 output (and residual) through TMA tiles
 };
 
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, int lo) {
+  return (uint32_t(uint8_t(sat_rne_i8(a, lo)))) | (uint32_t(uint8_t(sat_rne_i8(b, lo))) << 8) |
+         (uint32_t(uint8_t(sat_rne_i8(c, lo))) << 16) | (uint32_t(uint8_t(sat_rne_i8(d, lo))) << 24);
+}
+
+template <int AMODE>
+constexpr int epi_warps() {
+  return AMODE == 1 ? 4 : 8;
+}
+
 template <int BN, int STAGES, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_i8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap ymap, const __grid_constant__ CUtensorMap rmap,
                    const int8_t *__restrict__ x, const int32_t *__restrict__ bias_q,
                    const float *__restrict__ scale_m, const int8_t *__restrict__ res, void *__restrict__ y,
                    I8Params tp, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int EPIW = epi_warps<AMODE>();
+  constexpr int CW = BN * 4 / EPIW;  // columns (bytes) per epilogue warp
   constexpr int B_BYTES = BN * kBK;
   constexpr int STAGE = kABytes + B_BYTES;
   constexpr int kCols = 2 * BN;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
+  uint8_t *staging = smem + STAGES * STAGE;  // EPIW x (32 rows x CW bytes)
   __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
+  __shared__ uint64_t res_bar[EPIW];
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
 
@@ -72,14 +98,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&raw_bar[s], 1);     // TMA: B (and A in AMODE 2)
+      mbar_init(&raw_bar[s], 1);     // TMA: B (and A in AMODE 2/3)
       mbar_init(&full_bar[s], 128);  // A gathers landed (AMODE 1)
       mbar_init(&empty_bar[s], 1);   // MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 128);
+      mbar_init(&acce_bar[b], 32 * EPIW);
     }
+    for (int w = 0; w < EPIW; ++w) mbar_init(&res_bar[w], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -93,20 +120,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_holder;
 
-  if (warp < 4) {
+  if (warp < EPIW) {
     // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;            // TMEM lanes / tile rows 32q..32q+31
+    const int col0 = (warp >> 2) * CW;       // first tile column of this warp
     const int lo = g.act == 1 ? 0 : -128;
     const bool vec_out = g.ys[1] == 1 && (g.M % 16) == 0;
     const bool vec_res = g.has_res && g.rs[1] == 1 && (g.M % 16) == 0;
-    const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
+    uint8_t *stile = staging + warp * (32 * CW);
     int ti = 0;
     for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x, ++ti) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * kBM;
+      const int64_t row0 = m0 + quarter * 32;  // first output pixel of this warp
       const int ab = ti & 1;
+      if (tp.epi_tma) {
+        // The staging tile is free once the previous tile's store has read
+        // it; then the residual tile starts loading into it.
+        if (lane == 0) {
+          tma_store_wait_read0();
+          if (g.has_res) {
+            mbar_arrive_expect_tx(&res_bar[warp], 32 * CW);
+            tma_load_2d(stile, &rmap, n0 + col0, int(row0), &res_bar[warp]);
+          }
+        }
+        __syncwarp();
+      }
       if (!mbar_wait(&accf_bar[ab], (ti >> 1) & 1, &abort_flag, status, 4)) break;
       tc_fence_after();
-      const int64_t p = m0 + warp * 32 + lane;
+      if (tp.epi_tma && g.has_res && !mbar_wait(&res_bar[warp], ti & 1, &abort_flag, status, 6)) break;
+      const int64_t p = row0 + lane;
       const bool pv = p < g.P;
       int n = 0, oh = 0, ow = 0;
       if (pv) {
@@ -118,27 +162,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
 #pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 32) {
+      for (int cb = 0; cb < CW; cb += 32) {
         uint32_t acc[32];
-        tmem_ld32(trow + uint32_t(ab * BN + cb), acc);
-        if (cb + 32 >= BN) {
+        tmem_ld32(trow + uint32_t(ab * BN + col0 + cb), acc);
+        if (cb + 32 >= CW) {
           tc_fence_before();
           mbar_arrive(&acce_bar[ab]);
         }
-        const int c0 = n0 + cb;
-        if (c0 >= g.M || !pv) continue;
+        const int c0 = n0 + col0 + cb;
+        if (c0 >= g.M) continue;  // channel padding (warp-uniform)
         const int cn = min(32, g.M - c0);
         int32_t a[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          const int4 b = (g.has_bias && j < cn) ? __ldg(reinterpret_cast<const int4 *>(bias_q + c0 + j))
-                                                : make_int4(0, 0, 0, 0);
+          const int4 b = g.has_bias ? __ldg(reinterpret_cast<const int4 *>(bias_q + c0 + j)) : make_int4(0, 0, 0, 0);
           a[j] = int32_t(acc[j]) + b.x;
           a[j + 1] = int32_t(acc[j + 1]) + b.y;
           a[j + 2] = int32_t(acc[j + 2]) + b.z;
           a[j + 3] = int32_t(acc[j + 3]) + b.w;
         }
         if (tp.out_i32) {
+          if (!pv) continue;
           int32_t *y32 = static_cast<int32_t *>(y);
           if (cn == 32 && vec_out) {
 #pragma unroll
@@ -154,50 +198,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          const float4 m = j < cn ? __ldg(reinterpret_cast<const float4 *>(scale_m + c0 + j)) : make_float4(0, 0, 0, 0);
+          const float4 m = __ldg(reinterpret_cast<const float4 *>(scale_m + c0 + j));
           v[j] = __fmul_rn(float(a[j]), m.x);
           v[j + 1] = __fmul_rn(float(a[j + 1]), m.y);
           v[j + 2] = __fmul_rn(float(a[j + 2]), m.z);
           v[j + 3] = __fmul_rn(float(a[j + 3]), m.w);
         }
+        uint8_t *srow = stile + lane * CW + cb;  // this thread's 32 bytes of the staging tile
         if (g.has_res) {
           int8_t r[32];
-          if (cn == 32 && vec_res) {
+          if (tp.epi_tma) {
+            *reinterpret_cast<uint4 *>(r) = *reinterpret_cast<const uint4 *>(srow);
+            *reinterpret_cast<uint4 *>(r + 16) = *reinterpret_cast<const uint4 *>(srow + 16);
+          } else if (pv && cn == 32 && vec_res) {
             *reinterpret_cast<int4 *>(r) = __ldg(reinterpret_cast<const int4 *>(res + rbase + c0));
             *reinterpret_cast<int4 *>(r + 16) = __ldg(reinterpret_cast<const int4 *>(res + rbase + c0 + 16));
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = j < cn ? res[rbase + int64_t(c0 + j) * g.rs[1]] : int8_t(0);
+            for (int j = 0; j < 32; ++j) r[j] = (pv && j < cn) ? res[rbase + int64_t(c0 + j) * g.rs[1]] : int8_t(0);
           }
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __fmul_rn(float(r[j]), g.res_scale));
         }
-        int8_t *y8 = static_cast<int8_t *>(y);
-        if (cn == 32 && vec_out) {
-          uint32_t w[8];
+        uint32_t w[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            w[j] = (uint32_t(sat_rne_i8(v[4 * j], lo)) & 0xffu) | ((uint32_t(sat_rne_i8(v[4 * j + 1], lo)) & 0xffu) << 8) |
-                   ((uint32_t(sat_rne_i8(v[4 * j + 2], lo)) & 0xffu) << 16) |
-                   ((uint32_t(sat_rne_i8(v[4 * j + 3], lo)) & 0xffu) << 24);
-          *reinterpret_cast<uint4 *>(y8 + ybase + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4 *>(y8 + ybase + c0 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
+        for (int j = 0; j < 8; ++j) w[j] = pack4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3], lo);
+        if (tp.epi_tma) {
+          *reinterpret_cast<uint4 *>(srow) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4 *>(srow + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        } else if (pv) {
+          int8_t *y8 = static_cast<int8_t *>(y);
+          if (cn == 32 && vec_out) {
+            *reinterpret_cast<uint4 *>(y8 + ybase + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4 *>(y8 + ybase + c0 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+            const int8_t *bytes = reinterpret_cast<const int8_t *>(w);
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < cn) y8[ybase + int64_t(c0 + j) * g.ys[1]] = int8_t(sat_rne_i8(v[j], lo));
+            for (int j = 0; j < 32; ++j)
+              if (j < cn) y8[ybase + int64_t(c0 + j) * g.ys[1]] = bytes[j];
+          }
         }
       }
+      if (tp.epi_tma && !tp.out_i32) {
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0 && row0 < g.P && n0 + col0 < g.M) tma_store_2d(&ymap, n0 + col0, int(row0), stile);
+      }
     }
-  } else if (warp < 8) {
+    if (tp.epi_tma && lane == 0) tma_store_wait_all();
+  } else if (AMODE == 1 && warp < 8) {
     // ------------------------------------------------------------ A gathers
     if constexpr (AMODE == 1) {
       const int at = tid - 128;
       const int chunk = at & 7, rsub = at >> 3;
       uint32_t it = 0;
       bool ok = true;
-      // Step `pit`'s chunks of this thread have landed: publish them.
-      auto publish = [&](uint32_t pit) {
+      auto publish = [&](uint32_t pit) {  // this thread's chunks of step pit have landed
         fence_proxy_async();
         mbar_arrive(&full_bar[pit % STAGES]);
       };
@@ -248,12 +304,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t bytes = B_BYTES + (AMODE == 2 ? kABytes : 0);
+      const uint32_t bytes = B_BYTES + (AMODE != 1 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
         const int n0 = int(t % tp.n_tiles) * BN;
         const int64_t m0 = (t / tp.n_tiles) * kBM;
+        int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
+        if (AMODE == 3) {
+          const int ow = int(m0 % g.OW);
+          const int64_t q = m0 / g.OW;
+          bw = ow * g.sw - g.pw;
+          bh = int(q % g.OH) * g.sh - g.ph;
+          bn = int(q / g.OH);
+        }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 2);
@@ -262,10 +326,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&raw_bar[s], bytes);
           tma_load_2d(a_st + kABytes, &wmap, kb * kBK, n0, &raw_bar[s]);
           if (AMODE == 2) tma_load_2d(a_st, &amap, kb * kBK, int(m0), &raw_bar[s]);
+          if (AMODE == 3) {
+            const int k0 = kb * kBK;
+            const int tap = k0 / g.C, c0 = k0 - tap * g.C;  // C % 128 == 0: one tap per K step
+            const int r = tap / g.KW, sx = tap - r * g.KW;
+            tma_load_im2col_4d(a_st, &amap, c0, bw, bh, bn, uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+          }
         }
       }
     }
-  } else {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc =
@@ -330,44 +400,65 @@ __global__ void pack_i8_kernel(int8_t *__restrict__ dst, const int8_t *__restric
 }
 
 constexpr int stages_of(int bn) { return bn == 256 ? 4 : bn == 128 ? 6 : 8; }
+constexpr size_t smem_of(int bn) { return size_t(stages_of(bn)) * (kABytes + bn * kBK) + size_t(128) * bn + 1024; }
 
 struct I8State {
-  CUtensorMap wmap, amap;
+  CUtensorMap wmap, amap, ymap, rmap;
   I8Params tp;
   int bn = 128, amode = 1, grid = 148;
   size_t smem = 0;
   bool set_attr_only = false;
-  mutable const void *amap_base = nullptr;  // activation pointer the A map was encoded for
+  const void *x_base = nullptr, *y_base = nullptr, *r_base = nullptr;  // pointers the maps were encoded for
 };
+
+int epi_cols(const I8State &st) { return st.bn * 4 / (st.amode == 1 ? 4 : 8); }
 
 bool encode_a(const I8State &st, CUtensorMap *map, const void *x) {
   const ConvGeo &g = st.tp.g;
+  if (st.amode == 3)
+    return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
+                              kBK, kBM);
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
 }
 
+bool encode_rows(const I8State &st, CUtensorMap *map, const void *base) {
+  const ConvGeo &g = st.tp.g;
+  return encode_2d_box(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, uint64_t(g.M), uint64_t(g.P), uint64_t(g.M),
+                       uint32_t(epi_cols(st)), 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+struct Maps {
+  CUtensorMap a, y, r;
+};
+
 template <int BN, int AMODE>
-int launch_cfg(const I8State &st, const CUtensorMap &amap, const ConvPlan &p, const void *x, void *y, const void *res,
+int launch_cfg(const I8State &st, const Maps &mp, const ConvPlan &p, const void *x, void *y, const void *res,
                int *status, cudaStream_t s) {
   auto kern = conv_i8_kernel<BN, stages_of(BN), AMODE>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, amap, static_cast<const int8_t *>(x), p.bias_q,
-                                                    p.scale_m, static_cast<const int8_t *>(res), y, st.tp, status);
+  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, static_cast<const int8_t *>(x),
+                                                    p.bias_q, p.scale_m, static_cast<const int8_t *>(res), y, st.tp,
+                                                    status);
   return cuda_status(cudaGetLastError());
 }
 
 template <int BN>
-int launch_bn(const I8State &st, const CUtensorMap &amap, const ConvPlan &p, const void *x, void *y, const void *res,
+int launch_bn(const I8State &st, const Maps &mp, const ConvPlan &p, const void *x, void *y, const void *res,
               int *status, cudaStream_t s) {
-  return st.amode == 2 ? launch_cfg<BN, 2>(st, amap, p, x, y, res, status, s)
-                       : launch_cfg<BN, 1>(st, amap, p, x, y, res, status, s);
+  switch (st.amode) {
+    case 3: return launch_cfg<BN, 3>(st, mp, p, x, y, res, status, s);
+    case 2: return launch_cfg<BN, 2>(st, mp, p, x, y, res, status, s);
+    default: return launch_cfg<BN, 1>(st, mp, p, x, y, res, status, s);
+  }
 }
 
 }  // namespace
 
 // Eligible: int8 x / w, group 1, dense NHWC input with C % 16 == 0, 16-byte
 // aligned activations, Cout >= 16.
-int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaStream_t s) {
+int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const void *y_dev, const void *r_dev,
+                       cudaStream_t s) {
   const ConvGeo &g = p.g;
   if ((p.mode != kConvI8 && p.mode != kConvI8ToI32) || g.groups != 1 || g.M < 16) return SPKV2_ERR_UNSUPPORTED;
   const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
@@ -376,13 +467,23 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaSt
   I8State *st = new I8State();
   memset(&st->wmap, 0, sizeof(st->wmap));
   memset(&st->amap, 0, sizeof(st->amap));
+  memset(&st->ymap, 0, sizeof(st->ymap));
+  memset(&st->rmap, 0, sizeof(st->rmap));
+  const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
+  if (g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
+    st->amode = 2;
+  else if (square && g.C % kBK == 0 && encode_im2col_fn())
+    st->amode = 3;
+  else
+    st->amode = 1;
   int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : g.M <= 128 ? 128 : 256;
   if (const char *e = getenv("SPKV2_TC_BN")) {
     const int v = atoi(e);
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
   }
+  if (st->amode == 1 && bn == 256) bn = 128;  // 4 epilogue warps: at most 128 columns each
+  if (st->amode != 1 && bn == 32) bn = 64;    // 8 epilogue warps: at least 32 columns each
   st->bn = bn;
-  st->amode = (g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0) ? 2 : 1;
   I8Params &tp = st->tp;
   tp.g = g;
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);
@@ -391,6 +492,12 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaSt
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
   tp.out_i32 = p.mode == kConvI8ToI32 ? 1 : 0;
+  const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
+  const bool nhwc_res = !g.has_res || (g.rs[1] == 1 && g.rs[3] == g.M && g.rs[2] == int64_t(g.OW) * g.M);
+  tp.epi_tma = (!tp.out_i32 && nhwc_out && nhwc_res && g.M % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(y_dev) % 16 == 0 && reinterpret_cast<uintptr_t>(r_dev) % 16 == 0)
+                   ? 1
+                   : 0;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   st->grid = int(std::min<int64_t>(tp.tiles, sms));
@@ -404,16 +511,18 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaSt
   int rc = cuda_status(cudaGetLastError());
   bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, wp, uint64_t(tp.Kpad),
                                  uint64_t(tp.Npad), uint64_t(tp.Kpad), uint32_t(bn));
-  if (ok && st->amode == 2) {
-    ok = encode_a(*st, &st->amap, x_dev);
-    st->amap_base = x_dev;
-  }
+  if (ok && st->amode != 1) ok = encode_a(*st, &st->amap, x_dev);
+  if (ok && tp.epi_tma) ok = encode_rows(*st, &st->ymap, y_dev);
+  if (ok && tp.epi_tma && g.has_res) ok = encode_rows(*st, &st->rmap, r_dev);
+  st->x_base = x_dev;
+  st->y_base = y_dev;
+  st->r_base = r_dev;
   if (!ok) {
     device_free(wp);
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  st->smem = size_t(stages_of(bn)) * (kABytes + bn * kBK) + 1024;
+  st->smem = smem_of(bn);
   p.w_tc = wp;
   p.tc_state = st;
   p.tc_i8 = true;
@@ -423,7 +532,8 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, cudaSt
   rc = conv_tc_i8_launch(p, nullptr, nullptr, nullptr, nullptr, s);
   st->set_attr_only = false;
   if (rc) return rc;
-  p.variant = std::string("tc_int8_bn") + std::to_string(bn) + (st->amode == 2 ? "_tma" : "_cpasync") +
+  static const char *amodes[] = {"", "_cpasync", "_tma", "_im2col"};
+  p.variant = std::string("tc_int8_bn") + std::to_string(bn) + amodes[st->amode] + (tp.epi_tma ? "_tmastore" : "") +
               (tp.out_i32 ? "_i32out" : "");
   return 0;
 }
@@ -432,16 +542,19 @@ void conv_tc_i8_release(void *state) { delete static_cast<I8State *>(state); }
 
 int conv_tc_i8_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s) {
   const I8State &st = *static_cast<const I8State *>(p.tc_state);
-  CUtensorMap amap = st.amap;
-  if (st.amode == 2 && !st.set_attr_only && x != st.amap_base) {
-    // The input was rebound to another device buffer since prepare.
-    if (!encode_a(st, &amap, x)) return SPKV2_ERR_UNSUPPORTED;
+  // Tensor maps follow the tensors: one rebound to another device buffer
+  // since prepare gets a freshly encoded map.
+  Maps mp{st.amap, st.ymap, st.rmap};
+  if (!st.set_attr_only) {
+    if (st.amode != 1 && x != st.x_base && !encode_a(st, &mp.a, x)) return SPKV2_ERR_UNSUPPORTED;
+    if (st.tp.epi_tma && y != st.y_base && !encode_rows(st, &mp.y, y)) return SPKV2_ERR_UNSUPPORTED;
+    if (st.tp.epi_tma && p.g.has_res && res != st.r_base && !encode_rows(st, &mp.r, res)) return SPKV2_ERR_UNSUPPORTED;
   }
   switch (st.bn) {
-    case 32: return launch_bn<32>(st, amap, p, x, y, res, status, s);
-    case 64: return launch_bn<64>(st, amap, p, x, y, res, status, s);
-    case 128: return launch_bn<128>(st, amap, p, x, y, res, status, s);
-    default: return launch_bn<256>(st, amap, p, x, y, res, status, s);
+    case 32: return launch_bn<32>(st, mp, p, x, y, res, status, s);
+    case 64: return launch_bn<64>(st, mp, p, x, y, res, status, s);
+    case 128: return launch_bn<128>(st, mp, p, x, y, res, status, s);
+    default: return launch_bn<256>(st, mp, p, x, y, res, status, s);
   }
 }
 

@@ -135,6 +135,38 @@ __global__ void maxpool_nhwc4_kernel(float *__restrict__ y, const float *__restr
   }
 }
 
+// Both tensors NHWC int8, C % 16 == 0: 16 channels (one 16-byte load) per
+// thread, per-byte signed max on 32-bit words; an empty window gives -128.
+__global__ void maxpool_nhwc16_i8_kernel(int8_t *__restrict__ y, const int8_t *__restrict__ x, Geo g,
+                                         int64_t total16) {
+  const int C16 = g.C / 16;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total16; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c16 = int(r % C16);
+    r /= C16;
+    const int ow = int(r % g.OW);
+    r /= g.OW;
+    const int oh = int(r % g.OH);
+    const int n = int(r / g.OH);
+    uint4 best = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+    const int8_t *xb = x + int64_t(n) * g.H * g.W * g.C + c16 * 16;
+    for (int rr = 0; rr < g.kh; ++rr) {
+      const int ih = oh * g.sh + rr - g.ph;
+      if (ih < 0 || ih >= g.H) continue;
+      for (int s = 0; s < g.kw; ++s) {
+        const int iw = ow * g.sw + s - g.pw;
+        if (iw < 0 || iw >= g.W) continue;
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xb + (int64_t(ih) * g.W + iw) * g.C));
+        best.x = __vmaxs4(best.x, v.x);
+        best.y = __vmaxs4(best.y, v.y);
+        best.z = __vmaxs4(best.z, v.z);
+        best.w = __vmaxs4(best.w, v.w);
+      }
+    }
+    reinterpret_cast<uint4 *>(y)[i] = best;
+  }
+}
+
 void strides_of(const TensorState &t, int64_t s[4]) {
   View v = make_view(t);
   for (int i = 0; i < 4; ++i) s[i] = v.stride[i];
@@ -252,7 +284,10 @@ int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   p->out_nhwc = ty.layout == kNHWC;
   p->is_int8 = is_int8;
   p->vec = (!is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 4 == 0) ? 4 : 1;
-  p->variant = p->vec == 4 ? "maxpool_nhwc_vec4" : "pool_generic";
+  if (is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(tx.data) % 16 == 0 && reinterpret_cast<uintptr_t>(ty.data) % 16 == 0)
+    p->vec = 16;
+  p->variant = p->vec == 4 ? "maxpool_nhwc_vec4" : p->vec == 16 ? "maxpool_nhwc_i8_vec16" : "pool_generic";
   set_node_plan(ctx, node, p);
   return 0;
 }
@@ -266,9 +301,14 @@ int pool_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   if (total == 0) return 0;
   void *y = ctx->tensors[node->outputs[0]].data;
   const void *x = ctx->tensors[node->inputs[0]].data;
-  if (p->vec == 4) {
+  // Vector paths need 16-byte aligned tensors (a rebinding may move them).
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0;
+  if (p->vec == 4 && aligned) {
     maxpool_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
         static_cast<float *>(y), static_cast<const float *>(x), g, total / 4);
+  } else if (p->vec == 16 && aligned) {
+    maxpool_nhwc16_i8_kernel<<<grid_for(total / 16, 256), 256, 0, ctx->stream>>>(
+        static_cast<int8_t *>(y), static_cast<const int8_t *>(x), g, total / 16);
   } else if (p->is_int8) {
     pool_kernel<int8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
         static_cast<int8_t *>(y), static_cast<const int8_t *>(x), g, p->kind, p->out_nhwc, total);

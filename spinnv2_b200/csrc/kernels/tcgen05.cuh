@@ -68,6 +68,20 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+// im2col load of a 4-D NHWC tensor map: `pixels x channels` box starting at
+// base position {c, w, h, n}, shifted by the filter tap {w_off, h_off}.
+__device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap *map, int c, int w, int h, int n,
+                                                   uint16_t w_off, uint16_t h_off, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(w_off),
+      "h"(h_off)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -177,6 +191,50 @@ inline bool encode_2d(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem
   return encode_fn()(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D tensor map with an explicit box and swizzle mode (inner box in
+// elements).
+inline bool encode_2d_box(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
+                          uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_inner, uint32_t box_rows,
+                          CUtensorMapSwizzle swizzle) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch * elem_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  }
+  return fn;
+}
+
+// im2col map of a dense NHWC tensor [N][H][W][C] for a square conv (kernel k,
+// stride s, pad p, dilation d): the bounding box of filter-window origins
+// runs from -p to (dim - 1) + p - (k - 1) * d in W and H, traversed with
+// step s; 128-byte rows of `channels` elements, 128-byte swizzle.
+inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
+                               int N, int H, int W, int C, int k, int s, int p, int d, uint32_t channels,
+                               uint32_t pixels) {
+  if (!encode_im2col_fn()) return false;
+  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+  const cuuint64_t strides[3] = {cuuint64_t(C) * elem_bytes, cuuint64_t(W) * C * elem_bytes,
+                                 cuuint64_t(H) * W * C * elem_bytes};
+  const int lower[2] = {-p, -p};
+  const int upper[2] = {p - (k - 1) * d, p - (k - 1) * d};
+  const cuuint32_t estr[4] = {1, cuuint32_t(s), cuuint32_t(s), 1};
+  return encode_im2col_fn()(map, dtype, 4, const_cast<void *>(base), dims, strides, lower, upper, channels, pixels,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace tc

@@ -127,6 +127,8 @@ CASES = {
     "1x1_48_40_noact": (2, 48, 9, 40, 1, 1, 0, False, None),
     "1x1s2_64_128": (2, 64, 14, 128, 1, 2, 0, False, "Relu"),
     "7x7s2_16_32": (1, 16, 23, 32, 7, 2, 3, False, "Relu"),
+    "3x3s1_256_res": (2, 256, 14, 256, 3, 1, 1, True, "Relu"),
+    "5x5s1p2_128_96": (2, 128, 11, 96, 5, 1, 2, False, None),
 }
 
 
@@ -156,13 +158,17 @@ def _int8_conv_graph(case: str, out_i32: bool = False):
     if act and not out_i32:
         attrs["fused_activation"] = act
     y = b.op("Conv", ins, [n, m, oh, oh], attrs, out_dtype=DTYPE_INT32 if out_i32 else DTYPE_INT8)
-    b.mark_output(y)
+    out = y
+    if not out_i32:  # keep the conv output internal (NHWC), as inside a network
+        out = b.op("MaxPool", [y], [n, m, oh, oh], pool, out_dtype=DTYPE_INT8)
+    b.mark_output(out)
     g = b.graph
     sx = 0.05
     q = [QuantParam(x0, "per_tensor", 0, 1, [sx], [0]), QuantParam(x, "per_tensor", 0, 1, [sx], [0]),
          QuantParam(w, "per_channel", 0, m, (rng.random(m) * 4e-3 + 1e-4).astype(np.float32).tolist(), [0] * m)]
     if not out_i32:
-        q.append(QuantParam(y, "per_tensor", 0, 1, [float(np.float32(2.0 + rng.random()))], [0]))
+        sy = float(np.float32(2.0 + rng.random()))
+        q += [QuantParam(y, "per_tensor", 0, 1, [sy], [0]), QuantParam(out, "per_tensor", 0, 1, [sy], [0])]
     if len(ins) > 3:
         q += [QuantParam(g.inputs[1], "per_tensor", 0, 1, [0.03], [0]), QuantParam(ins[3], "per_tensor", 0, 1, [0.03], [0])]
     return g, q, inputs
@@ -222,12 +228,18 @@ def test_int8_conv_bit_exact(gpu, case):
     with Runtime(spk, device=0) as rt:
         out = rt.run(*inputs)[0]
         variant = rt.node_variant(next(n.id for n in rt.package.nodes if n.op_type == "Conv"))
-    assert variant.startswith("tc_int8"), variant
+    assert variant.startswith("tc_int8") and "tmastore" in variant, variant
+    k, s, c = CASES[case][4], CASES[case][5], CASES[case][1]
+    if k == 1 and s == 1:
+        assert "_tma" in variant, variant
+    elif c % 128 == 0:
+        assert "_im2col" in variant, variant
     np.testing.assert_array_equal(out, ref)
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", ["3x3s1_64_res_relu", "1x1_256_1024_res", "1x1_48_40_noact", "7x7s2_16_32"])
+@pytest.mark.parametrize("case", ["3x3s1_64_res_relu", "1x1_256_1024_res", "1x1_48_40_noact", "7x7s2_16_32",
+                                  "3x3s2_128_256_relu", "5x5s1p2_128_96"])
 def test_int8_conv_int32_accumulators_bit_exact(gpu, case):
     from spinnv2_b200.runtime import Runtime
 
@@ -254,8 +266,13 @@ def test_int8_resnet50_bs2_every_node_against_the_oracle(gpu, r50_int8):
     x = seeded_input((2, 3, 224, 224))
     with Runtime(r50_int8, device=0) as rt:
         probs = rt.run(x)[0]
-        gpu = {t.id: rt.read_tensor(t.id) for t in pkg.tensors if t.role_name in ("activation", "output")
-               and t.size_bytes > 0}
+        # The memory plan reuses activation buffers, so read each node's
+        # outputs right after that node runs (node by node, same inputs).
+        gpu = {}
+        for n in pkg.nodes:
+            rt.run_nodes(n.id, n.id + 1)
+            for t in n.outputs:
+                gpu[t] = rt.read_tensor(t)
         variants = {n.id: rt.node_variant(n.id) for n in pkg.nodes}
     gpu[pkg.inputs[0].id] = x
     convs = [n for n in pkg.nodes if n.op_type == "Conv"]
