@@ -242,6 +242,11 @@ class Runtime:
         self._check(self.lib.spkv2_cuda_synchronize(self.ctx), "synchronize")
 
     def run_nodes(self, first: int, last: int) -> None:
+        """Run nodes [first, last) eagerly on the current tensor contents.
+
+        Inputs are not staged: the memory plan may reuse a graph input's
+        buffer after its last reader, so call set_input() again before
+        re-running nodes that read an input."""
         self._check(self.lib.spkv2_cuda_run_nodes(self.ctx, first, last), "run nodes")
 
     # -------------------------------------------------------------- introspection
