@@ -7,28 +7,31 @@
 // fly (implicit im2col), B = packed weights [Cout_pad][K_pad] K-major.
 //
 // Persistent kernel: one CTA per SM walks output tiles (128 pixels x BN
-// channels) in a static round-robin.  Warp roles (320 threads):
-//   warps 0-3  epilogue: TMEM lanes 32w..32w+31 (= tile rows of warp w) ->
-//              registers -> bias, residual, Relu/SiLU -> TMA store staged
-//              through shared memory (NHWC outputs) or direct stores.  TMEM
-//              holds two accumulator buffers, so the epilogue overlaps the
-//              next tile's mainloop.
-//   warps 4-7  A operand.  AMODE 2 (1x1, stride 1, C % 32 == 0): the A tile
-//              arrives by TMA (issued by warp 8) straight into the operand
-//              stage and, for 3xTF32, is split there in place.  AMODE 1 (any
-//              other conv): each thread gathers its 16-byte chunks with
-//              cp.async (zero-fill for padding) into a landing ring of LAND
-//              slots, LAND-1 K steps ahead of the MMA, and later converts ITS
-//              OWN chunks into the operand stage, so a per-thread
-//              cp.async.wait_group is the only synchronisation the landing
-//              needs and a slow MMA never stalls the gathers.
-//              Conversion: TF32 hi = round-to-nearest, lo = x - hi (3xTF32),
-//              in the 128B-swizzled K-major layout the MMA descriptors
-//              describe.
-//   warp 8     TMA producer (one thread): weight panels (hi, and lo for
-//              3xTF32), and the A tile in AMODE 2.  No multicast.
-//   warp 9     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
-//              K=8) and commits stage releases and finished accumulators.
+// channels) in a static round-robin.  Warp roles (448 threads):
+//   warps 0-7   epilogue: warps w and w+4 read TMEM lanes 32(w%4).. (tile
+//               rows) and split the tile's columns -> registers -> bias,
+//               residual (prefetched into L2 when the tile starts), Relu /
+//               SiLU -> TMA store staged through shared memory (NHWC
+//               outputs) or direct stores.  TMEM holds two accumulator
+//               buffers, so the epilogue overlaps the next tile's mainloop.
+//   warps 8-11  A operand.  AMODE 2 (1x1, stride 1, C % 32 == 0): the tile
+//               arrives by a tiled TMA load; AMODE 3 (other square convs,
+//               C % 32 == 0): by an im2col TMA load (128 output pixels x 32
+//               channels of one filter tap, padding zero-filled by the TMA
+//               unit).  Both land straight in the operand stage, where these
+//               warps round it to TF32 (3xTF32: split it) in place.  AMODE 1
+//               (any other conv): each thread gathers its 16-byte chunks with
+//               cp.async (zero-fill for padding) into a landing ring of LAND
+//               slots, LAND-1 K steps ahead of the MMA, and later converts
+//               ITS OWN chunks into the operand stage, so a per-thread
+//               cp.async.wait_group is the only synchronisation the landing
+//               needs.  Conversion: TF32 hi = round-to-nearest, lo = x - hi
+//               (3xTF32), in the 128B-swizzled K-major layout the MMA
+//               descriptors describe.
+//   warp 12     TMA producer (one thread): weight panels (hi, and lo for
+//               3xTF32), and the A tile in AMODE 2/3.  No multicast.
+//   warp 13     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
+//               K=8) and commits stage releases and finished accumulators.
 // 3xTF32: acc += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (three MMAs per K step).
 // The tensor core's fp32 accumulation truncates, which over long K chains
 // biases the sum (the error grows linearly with K).  In 3xTF32 mode each
@@ -58,8 +61,9 @@ using namespace tc;
 constexpr int kBM = 128;          // tile rows (pixels) = UMMA M
 constexpr int kBK = 32;           // fp32 elements per K step = 128 bytes
 constexpr int kABytes = kBM * 128;
-constexpr int kThreads = 320;
-constexpr int kStagingBytes = 4 * 2 * 4096;  // epilogue: 4 warps x 2 buffers x 32x32 fp32
+constexpr int kThreads = 448;               // 8 epilogue + 4 A-operand + TMA + MMA warps
+constexpr int kEpiWarps = 8;
+constexpr int kStagingBytes = kEpiWarps * 4096;  // epilogue: one 32x32 fp32 tile per warp
 
 // ---------------------------------------------------------------- kernel
 struct TcParams {
@@ -116,10 +120,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
   constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
-  // always for gathers, and for TMA-loaded tiles when they must be split.
-  // A TF32 TMA tile goes to the tensor core as loaded (the hardware ignores
-  // the low 13 mantissa bits).
-  constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
+  // always for gathers and im2col tiles (TF32 rounding to nearest), and for
+  // 1x1 TMA tiles when they must be split.  A TF32 1x1 TMA tile goes to the
+  // tensor core as loaded (the hardware ignores the low 13 mantissa bits).
+  constexpr bool CONVERT = (AMODE != 2) || SPLIT3;
   // TMEM: two accumulator buffers (MMA / epilogue overlap) + the promoted
   // sums for 3xTF32, rounded up to a power of two >= 32 columns.
   constexpr int kCols = (SPLIT3 ? 3 : 2) * BN;
@@ -142,12 +146,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 128);
+      mbar_init(&acce_bar[b], 32 * kEpiWarps);
     }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {
+  if (warp == 13) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_holder)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -157,18 +161,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_holder;
 
-  if (warp < 4) {
+  if (warp < kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    uint8_t *stage_buf = staging + warp * 8192;
+    // Warps w and w+4 read TMEM lanes 32(w%4).. (tile rows) and split the
+    // tile's columns; with BN = 32 warps 4-7 only hand the buffers back.
+    const int quarter = warp & 3;
+    const int ncol = BN >= 64 ? BN / 2 : (warp < 4 ? BN : 0);
+    const int col0 = BN >= 64 ? (warp >> 2) * (BN / 2) : 0;
+    uint8_t *stage_buf = staging + warp * 4096;
     const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
     uint32_t sc = 0;  // TMA-store chunks issued by this warp
     uint32_t gi = 0;  // accumulator hand-offs consumed (one per K group)
     const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
-    const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);  // this warp's TMEM lanes
-    const uint32_t tsum = trow + uint32_t(2 * BN);               // promoted sums (3xTF32)
+    const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
+    const uint32_t tsum = trow + uint32_t(2 * BN);                  // promoted sums (3xTF32)
     for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * kBM;
+      const int row = quarter * 32 + lane;
+      const int64_t p = m0 + row;
+      const bool pv = p < g.P;
+      int n = 0, oh = 0, ow = 0;
+      if (pv) {
+        ow = int(p % g.OW);
+        const int64_t q = p / g.OW;
+        oh = int(q % g.OH);
+        n = int(q / g.OH);
+      }
+      const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
+      const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
+      if (g.has_res && pv && rvec) {
+        // Pull this row's residual into L2 while the MMAs run.
+        for (int j = 0; j < ncol && n0 + col0 + j < g.M; j += 32)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(res + rbase + n0 + col0 + j));
+      }
       // All K groups but the last: add the group's partial into the sums
       // (round-to-nearest fp32 adds) and hand the partial buffer back.
       bool failed = false;
@@ -180,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int cb = 0; cb < BN; cb += 32) {
+        for (int cb = col0; cb < col0 + ncol; cb += 32) {
           uint32_t part[32];
           tmem_ld32(trow + uint32_t(pb * BN + cb), part);
           if (gidx > 0) {
@@ -199,18 +225,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ab = gi & 1;
       if (!mbar_wait(&accf_bar[ab], (gi >> 1) & 1, &abort_flag, status, 4)) break;
       tc_fence_after();
-      const int row = warp * 32 + lane;
-      const int64_t p = m0 + row;
-      const bool pv = p < g.P;
-      int n = 0, oh = 0, ow = 0;
-      if (pv) {
-        ow = int(p % g.OW);
-        const int64_t q = p / g.OW;
-        oh = int(q % g.OH);
-        n = int(q / g.OH);
-      }
-      const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
-      const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
       // Bias, residual, activation and store of accumulator columns
       // cb..cb+31 of this thread's row.
       auto store_chunk = [&](int cb, const uint32_t(&acc)[32]) {
@@ -266,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           return;
         }
         if (EPI_TMA) {
-          uint8_t *buf = stage_buf + (sc & 1) * 4096;
-          if (sc >= 2 && lane == 0) tma_store_wait_read1();  // previous store from this buffer has read it
+          uint8_t *buf = stage_buf;
+          if (sc >= 1 && lane == 0) tma_store_wait_read0();  // the previous store has read the tile
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -275,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2], vals[4 * j + 3]);
           fence_proxy_async();
           __syncwarp();
-          if (lane == 0 && m0 + warp * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + warp * 32), buf);
+          if (lane == 0 && m0 + quarter * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + quarter * 32), buf);
           ++sc;
         } else if (pv) {
           if (cn == 32 && g.ys[1] == 1 && (g.M % 4) == 0) {
@@ -291,8 +305,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       // Last K group: partial (+ sums) -> bias/residual/activation -> store.
+      if (ncol == 0) {
+        tc_fence_before();
+        mbar_arrive(&acce_bar[ab]);
+        ++gi;
+      }
 #pragma unroll 1
-      for (int cb = 0; cb < BN; cb += 32) {
+      for (int cb = col0; cb < col0 + ncol; cb += 32) {
         uint32_t acc[32];
         tmem_ld32(trow + uint32_t(ab * BN + cb), acc);
         if (ngroups > 1) {
@@ -301,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(sum[j]));
         }
-        if (cb + 32 >= BN) {
-          // All of this tile's accumulator has been read: hand the buffer back.
+        if (cb + 32 >= col0 + ncol) {
+          // All of this warp's accumulator columns are read: hand the buffer back.
           tc_fence_before();
           mbar_arrive(&acce_bar[ab]);
           ++gi;
@@ -311,13 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (EPI_TMA && lane == 0) tma_store_wait_all();
-  } else if (warp < 8) {
+  } else if (warp < kEpiWarps + 4) {
     // ------------------------------------------------------------ A operand
-    const int at = tid - 128;
+    const int at = tid - 32 * kEpiWarps;
     uint32_t it = 0;  // global K-step counter
     bool ok = true;
-    if constexpr (AMODE == 2) {
-      if (CONVERT) {  // 3xTF32: split the TMA-landed tile in place
+    if constexpr (AMODE != 1) {
+      if (CONVERT) {  // round (and for 3xTF32 split) the TMA-landed tile in place
         for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
           for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
@@ -388,15 +407,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t pit = first; pit < it && ok; ++pit) ok = finish(pit);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == kEpiWarps + 4) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE == 2 ? kABytes : 0);
+      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE != 1 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
         const int n0 = int(t % tp.n_tiles) * BN;
         const int64_t m0 = (t / tp.n_tiles) * kBM;
+        int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
+        if (AMODE == 3) {
+          const int ow = int(m0 % g.OW);
+          const int64_t q = m0 / g.OW;
+          bw = ow * g.sw - g.pw;
+          bh = int(q % g.OH) * g.sh - g.ph;
+          bn = int(q / g.OH);
+        }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 2);
@@ -407,6 +434,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
           if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
           if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
+          if (AMODE == 3) {
+            const int k0 = kb * kBK;
+            const int tap = k0 / g.C, c0 = k0 - tap * g.C;  // C % 32 == 0: one tap per K step
+            const int r = tap / g.KW, sx = tap - r * g.KW;
+            tma_load_im2col_4d(a_hi, &amap, c0, bw, bh, bn, uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+          }
         }
       }
     }
@@ -436,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // B (and, in AMODE 2, A) lands by TMA on raw_bar; a converted A
           // tile is signalled on full_bar (in AMODE 2 only after the A warps
           // saw raw_bar themselves).
-          ok = (AMODE == 2 && CONVERT) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
+          ok = (AMODE != 1 && CONVERT) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
           if (ok && CONVERT) ok = mbar_wait(&full_bar[s], ph, &abort_flag, status, 3);
           if (!ok) break;
           tc_fence_after();
@@ -477,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -534,7 +567,7 @@ struct PipeShape {
   int stages, land;
 };
 constexpr PipeShape pipe_shape(int bn, bool split3, int amode) {
-  return amode == 2 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
+  return amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
                               : PipeShape{bn == 256 ? 4 : 6, 0})
                     : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
                               : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
@@ -564,6 +597,9 @@ struct TcState {
 
 bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
   const ConvGeo &g = st.tp.g;
+  if (st.amode == 3)
+    return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
+                              kBK, kBM);
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
 }
 
@@ -590,11 +626,18 @@ int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, cons
 template <int BN, bool SPLIT3>
 int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
                  int *status, cudaStream_t s) {
-  if (st.epi_tma)
-    return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, status, s)
-                         : launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, status, s);
-  return st.amode == 2 ? launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, status, s)
-                       : launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, status, s);
+  if (st.epi_tma) {
+    switch (st.amode) {
+      case 3: return launch_cfg<BN, SPLIT3, 3, true>(st, mp, x, y, bias, res, status, s);
+      case 2: return launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, status, s);
+      default: return launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, status, s);
+    }
+  }
+  switch (st.amode) {
+    case 3: return launch_cfg<BN, SPLIT3, 3, false>(st, mp, x, y, bias, res, status, s);
+    case 2: return launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, status, s);
+    default: return launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, status, s);
+  }
 }
 
 }  // namespace
@@ -632,7 +675,15 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     p.launches = 2;
   }
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
-  st->amode = (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0) ? 2 : 1;
+  // A operand: tiled TMA for 1x1 stride-1 convs, im2col TMA for other
+  // square convs with C % 32 == 0, cp.async gathers otherwise.
+  const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
+  if (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
+    st->amode = 2;
+  else if (g.C % 32 == 0 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
+    st->amode = 3;
+  else
+    st->amode = 1;
   // Tile width: the smallest that covers Cout up to 128; 256 for wide TF32
   // layers.  3xTF32 keeps 128: two partial buffers plus the promoted sums
   // take 3 x BN TMEM columns, and TMEM has 512.
@@ -675,7 +726,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   int rc = cuda_status(cudaGetLastError());
   bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad),
                                  uint32_t(bn));
-  if (ok && st->amode == 2) ok = encode_a(*st, &st->amap, x_dev);
+  if (ok && st->amode != 1) ok = encode_a(*st, &st->amap, x_dev);
   if (ok && st->epi_tma) ok = encode_y(*st, &st->ymap, y_dev);
   st->amap_base = x_dev;
   st->ymap_base = y_dev;
@@ -694,7 +745,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   st->set_attr_only = false;
   if (rc) return rc;
   p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) +
-              (st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
+              (st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
               (st->staged_x ? "_relayout" : "");
   return 0;
 }
@@ -725,7 +776,7 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   // another device buffer since prepare gets freshly encoded maps.
   Maps mp{st.amap, st.ymap};
   if (!st.set_attr_only) {
-    if (st.amode == 2 && !st.staged_x && xf != st.amap_base && !encode_a(st, &mp.a, xf)) return SPKV2_ERR_UNSUPPORTED;
+    if (st.amode != 1 && !st.staged_x && xf != st.amap_base && !encode_a(st, &mp.a, xf)) return SPKV2_ERR_UNSUPPORTED;
     if (st.epi_tma && yf != st.ymap_base && !encode_y(st, &mp.y, yf)) return SPKV2_ERR_UNSUPPORTED;
   }
   if (st.split3) {
