@@ -18,16 +18,19 @@
 //               arrives by a tiled TMA load; AMODE 3 (other square convs,
 //               C % 32 == 0): by an im2col TMA load (128 output pixels x 32
 //               channels of one filter tap, padding zero-filled by the TMA
-//               unit).  Both land straight in the operand stage, where these
-//               warps round it to TF32 (3xTF32: split it) in place.  AMODE 1
-//               (any other conv): each thread gathers its 16-byte chunks with
-//               cp.async (zero-fill for padding) into a landing ring of LAND
-//               slots, LAND-1 K steps ahead of the MMA, and later converts
-//               ITS OWN chunks into the operand stage, so a per-thread
-//               cp.async.wait_group is the only synchronisation the landing
-//               needs.  Conversion: TF32 hi = round-to-nearest, lo = x - hi
-//               (3xTF32), in the 128B-swizzled K-major layout the MMA
-//               descriptors describe.
+//               unit); AMODE 4 (4-channel inputs): eight 16-byte im2col
+//               columns per K step in an unswizzled core-matrix layout.  The
+//               tile lands straight in the operand stage; for 3xTF32 these
+//               warps add its low part.  AMODE 1 (any other conv): each
+//               thread gathers its 16-byte chunks with cp.async (zero-fill
+//               for padding) into a landing ring of LAND slots, LAND-1 K
+//               steps ahead of the MMA, and later copies ITS OWN chunks into
+//               the operand stage, so a per-thread cp.async.wait_group is the
+//               only synchronisation the landing needs.
+//               TF32 split: the tensor core reads fp32 operands as TF32 by
+//               dropping the low 13 mantissa bits, so the raw tile is the
+//               high part and lo = x - trunc_tf32(x) is exact in fp32 (half
+//               the shared-memory traffic of writing a rounded high part).
 //   warp 12     TMA producer (one thread): weight panels (hi, and lo for
 //               3xTF32), and the A tile in AMODE 2/3.  No multicast.
 //   warp 13     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
@@ -89,23 +92,27 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Converts thread t's chunks of an fp32 A tile at `src` into TF32 hi (and lo)
-// at dst_hi / dst_lo; src may equal dst_hi (in place).
+// The tensor core reads an fp32 operand of kind::tf32 as TF32 by dropping
+// the low 13 mantissa bits.  So a raw fp32 tile is its own high part, and the
+// 3xTF32 low part is lo = x - trunc_tf32(x), exact in fp32.  Thread t handles
+// its chunks of the tile at `src`: copies them to dst_hi unless src == dst_hi,
+// and for 3xTF32 writes the low parts to dst_lo.
 template <bool SPLIT3>
 __device__ __forceinline__ void convert_tile(const uint8_t *src, uint8_t *dst_hi, uint8_t *dst_lo, int t) {
   const int chunk = t & 7, rsub = t >> 3;
+  const bool copy = src != dst_hi;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t off = swz_off(i * 16 + rsub, chunk);
     const float4 v = *reinterpret_cast<const float4 *>(src + off);
-    float4 hi;
-    hi.x = tf32_rna(v.x);
-    hi.y = tf32_rna(v.y);
-    hi.z = tf32_rna(v.z);
-    hi.w = tf32_rna(v.w);
-    *reinterpret_cast<float4 *>(dst_hi + off) = hi;
-    if (SPLIT3)
-      *reinterpret_cast<float4 *>(dst_lo + off) = make_float4(v.x - hi.x, v.y - hi.y, v.z - hi.z, v.w - hi.w);
+    if (copy) *reinterpret_cast<float4 *>(dst_hi + off) = v;
+    if (SPLIT3) {
+      const float hx = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+      const float hy = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+      const float hz = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+      const float hw = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+      *reinterpret_cast<float4 *>(dst_lo + off) = make_float4(v.x - hx, v.y - hy, v.z - hz, v.w - hw);
+    }
   }
 }
 
@@ -120,10 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
   constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
-  // always for gathers and im2col tiles (TF32 rounding to nearest), and for
-  // 1x1 TMA tiles when they must be split.  A TF32 1x1 TMA tile goes to the
-  // tensor core as loaded (the hardware ignores the low 13 mantissa bits).
-  constexpr bool CONVERT = (AMODE != 2) || SPLIT3;
+  // for gathers (copied from the landing ring) and for 3xTF32 (low parts).
+  // TF32 TMA tiles go to the tensor core as loaded.
+  constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
   // TMEM: two accumulator buffers (MMA / epilogue overlap) + the promoted
   // sums for 3xTF32, rounded up to a power of two >= 32 columns.
   constexpr int kCols = (SPLIT3 ? 3 : 2) * BN;
@@ -336,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;  // global K-step counter
     bool ok = true;
     if constexpr (AMODE != 1) {
-      if (CONVERT) {  // round (and for 3xTF32 split) the TMA-landed tile in place
+      if (CONVERT) {  // 3xTF32: the low parts of the TMA-landed tile
         for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
           for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
@@ -417,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = int(t % tp.n_tiles) * BN;
         const int64_t m0 = (t / tp.n_tiles) * kBM;
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
-        if (AMODE == 3) {
+        if (AMODE == 3 || AMODE == 4) {
           const int ow = int(m0 % g.OW);
           const int64_t q = m0 / g.OW;
           bw = ow * g.sw - g.pw;
@@ -439,6 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tap = k0 / g.C, c0 = k0 - tap * g.C;  // C % 32 == 0: one tap per K step
             const int r = tap / g.KW, sx = tap - r * g.KW;
             tma_load_im2col_4d(a_hi, &amap, c0, bw, bh, bn, uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+          }
+          if (AMODE == 4) {
+            // C == 4: eight taps per K step, one 128 pixel x 16 byte column
+            // each; taps past the filter read an image past the batch (zeros).
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              const int tap = kb * 8 + j;
+              const bool real = tap < g.KH * g.KW;
+              const int r = real ? tap / g.KW : 0, sx = real ? tap - r * g.KW : 0;
+              tma_load_im2col_4d(a_hi + j * 2048, &amap, 0, bw, bh, real ? bn : g.N, uint16_t(sx * g.dw),
+                                 uint16_t(r * g.dh), &raw_bar[s]);
+            }
           }
         }
       }
@@ -477,18 +495,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *a_lo = a_hi + kABytes;
           uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
           uint8_t *b_lo = b_hi + B_BYTES;
-          const uint64_t dah = smem_desc(a_hi), dbh = smem_desc(b_hi);
-          const uint64_t dal = smem_desc(a_lo), dbl = smem_desc(b_lo);
+          const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
+          // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
+          // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
+          const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
+          const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t step = uint64_t(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+            const uint64_t step = uint64_t(kk * 32) >> 4;            // 8 tf32 = 32 bytes along K
+            const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
             const uint32_t first = (group_start && kk == 0) ? 0u : 1u;
             if (SPLIT3) {
-              mma_tf32(dtm, dal + step, dbh + step, idesc, first);
-              mma_tf32(dtm, dah + step, dbl + step, idesc, 1u);
-              mma_tf32(dtm, dah + step, dbh + step, idesc, 1u);
+              mma_tf32(dtm, dal + astep, dbh + step, idesc, first);
+              mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
+              mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
             } else {
-              mma_tf32(dtm, dah + step, dbh + step, idesc, first);
+              mma_tf32(dtm, dah + astep, dbh + step, idesc, first);
             }
           }
           mma_commit(&empty_bar[s]);
@@ -600,6 +622,9 @@ bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
   if (st.amode == 3)
     return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
                               kBK, kBM);
+  if (st.amode == 4)
+    return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 4, g.KH, g.sh, g.ph, g.dh, 4,
+                              kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
 }
 
@@ -628,12 +653,14 @@ int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, co
                  int *status, cudaStream_t s) {
   if (st.epi_tma) {
     switch (st.amode) {
+      case 4: return launch_cfg<BN, SPLIT3, 4, true>(st, mp, x, y, bias, res, status, s);
       case 3: return launch_cfg<BN, SPLIT3, 3, true>(st, mp, x, y, bias, res, status, s);
       case 2: return launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, status, s);
       default: return launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, status, s);
     }
   }
   switch (st.amode) {
+    case 4: return launch_cfg<BN, SPLIT3, 4, false>(st, mp, x, y, bias, res, status, s);
     case 3: return launch_cfg<BN, SPLIT3, 3, false>(st, mp, x, y, bias, res, status, s);
     case 2: return launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, status, s);
     default: return launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, status, s);
@@ -682,6 +709,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     st->amode = 2;
   else if (g.C % 32 == 0 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
     st->amode = 3;
+  else if (g.C == 4 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
+    st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
   else
     st->amode = 1;
   // Tile width: the smallest that covers Cout up to 128; 256 for wide TF32
@@ -745,7 +774,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   st->set_attr_only = false;
   if (rc) return rc;
   p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) +
-              (st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
+              (st->amode == 4 ? "_im2col4" : st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
               (st->staged_x ? "_relayout" : "");
   return 0;
 }

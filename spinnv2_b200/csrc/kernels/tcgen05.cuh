@@ -33,12 +33,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
+// One bounded probe: the thread is suspended (not spinning, so it takes no
+// issue slots from the warps doing work) until the phase completes or about
+// a millisecond passes.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
@@ -112,6 +115,14 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ uint64_t smem_desc(const void *p) {
   const uint64_t addr = smem_u32(p);
   return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// K-major operand without swizzle, in 8-row x 16-byte core matrices: `lbo`
+// bytes between core matrices along K, `sbo` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc_noswz(const void *p, uint32_t lbo, uint32_t sbo) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr & 0x3FFFFull) >> 4) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) | (uint64_t((sbo >> 4) & 0x3FFF) << 32) |
+         (1ull << 46);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -221,10 +232,11 @@ inline PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
 // im2col map of a dense NHWC tensor [N][H][W][C] for a square conv (kernel k,
 // stride s, pad p, dilation d): the bounding box of filter-window origins
 // runs from -p to (dim - 1) + p - (k - 1) * d in W and H, traversed with
-// step s; 128-byte rows of `channels` elements, 128-byte swizzle.
+// step s; rows of `channels` elements (128 bytes with the default 128-byte
+// swizzle; 16 bytes per pixel, unswizzled, for 4-channel inputs).
 inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
                                int N, int H, int W, int C, int k, int s, int p, int d, uint32_t channels,
-                               uint32_t pixels) {
+                               uint32_t pixels, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   if (!encode_im2col_fn()) return false;
   const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
   const cuuint64_t strides[3] = {cuuint64_t(C) * elem_bytes, cuuint64_t(W) * C * elem_bytes,
@@ -233,8 +245,8 @@ inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint
   const int upper[2] = {p - (k - 1) * d, p - (k - 1) * d};
   const cuuint32_t estr[4] = {1, cuuint32_t(s), cuuint32_t(s), 1};
   return encode_im2col_fn()(map, dtype, 4, const_cast<void *>(base), dims, strides, lower, upper, channels, pixels,
-                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace tc
