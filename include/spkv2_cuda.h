@@ -93,6 +93,21 @@ const char *spkv2_cuda_node_variant(Spkv2Context *ctx, uint32_t node_id);
 /* Human-readable text for a runtime return code. */
 const char *spkv2_cuda_status_string(int code);
 
+/* Bounded-wait watchdog.  Every mbarrier / flag wait in the device kernels
+ * gives up after about a second, records a role code in the context's device
+ * status word and lets the kernel return; the next spkv2_run /
+ * spkv2_cuda_synchronize then reports SPKV2_ERR_DEVICE_STATUS and the
+ * context stays usable.  spkv2_cuda_last_device_code returns the code of the
+ * last such timeout (1 A-operand producer, 2 TMA producer, 3 MMA issuer,
+ * 4 epilogue, 5/6 operand or residual landing, 7 accumulator hand-off,
+ * 9 watchdog probe).
+ * spkv2_cuda_watchdog_probe (no reference counterpart) exercises that path on
+ * purpose: one block waits on an mbarrier that nothing completes, with a
+ * limit of wait_us microseconds (1 .. 2,000,000); it returns
+ * SPKV2_ERR_DEVICE_STATUS with *code = 9.  Nothing faults or traps. */
+int spkv2_cuda_watchdog_probe(Spkv2Context *ctx, uint32_t wait_us, int *code);
+int spkv2_cuda_last_device_code(Spkv2Context *ctx);
+
 /* FNV-1a 32 over `size` bytes: the SPK package checksum (the loader checks
  * it; the Python SPK writer calls it for large packages). */
 uint32_t spkv2_fnv1a32(const void *data, size_t size);

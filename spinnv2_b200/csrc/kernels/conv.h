@@ -28,6 +28,29 @@ struct ConvGeo {
   float res_scale;      // s_r / s_y          (kConvI8 with residual)
 };
 
+// Tile width (output channels per tile) for the tcgen05 kernels: the one
+// with the shortest estimated run, waves x K steps x cycles per K step.
+// One wave = one tile per SM; a K step is four M=128 MMAs whose issue cost,
+// measured on B200 for TF32 (K=8) and INT8 (K=32), is max(48, N/2) cycles
+// each (narrow tiles are bound by shared-memory operand reads).  Ties go to
+// the wider tile.
+inline int pick_block_n(int64_t P, int M, int64_t K_steps, int sms, int min_bn, int max_bn) {
+  const int64_t m_tiles = (P + 127) / 128;
+  int best = max_bn;
+  int64_t best_cost = -1;
+  for (int bn = max_bn; bn >= min_bn; bn /= 2) {
+    if (bn > 32 && (bn / 2) >= M) continue;  // a narrower tile already covers Cout
+    const int64_t tiles = m_tiles * ((M + bn - 1) / bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * K_steps * 4 * (bn / 2 > 48 ? bn / 2 : 48);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 void conv_tc_release(void *state);
 void conv_tc_i8_release(void *state);
 

@@ -713,11 +713,13 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
   else
     st->amode = 1;
-  // Tile width: the smallest that covers Cout up to 128; 256 for wide TF32
-  // layers.  3xTF32 keeps 128: two partial buffers plus the promoted sums
-  // take 3 x BN TMEM columns, and TMEM has 512.
-  int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128;
-  if (g.M >= 256 && !st->split3) bn = 256;
+  // Tile width from the wave / MMA-rate model.  3xTF32 stays at <= 128: two
+  // partial buffers plus the promoted sums take 3 x BN TMEM columns, and TMEM
+  // has 512.
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int bn = pick_block_n(g.P, g.M, ceil_div(g.K, kBK), sms, 32, st->split3 ? 128 : 256);
   if (const char *e = getenv("SPKV2_TC_BN")) {
     const int v = atoi(e);
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
@@ -740,9 +742,6 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     tp.group = 2;
     if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
   }
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   st->grid = int(std::min<int64_t>(tp.tiles, sms));
   const int parts = st->split3 ? 2 : 1;
   float *wtc = static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));

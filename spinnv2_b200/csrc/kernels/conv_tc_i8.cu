@@ -476,7 +476,11 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
     st->amode = 3;
   else
     st->amode = 1;
-  int bn = g.M <= 32 ? 32 : g.M <= 64 ? 64 : g.M <= 128 ? 128 : 256;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Tile width from the wave / MMA-rate model; 4 epilogue warps (AMODE 1)
+  // take at most 128 columns, 8 (AMODE 2/3) at least 64.
+  int bn = pick_block_n(g.P, g.M, ceil_div(g.K, kBK), sms, st->amode == 1 ? 32 : 64, st->amode == 1 ? 128 : 256);
   if (const char *e = getenv("SPKV2_TC_BN")) {
     const int v = atoi(e);
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
@@ -498,8 +502,6 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
                 reinterpret_cast<uintptr_t>(y_dev) % 16 == 0 && reinterpret_cast<uintptr_t>(r_dev) % 16 == 0)
                    ? 1
                    : 0;
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   st->grid = int(std::min<int64_t>(tp.tiles, sms));
   int8_t *wp = static_cast<int8_t *>(device_alloc(size_t(tp.Npad) * tp.Kpad));
   if (!wp) {

@@ -34,6 +34,10 @@ SPKV2_DECLARE_OP(topk)
 
 #undef SPKV2_DECLARE_OP
 
+// Watchdog self-test: a block whose bounded mbarrier wait never completes
+// gives up after `wait_us` and records code 9 in *d_status (watchdog.cu).
+int watchdog_probe(int *d_status, uint32_t wait_us, cudaStream_t stream);
+
 // XOR `mask` into one 32-bit word on the device (fault-event injection).
 int launch_bit_flip(uint32_t *word, uint32_t mask, cudaStream_t stream);
 

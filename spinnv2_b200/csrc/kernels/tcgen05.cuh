@@ -46,19 +46,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false on timeout or when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
-                                          int code) {
+// Bounded wait: false on timeout (after `limit` clock cycles; the first
+// role to give up records `code` in the status word) or when another role
+// already aborted.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                                int code, long long limit) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       if (status) atomicExch(status, code);
       return false;
     }
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                          int code) {
+  return mbar_wait_limit(bar, parity, abort_flag, status, code, kWaitCycles);
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

@@ -87,6 +87,7 @@ struct Spkv2Context {
   int math_mode = SPKV2_CUDA_MATH_SPEC;
   int graph_mode = 1;
   int *d_status = nullptr;  // device-side status word written by bounded waits
+  int last_device_code = 0; // code of the last bounded wait that gave up
 
   // ---- per-node cache (reference context.h:46-48) ----
   std::vector<void *> node_cache;

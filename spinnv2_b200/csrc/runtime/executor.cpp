@@ -365,6 +365,7 @@ int take_device_status(Spkv2Context *ctx) {
   if (!ctx->d_status) return 0;
   if (cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return SPKV2_ERR_CUDA;
   if (st != 0) {
+    ctx->last_device_code = st;
     cudaMemset(ctx->d_status, 0, sizeof(int));
     return SPKV2_ERR_DEVICE_STATUS;
   }
@@ -783,6 +784,20 @@ int spkv2_cuda_write_tensor(Spkv2Context *ctx, uint32_t tensor_id, const void *h
   cudaSetDevice(ctx->device);
   return copy_tensor_from_host(t, host, ctx->stream);
 }
+
+int spkv2_cuda_watchdog_probe(Spkv2Context *ctx, uint32_t wait_us, int *code) {
+  if (!ctx || wait_us == 0 || wait_us > 2000000u) return -1;
+  if (!ctx->prepared || !ctx->d_status) return SPKV2_ERR_NOT_PREPARED;
+  cudaSetDevice(ctx->device);
+  int rc = watchdog_probe(ctx->d_status, wait_us, ctx->stream);
+  if (rc) return rc;
+  if ((rc = cuda_status(cudaStreamSynchronize(ctx->stream)))) return rc;
+  rc = take_device_status(ctx);
+  if (code) *code = rc ? ctx->last_device_code : 0;
+  return rc;
+}
+
+int spkv2_cuda_last_device_code(Spkv2Context *ctx) { return ctx ? ctx->last_device_code : 0; }
 
 int spkv2_cuda_launches_per_run(Spkv2Context *ctx, uint32_t *count) {
   if (!ctx || !count) return -1;

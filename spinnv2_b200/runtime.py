@@ -123,6 +123,8 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "spkv2_cuda_run_async": (i32, [vp]),
         "spkv2_cuda_synchronize": (i32, [vp]),
         "spkv2_cuda_run_nodes": (i32, [vp, u32, u32]),
+        "spkv2_cuda_watchdog_probe": (i32, [vp, u32, ctypes.POINTER(i32)]),
+        "spkv2_cuda_last_device_code": (i32, [vp]),
         "spkv2_cuda_profile_nodes": (i32, [vp, ctypes.POINTER(ctypes.c_float), u32]),
         "spkv2_cuda_read_tensor": (i32, [vp, u32, vp, sz]),
         "spkv2_cuda_write_tensor": (i32, [vp, u32, vp, sz]),
@@ -278,6 +280,12 @@ class Runtime:
         out = (ctypes.c_float * max(n, 1))()
         self._check(self.lib.spkv2_cuda_profile_nodes(self.ctx, out, n), "profile nodes")
         return np.array(out[:n], dtype=np.float64)
+
+    def watchdog_probe(self, wait_us: int = 1000) -> tuple[int, int]:
+        """Run the bounded-wait self-test; returns (return code, recorded code)."""
+        code = ctypes.c_int(0)
+        rc = self.lib.spkv2_cuda_watchdog_probe(self.ctx, int(wait_us), ctypes.byref(code))
+        return int(rc), int(code.value)
 
     def stream(self) -> int:
         return int(self.lib.spkv2_cuda_stream(self.ctx) or 0)
