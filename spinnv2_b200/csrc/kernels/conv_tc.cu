@@ -116,7 +116,7 @@ __device__ __forceinline__ void convert_tile(const uint8_t *src, uint8_t *dst_hi
   }
 }
 
-template <int BN, int STAGES, int LAND, bool SPLIT3, int AMODE, bool EPI_TMA>
+template <int BN, int STAGES, int LAND, bool SPLIT3, int AMODE, bool EPI_TMA, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap ymap, const float *__restrict__ x,
@@ -124,12 +124,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                    int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int B_BYTES = StageBytes<BN, SPLIT3>::B;
-  constexpr int STAGE = StageBytes<BN, SPLIT3>::value;
+  // PAIR: 2-SM tiles.  The two CTAs of a cluster share one M = 256 x N = BN
+  // MMA issued by CTA 0; each holds its 128 rows of A and BN/2 rows of B.
+  static_assert(!PAIR || (AMODE == 2 || AMODE == 3), "CTA pairs take TMA-fed A operands");
+  constexpr int BROWS = PAIR ? BN / 2 : BN;  // weight rows held by this CTA
+  constexpr int TILE_ROWS = PAIR ? 2 * kBM : kBM;
+  constexpr int B_BYTES = StageBytes<BROWS, SPLIT3>::B;
+  constexpr int STAGE = StageBytes<BROWS, SPLIT3>::value;
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
-  // for gathers (copied from the landing ring) and for 3xTF32 (low parts).
-  // TF32 TMA tiles go to the tensor core as loaded.
+  // for gathers (copied from the landing ring), for 3xTF32 (low parts) and,
+  // in a CTA pair, to tell the leader that this CTA's operands have landed.
+  // Otherwise TF32 TMA tiles go to the tensor core as loaded.
   constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
+  constexpr bool RELAY = CONVERT || PAIR;
   // TMEM: two accumulator buffers (MMA / epilogue overlap) + the promoted
   // sums for 3xTF32, rounded up to a power of two >= 32 columns.
   constexpr int kCols = (SPLIT3 ? 3 : 2) * BN;
@@ -143,27 +150,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const ConvGeo &g = tp.g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;                    // 0 = leader of the pair
+  const int64_t tile0 = PAIR ? int64_t(cluster_id_x()) : int64_t(blockIdx.x);
+  const int64_t tstep = PAIR ? int64_t(cluster_count_x()) : int64_t(gridDim.x);
+  // Barriers completed by the other CTA of a pair are waited on with
+  // acquire at cluster scope.
+  auto wait_any = [&](uint64_t *bar, uint32_t parity, int code) {
+    return PAIR ? mbar_wait_cluster(bar, parity, &abort_flag, status, code)
+                : mbar_wait(bar, parity, &abort_flag, status, code);
+  };
+  // Arrivals that the leader's MMA thread waits for come from both CTAs.
+  auto arrive_leader = [&](uint64_t *bar) {
+    if (PAIR)
+      mbar_arrive_rank(bar, 0);
+    else
+      mbar_arrive(bar);
+  };
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&raw_bar[s], 1);     // TMA producer's arrive.expect_tx (+ transaction bytes)
-      mbar_init(&full_bar[s], 128);  // A warps, after converting
-      mbar_init(&empty_bar[s], 1);   // MMA commit
+      mbar_init(&raw_bar[s], 1);                     // TMA producer's arrive.expect_tx (+ transaction bytes)
+      mbar_init(&full_bar[s], PAIR ? 256 : 128);     // A warps (of both CTAs of a pair)
+      mbar_init(&empty_bar[s], 1);                   // MMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 32 * kEpiWarps);
+      mbar_init(&acce_bar[b], 32 * kEpiWarps * (PAIR ? 2 : 1));
     }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 13) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_holder)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&tmem_base_holder)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&tmem_base_holder)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_holder;
 
@@ -181,9 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
     const uint32_t tsum = trow + uint32_t(2 * BN);                  // promoted sums (3xTF32)
-    for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x) {
+    for (int64_t t = tile0; t < tp.tiles; t += tstep) {
       const int n0 = int(t % tp.n_tiles) * BN;
-      const int64_t m0 = (t / tp.n_tiles) * kBM;
+      const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
       const int row = quarter * 32 + lane;
       const int64_t p = m0 + row;
       const bool pv = p < g.P;
@@ -206,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool failed = false;
       for (int gidx = 0; gidx + 1 < ngroups; ++gidx, ++gi) {
         const int pb = gi & 1;
-        if (!mbar_wait(&accf_bar[pb], (gi >> 1) & 1, &abort_flag, status, 4)) {
+        if (!wait_any(&accf_bar[pb], (gi >> 1) & 1, 4)) {
           failed = true;
           break;
         }
@@ -225,11 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&acce_bar[pb]);
+        arrive_leader(&acce_bar[pb]);
       }
       if (failed) break;
       const int ab = gi & 1;
-      if (!mbar_wait(&accf_bar[ab], (gi >> 1) & 1, &abort_flag, status, 4)) break;
+      if (!wait_any(&accf_bar[ab], (gi >> 1) & 1, 4)) break;
       tc_fence_after();
       // Bias, residual, activation and store of accumulator columns
       // cb..cb+31 of this thread's row.
@@ -313,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Last K group: partial (+ sums) -> bias/residual/activation -> store.
       if (ncol == 0) {
         tc_fence_before();
-        mbar_arrive(&acce_bar[ab]);
+        arrive_leader(&acce_bar[ab]);
         ++gi;
       }
 #pragma unroll 1
@@ -329,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cb + 32 >= col0 + ncol) {
           // All of this warp's accumulator columns are read: hand the buffer back.
           tc_fence_before();
-          mbar_arrive(&acce_bar[ab]);
+          arrive_leader(&acce_bar[ab]);
           ++gi;
         }
         store_chunk(cb, acc);
@@ -342,16 +376,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;  // global K-step counter
     bool ok = true;
     if constexpr (AMODE != 1) {
-      if (CONVERT) {  // 3xTF32: the low parts of the TMA-landed tile
-        for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+      if (RELAY) {  // 3xTF32: the low parts of the TMA-landed tile; pairs: tell the leader
+        for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
           for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
             const int s = it % STAGES;
             ok = mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5);
             if (!ok) break;
             uint8_t *a_hi = smem + s * STAGE;
-            convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
+            if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
             fence_proxy_async();
-            mbar_arrive(&full_bar[s]);
+            arrive_leader(&full_bar[s]);
           }
         }
       }
@@ -419,9 +453,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE != 1 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+      for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
         const int n0 = int(t % tp.n_tiles) * BN;
-        const int64_t m0 = (t / tp.n_tiles) * kBM;
+        const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
+        const int brow = n0 + int(rank) * BROWS;  // first weight row this CTA loads
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
         if (AMODE == 3 || AMODE == 4) {
           const int ow = int(m0 % g.OW);
@@ -432,13 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
           const int s = it % STAGES;
-          ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1, &abort_flag, status, 2);
+          ok = wait_any(&empty_bar[s], ((it / STAGES) & 1) ^ 1, 2);
           if (!ok) break;
           uint8_t *a_hi = smem + s * STAGE;
           uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
           mbar_arrive_expect_tx(&raw_bar[s], bytes);
-          tma_load_2d(b_hi, &wmap, kb * kBK, n0, &raw_bar[s]);
-          if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + n0, &raw_bar[s]);
+          tma_load_2d(b_hi, &wmap, kb * kBK, brow, &raw_bar[s]);
+          if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + brow, &raw_bar[s]);
           if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
           if (AMODE == 3) {
             const int k0 = kb * kBK;
@@ -463,32 +498,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc =
-          (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+    // (in a CTA pair only the leader issues; the peer's warp just frees TMEM)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
+                                 (uint32_t(TILE_ROWS >> 4) << 24);
       uint32_t it = 0;
       uint32_t gi = 0;  // accumulator hand-offs issued (one per K group)
       bool ok = true;
       int ab = 0;
       uint32_t dtm = tmem;
-      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
+      for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
           const bool group_start = kb % tp.group == 0;
           const bool group_end = kb % tp.group == tp.group - 1 || kb == tp.num_kb - 1;
           if (group_start) {
             ab = gi & 1;
-            ok = mbar_wait(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, &abort_flag, status, 7);
+            ok = wait_any(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, 7);
             if (!ok) break;
             tc_fence_after();
             dtm = tmem + uint32_t(ab * BN);
           }
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          // B (and, in AMODE 2, A) lands by TMA on raw_bar; a converted A
-          // tile is signalled on full_bar (in AMODE 2 only after the A warps
-          // saw raw_bar themselves).
-          ok = (AMODE != 1 && CONVERT) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
-          if (ok && CONVERT) ok = mbar_wait(&full_bar[s], ph, &abort_flag, status, 3);
+          // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
+          // (or, in a pair, relayed) stage is signalled on full_bar, after
+          // the A warps saw raw_bar themselves.
+          ok = (AMODE != 1 && RELAY) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
+          if (ok && RELAY) ok = wait_any(&full_bar[s], ph, 3);
           if (!ok) break;
           tc_fence_after();
           uint8_t *a_hi = smem + s * STAGE;
@@ -505,7 +541,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t step = uint64_t(kk * 32) >> 4;            // 8 tf32 = 32 bytes along K
             const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
             const uint32_t first = (group_start && kk == 0) ? 0u : 1u;
-            if (SPLIT3) {
+            if (PAIR) {
+              if (SPLIT3) {
+                mma_tf32_pair(dtm, dal + astep, dbh + step, idesc, first);
+                mma_tf32_pair(dtm, dah + astep, dbl + step, idesc, 1u);
+                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, 1u);
+              } else {
+                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, first);
+              }
+            } else if (SPLIT3) {
               mma_tf32(dtm, dal + astep, dbh + step, idesc, first);
               mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
               mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
@@ -513,9 +557,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_tf32(dtm, dah + astep, dbh + step, idesc, first);
             }
           }
-          mma_commit(&empty_bar[s]);
+          if (PAIR)
+            mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
+          else
+            mma_commit(&empty_bar[s]);
           if (group_end) {
-            mma_commit(&accf_bar[ab]);
+            if (PAIR)
+              mma_commit_pair(&accf_bar[ab]);
+            else
+              mma_commit(&accf_bar[ab]);
             ++gi;
           }
         }
@@ -531,10 +581,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync();  // the leader's MMAs read the peer's shared memory until here
+  else
+    __syncthreads();
   if (warp == 13) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
@@ -588,17 +644,27 @@ __global__ void to_nhwc4_kernel(float *__restrict__ dst, const float *__restrict
 struct PipeShape {
   int stages, land;
 };
-constexpr PipeShape pipe_shape(int bn, bool split3, int amode) {
-  return amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
-                              : PipeShape{bn == 256 ? 4 : 6, 0})
-                    : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
-                              : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
+// In a CTA pair each CTA holds BN/2 weight rows, so its stages are those of
+// a BN/2-wide single-CTA tile.
+constexpr PipeShape pipe_shape(int bn, bool split3, int amode, bool pair = false) {
+  return pair ? pipe_shape(bn / 2, split3, amode)
+              : amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
+                                     : PipeShape{bn == 256 ? 4 : 6, 0})
+                           : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
+                                     : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
 }
 
-size_t smem_bytes(int bn, bool split3, int amode) {
-  const PipeShape ps = pipe_shape(bn, split3, amode);
-  return size_t(ps.stages) * size_t(split3 ? 2 : 1) * (kABytes + bn * 128) + size_t(ps.land) * kABytes +
+size_t smem_bytes(int bn, bool split3, int amode, bool pair) {
+  const PipeShape ps = pipe_shape(bn, split3, amode, pair);
+  const int brows = pair ? bn / 2 : bn;
+  return size_t(ps.stages) * size_t(split3 ? 2 : 1) * (kABytes + brows * 128) + size_t(ps.land) * kABytes +
          kStagingBytes + 1024;
+}
+
+// Clusters of two CTAs with this kernel's shared memory can be scheduled.
+bool cluster_launch_ok(int dev) {
+  int ok = 0;
+  return cudaDeviceGetAttribute(&ok, cudaDevAttrClusterLaunch, dev) == cudaSuccess && ok;
 }
 
 struct TcState {
@@ -607,6 +673,7 @@ struct TcState {
   int bn = 128;
   bool split3 = true;
   int amode = 1;
+  bool pair = false;  // 2-SM tiles (cluster of 2, cta_group::2 MMA)
   bool epi_tma = false;
   size_t smem = 0;
   int grid = 148;
@@ -637,20 +704,44 @@ struct Maps {
   CUtensorMap a, y;
 };
 
-template <int BN, bool SPLIT3, int AMODE, bool EPI>
+template <int BN, bool SPLIT3, int AMODE, bool EPI, bool PAIR = false>
 int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
                int *status, cudaStream_t s) {
-  constexpr PipeShape ps = pipe_shape(BN, SPLIT3, AMODE);
-  auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI>;
+  constexpr PipeShape ps = pipe_shape(BN, SPLIT3, AMODE, PAIR);
+  auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI, PAIR>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status);
-  return cuda_status(cudaGetLastError());
+  if (!PAIR) {
+    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status);
+    return cuda_status(cudaGetLastError());
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(st.grid), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = st.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status));
 }
 
 template <int BN, bool SPLIT3>
 int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
                  int *status, cudaStream_t s) {
+  if constexpr (BN >= 128) {
+    if (st.pair) {
+      if (st.epi_tma)
+        return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, true, true>(st, mp, x, y, bias, res, status, s)
+                             : launch_cfg<BN, SPLIT3, 2, true, true>(st, mp, x, y, bias, res, status, s);
+      return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, false, true>(st, mp, x, y, bias, res, status, s)
+                           : launch_cfg<BN, SPLIT3, 2, false, true>(st, mp, x, y, bias, res, status, s);
+    }
+  }
   if (st.epi_tma) {
     switch (st.amode) {
       case 4: return launch_cfg<BN, SPLIT3, 4, true>(st, mp, x, y, bias, res, status, s);
@@ -725,6 +816,22 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     if ((v == 32 || v == 64 || v == 128 || v == 256) && v <= std::max(32, int(ceil_div(g.M, 32) * 32))) bn = v;
   }
   if (st->split3 && bn == 256) bn = 128;
+  // 2-SM tiles (opt-in, SPKV2_TC_PAIR=1) for TMA-fed convs wide enough to
+  // fill the pairs: each CTA streams half of the weight panel (TF32 pairs use
+  // N = 256 when Cout >= 256).  Measured on B200 they are slower than single
+  // tiles at ResNet shapes: the stage hand-off from the peer CTA to the
+  // leader lengthens each K step more than the halved weight traffic saves.
+  {
+    const char *e = getenv("SPKV2_TC_PAIR");
+    const bool allow = e && e[0] == '1';
+    const int pbn = st->split3 ? 128 : (g.M >= 256 ? 256 : 128);
+    const int64_t pair_tiles = ceil_div(g.P, 2 * kBM) * ceil_div(g.M, pbn);
+    if (allow && (st->amode == 2 || st->amode == 3) && g.M >= 128 && pair_tiles >= sms / 4 &&
+        cluster_launch_ok(dev)) {
+      st->pair = true;
+      bn = pbn;
+    }
+  }
   st->bn = bn;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   st->epi_tma = p.mode == kConvF32 && nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
@@ -734,7 +841,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.Npad = int(ceil_div(g.M, bn) * bn);
   tp.num_kb = tp.Kpad / kBK;
   tp.n_tiles = tp.Npad / bn;
-  tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
+  tp.tiles = ceil_div(g.P, st->pair ? 2 * kBM : kBM) * tp.n_tiles;  // pair tiles have 256 rows
   // 3xTF32 promotes every `group` K steps; TF32 hands off once per tile.
   tp.out_i8 = p.mode == kConvF32ToI8 ? 1 : 0;
   tp.group = tp.num_kb;
@@ -742,7 +849,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     tp.group = 2;
     if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
   }
-  st->grid = int(std::min<int64_t>(tp.tiles, sms));
+  st->grid = st->pair ? 2 * int(std::min<int64_t>(tp.tiles, sms / 2)) : int(std::min<int64_t>(tp.tiles, sms));
   const int parts = st->split3 ? 2 : 1;
   float *wtc = static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));
   if (!wtc) {
@@ -752,8 +859,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
       wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0);
   int rc = cuda_status(cudaGetLastError());
-  bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad), uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad),
-                                 uint32_t(bn));
+  bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad),
+                                 uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(st->pair ? bn / 2 : bn));
   if (ok && st->amode != 1) ok = encode_a(*st, &st->amap, x_dev);
   if (ok && st->epi_tma) ok = encode_y(*st, &st->ymap, y_dev);
   st->amap_base = x_dev;
@@ -763,7 +870,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  st->smem = smem_bytes(bn, st->split3, st->amode);
+  st->smem = smem_bytes(bn, st->split3, st->amode, st->pair);
   p.w_tc = wtc;
   p.tc_state = st;
   p.tc_block_n = bn;
@@ -772,7 +879,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   rc = conv_tc_launch(p, nullptr, nullptr, nullptr, nullptr, s);
   st->set_attr_only = false;
   if (rc) return rc;
-  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + "_bn" + std::to_string(bn) +
+  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + (st->pair ? "_pair" : "") + "_bn" +
+              std::to_string(bn) +
               (st->amode == 4 ? "_im2col4" : st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
               (st->staged_x ? "_relayout" : "");
   return 0;

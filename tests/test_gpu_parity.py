@@ -163,3 +163,23 @@ def test_resnet101_tf32_mode_is_close(gpu):
     assert err < 2e-3
     assert rel < 3e-2
     np.testing.assert_array_equal(np.argmax(probs, axis=1), np.argmax(ref, axis=1))
+
+
+@pytest.mark.parametrize("case", ["conv3x3_256_14", "conv1x1_1024_256_14"])
+@pytest.mark.parametrize("math", ["3xtf32", "tf32"])
+def test_sweep_batch32_on_cta_pairs_matches_reference(gpu, case, math, monkeypatch):
+    """2-SM tiles (opt-in): one M = 256 MMA per CTA pair, each CTA holding
+    half of the weight panel, same numerics as single tiles."""
+    from spinnv2_b200.runtime import MATH_3XTF32, MATH_TF32
+    from spinnv2_b200.spk import read_spk
+
+    monkeypatch.setenv("SPKV2_TC_PAIR", "1")
+    spk = compile_pair(case, 32)
+    x = seeded_input(read_spk(spk["cuda_b200"]).inputs[0].shape)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x], math_mode=MATH_3XTF32 if math == "3xtf32" else MATH_TF32)
+    assert any("_pair_" in v for v in variants), variants
+    if math == "3xtf32":
+        np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+    else:
+        assert float(np.max(np.abs(out[0] - ref))) < 2e-2 * float(np.max(np.abs(ref)))
