@@ -825,9 +825,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     const char *e = getenv("SPKV2_TC_PAIR");
     const bool allow = e && e[0] == '1';
     const int pbn = st->split3 ? 128 : (g.M >= 256 ? 256 : 128);
-    const int64_t pair_tiles = ceil_div(g.P, 2 * kBM) * ceil_div(g.M, pbn);
-    if (allow && (st->amode == 2 || st->amode == 3) && g.M >= 128 && pair_tiles >= sms / 4 &&
-        cluster_launch_ok(dev)) {
+    if (allow && (st->amode == 2 || st->amode == 3) && g.M >= 128 && cluster_launch_ok(dev)) {
       st->pair = true;
       bn = pbn;
     }
