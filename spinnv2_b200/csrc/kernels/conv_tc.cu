@@ -598,20 +598,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 // [part][Npad][Kpad] with k = (r*KW + s)*Cg + c over the GEMM channel count
 // Cg (which may be padded above the weight's Cw); part 0 = TF32(rna) of w,
 // part 1 = w - part 0 (3xTF32 only); zero padding.  w_kn: the weights are a
-// [K][Cout] matrix (Gemm B with transB = 0) instead of OIHW.
+// [K][Cout] matrix (Gemm B with transB = 0) instead of OIHW.  packed_kw > 0:
+// row-packed input (see pack_rows_kernel), k = r*32 + s*4 + c for the
+// original kernel width packed_kw.
 __global__ void pack_tc_kernel(float *__restrict__ dst, const float *__restrict__ w, ConvGeo g, int Cw, int Npad,
-                               int Kpad, int split3, int w_kn) {
+                               int Kpad, int split3, int w_kn, int packed_kw) {
   const int64_t total = int64_t(Npad) * Kpad;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int m = int(i / Kpad), k = int(i % Kpad);
     float v = 0.f;
     if (m < g.M && k < g.K) {
-      const int c = k % g.Cg, rs = k / g.Cg, s = rs % g.KW, r = rs / g.KW;
-      if (c < Cw) v = w_kn ? w[int64_t(c) * g.M + m] : w[((int64_t(m) * Cw + c) * g.KH + r) * g.KW + s];
+      if (packed_kw > 0) {
+        const int r = k / 32, j = k % 32, s = j / 4, c = j % 4;
+        if (s < packed_kw && c < Cw) v = w[((int64_t(m) * Cw + c) * g.KH + r) * packed_kw + s];
+      } else {
+        const int c = k % g.Cg, rs = k / g.Cg, s = rs % g.KW, r = rs / g.KW;
+        if (c < Cw) v = w_kn ? w[int64_t(c) * g.M + m] : w[((int64_t(m) * Cw + c) * g.KH + r) * g.KW + s];
+      }
     }
     const float hi = tf32_rna(v);
     dst[i] = hi;
     if (split3) dst[total + i] = v - hi;
+  }
+}
+
+// Row packing for convs with few input channels (C <= 4, 4 * KW <= 32; a
+// network's first conv): dst[n][h][ow][s*4 + c] = x[n][c][h][ow*sw - pw + s]
+// for s < KW and c < C, zero elsewhere (padding, and the 32 - 4*KW tail), so
+// one 128-byte packed pixel holds a whole filter row for output column ow and
+// the conv becomes a KH x 1 conv over the packed tensor (stride sh x 1,
+// padding ph x 0).  One thread per (n, h, ow, 4-float group).
+__global__ void pack_rows_kernel(float *__restrict__ dst, const float *__restrict__ x, int N, int C, int H, int W,
+                                 int OW, int KW, int sw, int pw, int64_t xs0, int64_t xs1, int64_t xs2, int64_t xs3) {
+  const int64_t total = int64_t(N) * H * OW * 8;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int s = int(i & 7);
+    const int64_t pix = i >> 3;  // (n, h, ow)
+    const int ow = int(pix % OW);
+    const int h = int((pix / OW) % H);
+    const int n = int(pix / (int64_t(OW) * H));
+    const int iw = ow * sw - pw + s;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (s < KW && iw >= 0 && iw < W) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < C) v[c] = x[n * xs0 + c * xs1 + h * xs2 + iw * xs3];
+    }
+    *reinterpret_cast<float4 *>(dst + pix * 32 + s * 4) = make_float4(v[0], v[1], v[2], v[3]);
   }
 }
 
@@ -678,7 +711,8 @@ struct TcState {
   size_t smem = 0;
   int grid = 148;
   bool set_attr_only = false;  // dispatch only sets the kernel's smem attribute
-  float *staged_x = nullptr;   // NHWC4 copy of an input that needs relayout
+  float *staged_x = nullptr;   // NHWC4 (or row-packed) copy of an input that needs relayout
+  bool packed_rows = false;    // staged_x is row-packed (pack_rows_kernel)
   ConvGeo src;                 // geometry of the original input (relayout source)
   const void *amap_base = nullptr, *ymap_base = nullptr;  // pointers the A / Y maps were encoded for
   ~TcState() { device_free(staged_x); }
@@ -687,8 +721,8 @@ struct TcState {
 bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
   const ConvGeo &g = st.tp.g;
   if (st.amode == 3)
-    return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
-                              kBK, kBM);
+    return encode_im2col_nhwc2(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, g.C, g.KH, g.KW, g.sh, g.sw,
+                               g.ph, g.pw, g.dh, g.dw, kBK, kBM);
   if (st.amode == 4)
     return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 4, g.KH, g.sh, g.ph, g.dh, 4,
                               kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -775,7 +809,31 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   ConvGeo g = g0;
   const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
   const bool aligned_in = reinterpret_cast<uintptr_t>(x_dev) % 16 == 0;
-  if (!(nhwc_in && g.C % 4 == 0 && aligned_in)) {
+  const bool row_pack = !(nhwc_in && g.C % 4 == 0 && aligned_in) && g.C <= 4 && 4 * g.KW <= 32 &&
+                        encode_im2col_fn() && !getenv("SPKV2_TC_NO_ROWPACK");
+  if (row_pack) {
+    // Few-channel input: pack each filter row's KW x 4 channels into one
+    // 128-byte pixel; the GEMM side becomes a KH x 1 conv over 32 channels.
+    st->staged_x = static_cast<float *>(device_alloc(size_t(g.N) * g.H * g.OW * 32 * sizeof(float) + 256));
+    if (!st->staged_x) {
+      delete st;
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+    st->packed_rows = true;
+    g.C = g.Cg = 32;
+    g.W = g.OW;
+    g.KW = 1;
+    g.sw = 1;
+    g.pw = 0;
+    g.dw = 1;
+    g.K = g.KH * 32;
+    g.xs[0] = int64_t(g.H) * g.W * 32;
+    g.xs[1] = 1;
+    g.xs[2] = int64_t(g.W) * 32;
+    g.xs[3] = 32;
+    x_dev = st->staged_x;
+    p.launches = 2;
+  } else if (!(nhwc_in && g.C % 4 == 0 && aligned_in)) {
     // Re-lay the input out as dense NHWC with C rounded up to 4.
     const int C4 = int(ceil_div(g.C, 4) * 4);
     st->staged_x = static_cast<float *>(device_alloc(size_t(g.N) * g.H * g.W * C4 * sizeof(float) + 256));
@@ -798,7 +856,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
   if (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
     st->amode = 2;
-  else if (g.C % 32 == 0 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
+  else if (g.C % 32 == 0 && (square || st->packed_rows) && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
     st->amode = 3;
   else if (g.C == 4 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
     st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
@@ -855,7 +913,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     return SPKV2_ERR_DEVICE_ALLOC;
   }
   pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
-      wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0);
+      wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0,
+      st->packed_rows ? g0.KW : 0);
   int rc = cuda_status(cudaGetLastError());
   bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad),
                                  uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(st->pair ? bn / 2 : bn));
@@ -880,7 +939,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + (st->pair ? "_pair" : "") + "_bn" +
               std::to_string(bn) +
               (st->amode == 4 ? "_im2col4" : st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
-              (st->staged_x ? "_relayout" : "");
+              (st->packed_rows ? "_rowpack" : st->staged_x ? "_relayout" : "");
   return 0;
 }
 
@@ -895,10 +954,16 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   const float *xf = static_cast<const float *>(x);
   if (st.staged_x && !st.set_attr_only) {
     const ConvGeo &o = st.src;
-    const int C4 = st.tp.g.C;
-    const int64_t total = int64_t(o.N) * o.H * o.W * (C4 / 4);
-    to_nhwc4_kernel<<<grid_for(total, 256), 256, 0, s>>>(st.staged_x, xf, o.N, o.C, o.H, o.W, C4, o.xs[0], o.xs[1],
-                                                        o.xs[2], o.xs[3]);
+    if (st.packed_rows) {
+      const int64_t total = int64_t(o.N) * o.H * o.OW * 8;
+      pack_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(st.staged_x, xf, o.N, o.C, o.H, o.W, o.OW, o.KW, o.sw,
+                                                           o.pw, o.xs[0], o.xs[1], o.xs[2], o.xs[3]);
+    } else {
+      const int C4 = st.tp.g.C;
+      const int64_t total = int64_t(o.N) * o.H * o.W * (C4 / 4);
+      to_nhwc4_kernel<<<grid_for(total, 256), 256, 0, s>>>(st.staged_x, xf, o.N, o.C, o.H, o.W, C4, o.xs[0], o.xs[1],
+                                                          o.xs[2], o.xs[3]);
+    }
     int rc = cuda_status(cudaGetLastError());
     if (rc) return rc;
     xf = st.staged_x;

@@ -325,6 +325,25 @@ inline PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
 // runs from -p to (dim - 1) + p - (k - 1) * d in W and H, traversed with
 // step s; rows of `channels` elements (128 bytes with the default 128-byte
 // swizzle; 16 bytes per pixel, unswizzled, for 4-channel inputs).
+// General form: kernel kh x kw, stride sh x sw, padding ph x pw, dilation
+// dh x dw (corner and stride arrays in the tensor's dimension order, W
+// before H).
+inline bool encode_im2col_nhwc2(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
+                                int N, int H, int W, int C, int kh, int kw, int sh, int sw, int ph, int pw, int dh,
+                                int dw, uint32_t channels, uint32_t pixels,
+                                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  if (!encode_im2col_fn()) return false;
+  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+  const cuuint64_t strides[3] = {cuuint64_t(C) * elem_bytes, cuuint64_t(W) * C * elem_bytes,
+                                 cuuint64_t(H) * W * C * elem_bytes};
+  const int lower[2] = {-pw, -ph};
+  const int upper[2] = {pw - (kw - 1) * dw, ph - (kh - 1) * dh};
+  const cuuint32_t estr[4] = {1, cuuint32_t(sw), cuuint32_t(sh), 1};
+  return encode_im2col_fn()(map, dtype, 4, const_cast<void *>(base), dims, strides, lower, upper, channels, pixels,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
                                int N, int H, int W, int C, int k, int s, int p, int d, uint32_t channels,
                                uint32_t pixels, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
