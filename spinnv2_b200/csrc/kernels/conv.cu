@@ -366,7 +366,7 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (math != SPKV2_CUDA_MATH_FP32) {
     const void *r_dev = g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
     rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream)
-                 : conv_tc_prepare(*p, tw.data, tx.data, ty.data, ctx->stream);
+                 : conv_tc_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;
       return rc;

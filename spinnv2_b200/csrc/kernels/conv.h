@@ -80,10 +80,11 @@ int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res,
 
 // tcgen05 path (conv_tc.cu): returns 0 when the node is eligible and its
 // operand panels were built; SPKV2_ERR_UNSUPPORTED when the shape is not.
-int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s);
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, const void *r_dev,
+                    cudaStream_t s);
 // w_kn: the weights are a [K][Cout] matrix (Gemm B, transB = 0), not OIHW.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
-                       cudaStream_t s);
+                       cudaStream_t s, const void *r_dev = nullptr);
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
 
 // tcgen05 kind::i8 path (conv_tc_i8.cu) for kConvI8 / kConvI8ToI32.

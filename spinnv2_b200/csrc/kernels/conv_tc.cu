@@ -78,6 +78,7 @@ struct TcParams {
   int64_t tiles;   // m_tiles * n_tiles
   int group;       // K steps per TMEM partial when promoting (3xTF32)
   int out_i8;      // quantise the output: y = clamp(rne(act(v) * (1 / s_y)), -128, 127)
+  int res_tma;     // residual tiles arrive by TMA in the epilogue staging tile (NHWC residual, TMA store)
 };
 
 template <int BN, bool SPLIT3>
@@ -119,7 +120,8 @@ __device__ __forceinline__ void convert_tile(const uint8_t *src, uint8_t *dst_hi
 template <int BN, int STAGES, int LAND, bool SPLIT3, int AMODE, bool EPI_TMA, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                   const __grid_constant__ CUtensorMap ymap, const float *__restrict__ x,
+                   const __grid_constant__ CUtensorMap ymap, const __grid_constant__ CUtensorMap rmap,
+                   const float *__restrict__ x,
                    const float *__restrict__ bias, const float *__restrict__ res, float *__restrict__ y, TcParams tp,
                    int *status) {
   extern __shared__ uint8_t smem_raw[];
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *land = smem + STAGES * STAGE;    // AMODE 1 landing ring
   uint8_t *staging = land + LAND * kABytes;  // epilogue TMA-store staging
   __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
+  __shared__ uint64_t res_bar[kEpiWarps];  // residual tile landed in the warp's staging tile
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
 
@@ -177,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&accf_bar[b], 1);
       mbar_init(&acce_bar[b], 32 * kEpiWarps * (PAIR ? 2 : 1));
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bar[w], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -211,6 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *stage_buf = staging + warp * 4096;
     const bool rvec = g.rs[1] == 1 && (g.M % 4) == 0;
     uint32_t sc = 0;  // TMA-store chunks issued by this warp
+    uint32_t rc = 0;  // residual tiles loaded by this warp
+    const bool res_tma = EPI_TMA && tp.res_tma && g.has_res;
     uint32_t gi = 0;  // accumulator hand-offs consumed (one per K group)
     const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
@@ -272,7 +278,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c0 >= g.M) return;  // channel padding (warp-uniform)
         float vals[32];
         const int cn = min(32, g.M - c0);
-        if (cn == 32 && (!g.has_res || rvec)) {
+        if (res_tma) {
+          // (acc + bias) + residual, the residual read from the staging tile
+          // its TMA load filled (rows past the end of the tensor read zeros).
+          if (!mbar_wait(&res_bar[warp], rc & 1, &abort_flag, status, 6)) return;
+          ++rc;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
+            const float4 rr = *reinterpret_cast<const float4 *>(stage_buf + swz_off(lane, j / 4));
+            vals[j] = __uint_as_float(acc[j]) + b.x + rr.x;
+            vals[j + 1] = __uint_as_float(acc[j + 1]) + b.y + rr.y;
+            vals[j + 2] = __uint_as_float(acc[j + 2]) + b.z + rr.z;
+            vals[j + 3] = __uint_as_float(acc[j + 3]) + b.w + rr.w;
+          }
+        } else if (cn == 32 && (!g.has_res || rvec)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
@@ -321,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (EPI_TMA) {
           uint8_t *buf = stage_buf;
-          if (sc >= 1 && lane == 0) tma_store_wait_read0();  // the previous store has read the tile
+          if (!res_tma && sc >= 1 && lane == 0) tma_store_wait_read0();  // the previous store has read the tile
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -352,6 +372,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll 1
       for (int cb = col0; cb < col0 + ncol; cb += 32) {
+        if (res_tma && n0 + cb < g.M) {
+          // Start this chunk's residual tile into the staging tile (free once
+          // the previous chunk's store has read it); the TMEM reads and the
+          // bias overlap its flight.
+          if (lane == 0) {
+            if (sc >= 1) tma_store_wait_read0();
+            mbar_arrive_expect_tx(&res_bar[warp], 4096);
+            tma_load_2d(stage_buf, &rmap, n0 + cb, int(m0 + quarter * 32), &res_bar[warp]);
+          }
+          __syncwarp();
+        }
         uint32_t acc[32];
         tmem_ld32(trow + uint32_t(ab * BN + cb), acc);
         if (ngroups > 1) {
@@ -701,7 +732,7 @@ bool cluster_launch_ok(int dev) {
 }
 
 struct TcState {
-  CUtensorMap wmap, amap, ymap;
+  CUtensorMap wmap, amap, ymap, rmap;
   TcParams tp;
   int bn = 128;
   bool split3 = true;
@@ -714,7 +745,7 @@ struct TcState {
   float *staged_x = nullptr;   // NHWC4 (or row-packed) copy of an input that needs relayout
   bool packed_rows = false;    // staged_x is row-packed (pack_rows_kernel)
   ConvGeo src;                 // geometry of the original input (relayout source)
-  const void *amap_base = nullptr, *ymap_base = nullptr;  // pointers the A / Y maps were encoded for
+  const void *amap_base = nullptr, *ymap_base = nullptr, *rmap_base = nullptr;  // pointers the maps were encoded for
   ~TcState() { device_free(staged_x); }
 };
 
@@ -735,7 +766,7 @@ bool encode_y(const TcState &st, CUtensorMap *map, const void *y) {
 }
 
 struct Maps {
-  CUtensorMap a, y;
+  CUtensorMap a, y, r;
 };
 
 template <int BN, bool SPLIT3, int AMODE, bool EPI, bool PAIR = false>
@@ -746,7 +777,7 @@ int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, cons
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   if (!PAIR) {
-    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status);
+    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, status);
     return cuda_status(cudaGetLastError());
   }
   cudaLaunchConfig_t cfg = {};
@@ -761,7 +792,7 @@ int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, cons
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, x, bias, res, y, st.tp, status));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, status));
 }
 
 template <int BN, bool SPLIT3>
@@ -796,7 +827,7 @@ int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, co
 
 // Eligible: fp32 in and out, group 1, Cout >= 16, 3xTF32 or TF32 math.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
-                       cudaStream_t s) {
+                       cudaStream_t s, const void *r_dev) {
   const ConvGeo &g0 = p.g;
   if ((p.mode != kConvF32 && p.mode != kConvF32ToI8) || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
@@ -805,6 +836,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   memset(&st->wmap, 0, sizeof(st->wmap));
   memset(&st->amap, 0, sizeof(st->amap));
   memset(&st->ymap, 0, sizeof(st->ymap));
+  memset(&st->rmap, 0, sizeof(st->rmap));
   st->src = g0;
   ConvGeo g = g0;
   const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
@@ -900,6 +932,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.tiles = ceil_div(g.P, st->pair ? 2 * kBM : kBM) * tp.n_tiles;  // pair tiles have 256 rows
   // 3xTF32 promotes every `group` K steps; TF32 hands off once per tile.
   tp.out_i8 = p.mode == kConvF32ToI8 ? 1 : 0;
+  const bool nhwc_res = g.has_res && g.rs[1] == 1 && g.rs[3] == g.M && g.rs[2] == int64_t(g.OW) * g.M;
+  tp.res_tma = (st->epi_tma && nhwc_res && reinterpret_cast<uintptr_t>(r_dev) % 16 == 0) ? 1 : 0;
   tp.group = tp.num_kb;
   if (st->split3) {
     tp.group = 2;
@@ -920,6 +954,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
                                  uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(st->pair ? bn / 2 : bn));
   if (ok && st->amode != 1) ok = encode_a(*st, &st->amap, x_dev);
   if (ok && st->epi_tma) ok = encode_y(*st, &st->ymap, y_dev);
+  if (ok && tp.res_tma) ok = encode_y(*st, &st->rmap, r_dev);  // same geometry as the output
+  st->rmap_base = r_dev;
   st->amap_base = x_dev;
   st->ymap_base = y_dev;
   if (!ok) {
@@ -943,8 +979,9 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   return 0;
 }
 
-int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, cudaStream_t s) {
-  return conv_tc_prepare_ex(p, w_raw_dev, x_dev, y_dev, false, s);
+int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, const void *r_dev,
+                    cudaStream_t s) {
+  return conv_tc_prepare_ex(p, w_raw_dev, x_dev, y_dev, false, s, r_dev);
 }
 
 void conv_tc_release(void *state) { delete static_cast<TcState *>(state); }
@@ -973,10 +1010,11 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   const float *bias = p.bias_f;
   // Tensor maps follow the tensors: a graph input or output rebound to
   // another device buffer since prepare gets freshly encoded maps.
-  Maps mp{st.amap, st.ymap};
+  Maps mp{st.amap, st.ymap, st.rmap};
   if (!st.set_attr_only) {
     if (st.amode != 1 && !st.staged_x && xf != st.amap_base && !encode_a(st, &mp.a, xf)) return SPKV2_ERR_UNSUPPORTED;
     if (st.epi_tma && yf != st.ymap_base && !encode_y(st, &mp.y, yf)) return SPKV2_ERR_UNSUPPORTED;
+    if (st.tp.res_tma && rf != st.rmap_base && !encode_y(st, &mp.r, rf)) return SPKV2_ERR_UNSUPPORTED;
   }
   if (st.split3) {
     switch (st.bn) {
