@@ -116,6 +116,27 @@ def conv_flops(pkg, int8_only: bool = False) -> tuple[float, list[int]]:
     return total, ids
 
 
+def conv_bytes(pkg, ids: list[int]) -> int:
+    """Algorithmic HBM bytes of the given conv nodes: every input (activation,
+    weights, bias, residual) read once and the output written once."""
+    total = 0
+    for n in pkg.nodes:
+        if n.id in ids:
+            for t in list(n.inputs) + list(n.outputs):
+                if t >= 0:
+                    ten = pkg.tensors[t]
+                    total += int(np.prod(ten.shape)) * np.dtype(ten.np_dtype).itemsize
+    return total
+
+
+# DRAM bytes (read + write) of all Conv launches of one step, from one ncu
+# capture of `bench.py --steps 2 --warmup 3` (dram__bytes_read.sum +
+# dram__bytes_write.sum over the 105 conv launches of a step; the command is in
+# profiles/launches_resnet101_bs64_3xtf32.md).  Keyed by the workload it was
+# measured on; other workloads report null.
+MEASURED_CONV_TRAFFIC = {("resnet101", 64, "3xtf32", False): 6588.6e6 + 1540.4e6}
+
+
 def use_all_host_threads() -> None:
     """OpenMP threads for the reference CPU runtime: every host core (torchrun
     exports OMP_NUM_THREADS=1 to its workers), unless SPKV2_REF_THREADS says
@@ -204,6 +225,7 @@ def run_gpu_arm(args, group) -> None:
     from spinnv2_b200.runtime import MATH_3XTF32, MATH_FP32, MATH_SPEC, MATH_TF32, Runtime
 
     math_mode = {"spec": MATH_SPEC, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32, "fp32": MATH_FP32}[args.math]
+    math_label = "3xtf32" if args.math in ("spec", "3xtf32") else args.math
     torch.cuda.set_device(local)
     spk = pipeline.compile_config(args.config, args.batch, targets=("cuda_b200",), seed=0, int8=args.int8)["cuda_b200"]
     rt = Runtime(spk, device=local, math_mode=math_mode, graph=True)
@@ -258,6 +280,9 @@ def run_gpu_arm(args, group) -> None:
         peak_basis = f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"
     achieved = flops / (conv_ms / 1000.0) / 1e12
     variants = sorted({rt.node_variant(i) for i in conv_ids})
+    alg_bytes = conv_bytes(pkg, conv_ids)
+    eff_math = "int8" if args.int8 else math_label
+    traffic = MEASURED_CONV_TRAFFIC.get((args.config, args.batch, eff_math, args.int8))
 
     # ---- end to end through the public API: pinned host in/out, spkv2_run ----
     rt2 = Runtime(spk, device=local, math_mode=math_mode, graph=True)
@@ -292,7 +317,8 @@ def run_gpu_arm(args, group) -> None:
                     "d2h_bytes_per_step": int(np.prod(out_t.shape) * 4)},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": peak_unit,
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": traffic,
+                         "algorithmic_bytes_per_step": alg_bytes,
                          "kernel": ("all int8 Conv launches" if args.int8 else "all Conv launches") + " of one step",
                          "flops_per_step": flops, "conv_ms_per_step": conv_ms, "peak_basis": peak_basis},
         }

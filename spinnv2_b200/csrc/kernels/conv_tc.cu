@@ -81,10 +81,19 @@ struct TcParams {
   int res_tma;     // residual tiles arrive by TMA in the epilogue staging tile (NHWC residual, TMA store)
 };
 
+// One pipeline stage: [A (hi)][A lo (3xTF32)][B hi][B lo (3xTF32)].
+constexpr int stage_bytes(int brows, bool split3) { return (split3 ? 2 : 1) * (kABytes + brows * 128); }
+
+// TMEM accumulator buffers the MMA rotates through.  3xTF32 hands a partial
+// buffer to the epilogue every `group` K steps to be added into the fp32
+// sums; with three buffers the epilogue has two groups' time to do it before
+// the MMA needs the buffer again.  TF32 hands off once per tile (two buffers:
+// tile t's epilogue overlaps tile t+1's MMAs).
 template <int BN, bool SPLIT3>
-struct StageBytes {
-  static constexpr int B = BN * 128;
-  static constexpr int value = (SPLIT3 ? 2 : 1) * (kABytes + B);
+struct AccLayout {
+  static constexpr int nbuf = SPLIT3 && 4 * BN <= 512 ? 3 : 2;
+  static constexpr int sum_col = nbuf * BN;                     // promoted sums (3xTF32)
+  static constexpr int cols = sum_col + (SPLIT3 ? BN : 0);
 };
 
 // Row / chunk mapping shared by the A loads and the conversion pass: thread t
@@ -131,22 +140,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(!PAIR || (AMODE == 2 || AMODE == 3), "CTA pairs take TMA-fed A operands");
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // weight rows held by this CTA
   constexpr int TILE_ROWS = PAIR ? 2 * kBM : kBM;
-  constexpr int B_BYTES = StageBytes<BROWS, SPLIT3>::B;
-  constexpr int STAGE = StageBytes<BROWS, SPLIT3>::value;
+  constexpr int B_BYTES = BROWS * 128;
+  constexpr int STAGE = stage_bytes(BROWS, SPLIT3);
+  constexpr int B_OFF = (SPLIT3 ? 2 : 1) * kABytes;  // B hi within a stage
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
   // for gathers (copied from the landing ring), for 3xTF32 (low parts) and,
   // in a CTA pair, to tell the leader that this CTA's operands have landed.
   // Otherwise TF32 TMA tiles go to the tensor core as loaded.
   constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
   constexpr bool RELAY = CONVERT || PAIR;
-  // TMEM: two accumulator buffers (MMA / epilogue overlap) + the promoted
-  // sums for 3xTF32, rounded up to a power of two >= 32 columns.
-  constexpr int kCols = (SPLIT3 ? 3 : 2) * BN;
+  // TMEM: the accumulator buffers + the promoted sums for 3xTF32, rounded
+  // up to a power of two >= 32 columns.
+  using Acc = AccLayout<BN, SPLIT3>;
+  constexpr int NBUF = Acc::nbuf;
+  constexpr int kCols = Acc::cols;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
   static_assert(kCols <= 512, "accumulators exceed TMEM");
   uint8_t *land = smem + STAGES * STAGE;    // AMODE 1 landing ring
   uint8_t *staging = land + LAND * kABytes;  // epilogue TMA-store staging
-  __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
+  __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[NBUF], acce_bar[NBUF];
   __shared__ uint64_t res_bar[kEpiWarps];  // residual tile landed in the warp's staging tile
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_bar[s], PAIR ? 256 : 128);     // A warps (of both CTAs of a pair)
       mbar_init(&empty_bar[s], 1);                   // MMA commit
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&accf_bar[b], 1);
       mbar_init(&acce_bar[b], 32 * kEpiWarps * (PAIR ? 2 : 1));
     }
@@ -220,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t gi = 0;  // accumulator hand-offs consumed (one per K group)
     const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
-    const uint32_t tsum = trow + uint32_t(2 * BN);                  // promoted sums (3xTF32)
+    const uint32_t tsum = trow + uint32_t(Acc::sum_col);            // promoted sums (3xTF32)
     for (int64_t t = tile0; t < tp.tiles; t += tstep) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
@@ -245,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (round-to-nearest fp32 adds) and hand the partial buffer back.
       bool failed = false;
       for (int gidx = 0; gidx + 1 < ngroups; ++gidx, ++gi) {
-        const int pb = gi & 1;
-        if (!wait_any(&accf_bar[pb], (gi >> 1) & 1, 4)) {
+        const int pb = int(gi % NBUF);
+        if (!wait_any(&accf_bar[pb], (gi / NBUF) & 1, 4)) {
           failed = true;
           break;
         }
@@ -268,8 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         arrive_leader(&acce_bar[pb]);
       }
       if (failed) break;
-      const int ab = gi & 1;
-      if (!wait_any(&accf_bar[ab], (gi >> 1) & 1, 4)) break;
+      const int ab = int(gi % NBUF);
+      if (!wait_any(&accf_bar[ab], (gi / NBUF) & 1, 4)) break;
       tc_fence_after();
       // Bias, residual, activation and store of accumulator columns
       // cb..cb+31 of this thread's row.
@@ -501,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = wait_any(&empty_bar[s], ((it / STAGES) & 1) ^ 1, 2);
           if (!ok) break;
           uint8_t *a_hi = smem + s * STAGE;
-          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
+          uint8_t *b_hi = a_hi + B_OFF;
           mbar_arrive_expect_tx(&raw_bar[s], bytes);
           tma_load_2d(b_hi, &wmap, kb * kBK, brow, &raw_bar[s]);
           if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + brow, &raw_bar[s]);
@@ -533,80 +545,91 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
                                  (uint32_t(TILE_ROWS >> 4) << 24);
-      uint32_t it = 0;
-      uint32_t gi = 0;  // accumulator hand-offs issued (one per K group)
-      bool ok = true;
-      int ab = 0;
+      // One flat loop over this CTA's K steps (all its tiles), with the
+      // stage, K-step and group positions kept as counters: the issuing
+      // thread does as little as possible between its MMA batches.
+      const int64_t my_tiles = tile0 < tp.tiles ? (tp.tiles - 1 - tile0) / tstep + 1 : 0;
+      const uint32_t total = uint32_t(my_tiles) * uint32_t(tp.num_kb);
+      const int num_kb = tp.num_kb, group = tp.group;
+      uint32_t gi = 0;            // accumulator hand-offs issued (one per K group)
+      uint32_t ab = 0, abph = 0;  // accumulator buffer and its phase parity
       uint32_t dtm = tmem;
-      for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
-        for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
-          const bool group_start = kb % tp.group == 0;
-          const bool group_end = kb % tp.group == tp.group - 1 || kb == tp.num_kb - 1;
-          if (group_start) {
-            ab = gi & 1;
-            ok = wait_any(&acce_bar[ab], ((gi >> 1) & 1) ^ 1, 7);
-            if (!ok) break;
-            tc_fence_after();
-            dtm = tmem + uint32_t(ab * BN);
-          }
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
-          // (or, in a pair, relayed) stage is signalled on full_bar, after
-          // the A warps saw raw_bar themselves.
-          ok = (AMODE != 1 && RELAY) || mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
-          if (ok && RELAY) ok = wait_any(&full_bar[s], ph, 3);
-          if (!ok) break;
+      int kb = 0, gk = 0;      // K step within the tile / within its group
+      int s = 0;               // stage
+      uint32_t ph = 0;         // stage phase parity
+      for (uint32_t it = 0; it < total; ++it) {
+        if (gk == 0) {
+          if (!wait_any(&acce_bar[ab], abph ^ 1, 7)) break;
           tc_fence_after();
-          uint8_t *a_hi = smem + s * STAGE;
-          uint8_t *a_lo = a_hi + kABytes;
-          uint8_t *b_hi = a_hi + (SPLIT3 ? 2 : 1) * kABytes;
-          uint8_t *b_lo = b_hi + B_BYTES;
-          const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
-          // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
-          // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
-          const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
-          const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
+          dtm = tmem + ab * uint32_t(BN);
+        }
+        // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
+        // (or, in a pair, relayed) stage is signalled on full_bar, after the
+        // A warps saw raw_bar themselves.
+        if (!(AMODE != 1 && RELAY) && !mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3)) break;
+        if (RELAY && !wait_any(&full_bar[s], ph, 3)) break;
+        tc_fence_after();
+        uint8_t *a_hi = smem + s * STAGE;
+        uint8_t *a_lo = a_hi + kABytes;
+        uint8_t *b_hi = a_hi + B_OFF;
+        uint8_t *b_lo = b_hi + B_BYTES;
+        const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
+        // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
+        // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
+        const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
+        const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t step = uint64_t(kk * 32) >> 4;            // 8 tf32 = 32 bytes along K
-            const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
-            const uint32_t first = (group_start && kk == 0) ? 0u : 1u;
-            if (PAIR) {
-              if (SPLIT3) {
-                mma_tf32_pair(dtm, dal + astep, dbh + step, idesc, first);
-                mma_tf32_pair(dtm, dah + astep, dbl + step, idesc, 1u);
-                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, 1u);
-              } else {
-                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, first);
-              }
-            } else if (SPLIT3) {
-              mma_tf32(dtm, dal + astep, dbh + step, idesc, first);
-              mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
-              mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t step = uint64_t(kk * 32) >> 4;                          // 8 tf32 = 32 bytes along K
+          const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
+          const uint32_t acc = (gk | kk) ? 1u : 0u;                              // first MMA of a group overwrites
+          if (PAIR) {
+            if (SPLIT3) {
+              mma_tf32_pair(dtm, dal + astep, dbh + step, idesc, acc);
+              mma_tf32_pair(dtm, dah + astep, dbl + step, idesc, 1u);
+              mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, 1u);
             } else {
-              mma_tf32(dtm, dah + astep, dbh + step, idesc, first);
+              mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, acc);
             }
+          } else if (SPLIT3) {
+            mma_tf32(dtm, dal + astep, dbh + step, idesc, acc);
+            mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
+            mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
+          } else {
+            mma_tf32(dtm, dah + astep, dbh + step, idesc, acc);
           }
+        }
+        if (PAIR)
+          mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
+        else
+          mma_commit(&empty_bar[s]);
+        ++kb;
+        ++gk;
+        const bool tile_end = kb == num_kb;
+        if (gk == group || tile_end) {
           if (PAIR)
-            mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
+            mma_commit_pair(&accf_bar[ab]);
           else
-            mma_commit(&empty_bar[s]);
-          if (group_end) {
-            if (PAIR)
-              mma_commit_pair(&accf_bar[ab]);
-            else
-              mma_commit(&accf_bar[ab]);
-            ++gi;
+            mma_commit(&accf_bar[ab]);
+          ++gi;
+          gk = 0;
+          if (++ab == uint32_t(NBUF)) {
+            ab = 0;
+            abph ^= 1u;
           }
+        }
+        if (tile_end) kb = 0;
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
         }
       }
       // Every issued MMA must finish before TMEM is freed (also on abort):
       // a bounded wait on the last accumulator hand-off.
       if (gi > 0) {
-        const int last = (gi - 1) & 1;
+        const int last = int((gi - 1) % NBUF);
         const long long t0 = clock64();
-        while (!mbar_try_wait(&accf_bar[last], ((gi - 1) >> 1) & 1) && clock64() - t0 < kWaitCycles) {
+        while (!mbar_try_wait(&accf_bar[last], ((gi - 1) / NBUF) & 1) && clock64() - t0 < kWaitCycles) {
         }
       }
     }
@@ -721,8 +744,8 @@ constexpr PipeShape pipe_shape(int bn, bool split3, int amode, bool pair = false
 size_t smem_bytes(int bn, bool split3, int amode, bool pair) {
   const PipeShape ps = pipe_shape(bn, split3, amode, pair);
   const int brows = pair ? bn / 2 : bn;
-  return size_t(ps.stages) * size_t(split3 ? 2 : 1) * (kABytes + brows * 128) + size_t(ps.land) * kABytes +
-         kStagingBytes + 1024;
+  return size_t(ps.stages) * size_t(stage_bytes(brows, split3)) +
+         size_t(ps.land) * kABytes + kStagingBytes + 1024;
 }
 
 // Clusters of two CTAs with this kernel's shared memory can be scheduled.
