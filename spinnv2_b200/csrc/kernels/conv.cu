@@ -367,6 +367,7 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     const void *r_dev = g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
     rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream)
                  : conv_tc_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream);
+    if (rc == 0 && !int_acc) rc = conv_tc_attach(ctx, *p);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;
       return rc;
@@ -396,6 +397,24 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   return 0;
 }
 
+int conv_tc_attach(Spkv2Context *ctx, const ConvPlan &p) {
+  const size_t need = conv_tc_sk_workspace_bytes(p);
+  if (need > ctx->sk_ws_bytes) {
+    // Nothing in flight may still use the old buffer; a captured graph
+    // holding its address is re-captured.
+    int rc = cuda_status(cudaStreamSynchronize(ctx->stream));
+    if (rc) return rc;
+    device_free(ctx->d_sk_ws);
+    ctx->d_sk_ws = static_cast<float *>(device_alloc(need));
+    ctx->sk_ws_bytes = ctx->d_sk_ws ? need : 0;
+    ctx->graph_dirty = true;
+    if (!ctx->d_sk_ws) return SPKV2_ERR_DEVICE_ALLOC;
+  }
+  size_t bytes = 0;
+  if (void *cnt = conv_tc_sk_counters(p, &bytes)) ctx->sk_counters.emplace_back(cnt, bytes);
+  return 0;
+}
+
 int conv_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   ConvPlan *p = node_plan<ConvPlan>(ctx, node);
   if (!p) return SPKV2_ERR_NOT_PREPARED;
@@ -405,7 +424,7 @@ int conv_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   const void *res = p->g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
   if (p->w_tc)
     return p->tc_i8 ? conv_tc_i8_launch(*p, x, y, res, ctx->d_status, ctx->stream)
-                    : conv_tc_launch(*p, x, y, res, ctx->d_status, ctx->stream);
+                    : conv_tc_launch(*p, x, y, res, ctx->d_status, ctx->stream, ctx->d_sk_ws);
   return conv_simt_launch(*p, x, y, res, ctx->stream);
 }
 

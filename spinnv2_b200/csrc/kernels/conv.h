@@ -85,7 +85,18 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
 // w_kn: the weights are a [K][Cout] matrix (Gemm B, transB = 0), not OIHW.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
                        cudaStream_t s, const void *r_dev = nullptr);
-int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s);
+// sk_ws: the context's stream-K workspace (conv_tc_attach sized it); may be
+// null for plans that do not use stream-K.
+int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s,
+                   float *sk_ws);
+// Stream-K needs of a prepared tcgen05 plan: workspace bytes for partial
+// tiles (one buffer per context, shared by all convs since they run in
+// stream order) and the plan's arrival counters (zero between launches).
+size_t conv_tc_sk_workspace_bytes(const ConvPlan &p);
+void *conv_tc_sk_counters(const ConvPlan &p, size_t *bytes);
+// Grows the context's stream-K workspace to what plan p needs and registers
+// its counters (re-zeroed after a device-side abort).  Called at prepare.
+int conv_tc_attach(Spkv2Context *ctx, const ConvPlan &p);
 
 // tcgen05 kind::i8 path (conv_tc_i8.cu) for kConvI8 / kConvI8ToI32.
 int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const void *y_dev, const void *r_dev,

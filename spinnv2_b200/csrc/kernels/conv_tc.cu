@@ -49,6 +49,7 @@
 // the CTA records a code in the context's status word and winds down.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <math.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -79,6 +80,74 @@ struct TcParams {
   int group;       // K steps per TMEM partial when promoting (3xTF32)
   int out_i8;      // quantise the output: y = clamp(rne(act(v) * (1 / s_y)), -128, 127)
   int res_tma;     // residual tiles arrive by TMA in the epilogue staging tile (NHWC residual, TMA store)
+  int64_t dp_tiles;  // tiles walked whole, round-robin over the CTAs (all tiles without stream-K)
+  int64_t sk_units;  // stream-K: K steps of tiles dp_tiles.. spread evenly over the CTAs (0: off)
+};
+
+// One unit of a CTA's work: K steps [kb0, kb1) of output tile `tile`.  A
+// stream-K tile whose K steps are spread over several CTAs has nseg > 1
+// segments, of which this CTA's is number `seg`; its partial sums go to this
+// CTA's workspace slot `slot` (0: the first segment of its share, 1: the
+// last) and the epilogue warp that arrives last adds all of them.
+struct Seg {
+  int64_t tile;
+  int kb0, kb1;
+  int nseg, seg;
+  int tt;  // index among the stream-K tiles
+  int slot;
+};
+
+// The static schedule every role of a CTA walks in the same order: whole
+// tiles tile0, tile0 + tstep, ... below dp_tiles, then this CTA's contiguous
+// share [u0, u1) of the remaining tiles' K steps (unit u = K step u % nk of
+// stream-K tile u / nk), cut at tile boundaries.
+struct WorkIter {
+  int64_t t, tstep, dp_tiles;
+  int64_t u, u0, u1, U;
+  int nk, G, b;
+  __device__ WorkIter(const TcParams &tp, int64_t tile0, int64_t step, int cta, int grid)
+      : t(tile0), tstep(step), dp_tiles(tp.dp_tiles), U(tp.sk_units), nk(tp.num_kb), G(grid), b(cta) {
+    u0 = U ? int64_t(b) * U / G : 0;
+    u1 = U ? int64_t(b + 1) * U / G : 0;
+    u = u0;
+  }
+  __device__ int64_t start_of(int64_t cta) const { return cta * U / G; }
+  __device__ int64_t owner(int64_t v) const { return ((v + 1) * G - 1) / U; }  // CTA whose share holds unit v
+  // Workspace slot in which CTA `cta` keeps its segment of stream-K tile tt.
+  __device__ int slot_of(int64_t cta, int64_t tt) const { return start_of(cta) >= tt * nk ? 0 : 1; }
+  // K steps of this CTA's whole schedule.
+  __device__ uint32_t total_steps() const {
+    const int64_t mine = t < dp_tiles ? (dp_tiles - 1 - t) / tstep + 1 : 0;
+    return uint32_t(mine * nk + (u1 - u0));
+  }
+  __device__ bool next(Seg &s) {
+    if (t < dp_tiles) {
+      s.tile = t;
+      s.kb0 = 0;
+      s.kb1 = nk;
+      s.nseg = 1;
+      s.seg = s.tt = s.slot = 0;
+      t += tstep;
+      return true;
+    }
+    if (u >= u1) return false;
+    const int64_t tt = u / nk;
+    s.tt = int(tt);
+    s.tile = dp_tiles + tt;
+    s.kb0 = int(u - tt * nk);
+    s.kb1 = int(s.kb0 + u1 - u < nk ? s.kb0 + u1 - u : nk);
+    s.slot = u == u0 ? 0 : 1;
+    u += s.kb1 - s.kb0;
+    if (s.kb0 == 0 && s.kb1 == nk) {
+      s.nseg = 1;
+      s.seg = 0;
+    } else {
+      const int64_t blo = owner(tt * nk);
+      s.nseg = int(owner(tt * nk + nk - 1) - blo + 1);
+      s.seg = int(b - blo);
+    }
+    return true;
+  }
 };
 
 // One pipeline stage: [A (hi)][A lo (3xTF32)][B hi][B lo (3xTF32)].
@@ -132,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap ymap, const __grid_constant__ CUtensorMap rmap,
                    const float *__restrict__ x,
                    const float *__restrict__ bias, const float *__restrict__ res, float *__restrict__ y, TcParams tp,
-                   int *status) {
+                   float *__restrict__ sk_ws, int *__restrict__ sk_cnt, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // PAIR: 2-SM tiles.  The two CTAs of a cluster share one M = 256 x N = BN
@@ -230,10 +299,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t rc = 0;  // residual tiles loaded by this warp
     const bool res_tma = EPI_TMA && tp.res_tma && g.has_res;
     uint32_t gi = 0;  // accumulator hand-offs consumed (one per K group)
-    const int ngroups = (tp.num_kb + tp.group - 1) / tp.group;
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
     const uint32_t tsum = trow + uint32_t(Acc::sum_col);            // promoted sums (3xTF32)
-    for (int64_t t = tile0; t < tp.tiles; t += tstep) {
+    float4 *const ws4 = reinterpret_cast<float4 *>(sk_ws);
+    WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+    Seg sg;
+    while (wi.next(sg)) {
+      const int64_t t = sg.tile;
+      const int ngroups = (sg.kb1 - sg.kb0 + tp.group - 1) / tp.group;
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
       const int row = quarter * 32 + lane;
@@ -376,18 +449,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      // Last K group: partial (+ sums) -> bias/residual/activation -> store.
-      if (ncol == 0) {
-        tc_fence_before();
-        arrive_leader(&acce_bar[ab]);
-        ++gi;
-      }
-#pragma unroll 1
-      for (int cb = col0; cb < col0 + ncol; cb += 32) {
+      // Start chunk cb's residual tile into the staging tile (free once the
+      // previous chunk's store has read it); the TMEM reads and the bias
+      // overlap its flight.
+      auto issue_res = [&](int cb) {
         if (res_tma && n0 + cb < g.M) {
-          // Start this chunk's residual tile into the staging tile (free once
-          // the previous chunk's store has read it); the TMEM reads and the
-          // bias overlap its flight.
           if (lane == 0) {
             if (sc >= 1) tma_store_wait_read0();
             mbar_arrive_expect_tx(&res_bar[warp], 4096);
@@ -395,7 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         }
-        uint32_t acc[32];
+      };
+      // Last K group: partial (+ sums) of columns cb..cb+31; the buffer goes
+      // back to the MMA once the warp's last chunk is read.
+      auto read_acc = [&](int cb, uint32_t(&acc)[32]) {
         tmem_ld32(trow + uint32_t(ab * BN + cb), acc);
         if (ngroups > 1) {
           uint32_t sum[32];
@@ -404,10 +473,71 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(sum[j]));
         }
         if (cb + 32 >= col0 + ncol) {
-          // All of this warp's accumulator columns are read: hand the buffer back.
           tc_fence_before();
           arrive_leader(&acce_bar[ab]);
           ++gi;
+        }
+      };
+      if (ncol == 0) {
+        tc_fence_before();
+        arrive_leader(&acce_bar[ab]);
+        ++gi;
+        continue;
+      }
+      bool finish = true;
+      int64_t blo = 0;
+      if (sg.nseg > 1) {
+        // Stream-K segment: park this warp's part of the tile in the CTA's
+        // workspace slot ([chunk][4-column group][row] float4s, so a warp's
+        // stores are contiguous) and count the arrival; the segment's last
+        // warp to arrive adds all segments in segment order (the same sum
+        // whichever CTA finishes last) and finishes the tile below.
+        float4 *mine = ws4 + size_t(blockIdx.x * 2 + sg.slot) * (BN * 32);
+#pragma unroll 1
+        for (int cb = col0; cb < col0 + ncol; cb += 32) {
+          uint32_t acc[32];
+          read_acc(cb, acc);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(&mine[((cb >> 5) * 8 + q) * 128 + row],
+                   make_float4(__uint_as_float(acc[4 * q]), __uint_as_float(acc[4 * q + 1]),
+                               __uint_as_float(acc[4 * q + 2]), __uint_as_float(acc[4 * q + 3])));
+        }
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          int *cnt = &sk_cnt[int64_t(sg.tt) * kEpiWarps + warp];
+          last = atomicAdd(cnt, 1) == sg.nseg - 1;
+          if (last) atomicExch(cnt, 0);  // ready for the next launch
+        }
+        finish = __shfl_sync(0xffffffffu, last, 0) != 0;
+        if (finish) __threadfence();
+        blo = wi.owner(int64_t(sg.tt) * tp.num_kb);
+      }
+      if (!finish) continue;
+      // Bias, residual, activation -> store, chunk by chunk.
+#pragma unroll 1
+      for (int cb = col0; cb < col0 + ncol; cb += 32) {
+        issue_res(cb);
+        uint32_t acc[32];
+        if (sg.nseg == 1) {
+          read_acc(cb, acc);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0u;  // +0.0f
+#pragma unroll 1
+          for (int j = 0; j < sg.nseg; ++j) {
+            const float4 *src = ws4 + size_t((blo + j) * 2 + wi.slot_of(blo + j, sg.tt)) * (BN * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 f = __ldcg(&src[((cb >> 5) * 8 + q) * 128 + row]);
+              acc[4 * q] = __float_as_uint(__uint_as_float(acc[4 * q]) + f.x);
+              acc[4 * q + 1] = __float_as_uint(__uint_as_float(acc[4 * q + 1]) + f.y);
+              acc[4 * q + 2] = __float_as_uint(__uint_as_float(acc[4 * q + 2]) + f.z);
+              acc[4 * q + 3] = __float_as_uint(__uint_as_float(acc[4 * q + 3]) + f.w);
+            }
+          }
         }
         store_chunk(cb, acc);
       }
@@ -420,16 +550,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     if constexpr (AMODE != 1) {
       if (RELAY) {  // 3xTF32: the low parts of the TMA-landed tile; pairs: tell the leader
-        for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
-          for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
-            const int s = it % STAGES;
-            ok = mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5);
-            if (!ok) break;
-            uint8_t *a_hi = smem + s * STAGE;
-            if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
-            fence_proxy_async();
-            arrive_leader(&full_bar[s]);
-          }
+        const uint32_t total = WorkIter(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x)).total_steps();
+        for (; it < total; ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5)) break;
+          uint8_t *a_hi = smem + s * STAGE;
+          if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
+          fence_proxy_async();
+          arrive_leader(&full_bar[s]);
         }
       }
     } else {
@@ -446,8 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&full_bar[s]);
         return true;
       };
-      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
-        const int64_t m0 = (t / tp.n_tiles) * kBM;
+      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+      Seg sg;
+      while (ok && wi.next(sg)) {
+        const int64_t m0 = (sg.tile / tp.n_tiles) * kBM;
         int rn[8], rih[8], riw[8];
         bool rvalid[8];
 #pragma unroll
@@ -461,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           riw[i] = ow * g.sw - g.pw;
           rn[i] = int(q / g.OH);
         }
-        for (int kb = 0; kb < tp.num_kb && ok; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb, ++it) {
           // Gather K step `it` into landing slot it % LAND.  That slot's
           // previous step (it - LAND) was converted one iteration ago by this
           // same thread, which reads only the chunks it loads.
@@ -496,7 +626,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE != 1 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
-      for (int64_t t = tile0; t < tp.tiles && ok; t += tstep) {
+      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+      Seg sg;
+      while (ok && wi.next(sg)) {
+        const int64_t t = sg.tile;
         const int n0 = int(t % tp.n_tiles) * BN;
         const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
         const int brow = n0 + int(rank) * BROWS;  // first weight row this CTA loads
@@ -508,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bh = int(q % g.OH) * g.sh - g.ph;
           bn = int(q / g.OH);
         }
-        for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           ok = wait_any(&empty_bar[s], ((it / STAGES) & 1) ^ 1, 2);
           if (!ok) break;
@@ -545,19 +678,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
                                  (uint32_t(TILE_ROWS >> 4) << 24);
-      // One flat loop over this CTA's K steps (all its tiles), with the
-      // stage, K-step and group positions kept as counters: the issuing
-      // thread does as little as possible between its MMA batches.
-      const int64_t my_tiles = tile0 < tp.tiles ? (tp.tiles - 1 - tile0) / tstep + 1 : 0;
-      const uint32_t total = uint32_t(my_tiles) * uint32_t(tp.num_kb);
-      const int num_kb = tp.num_kb, group = tp.group;
+      // One flat loop over this CTA's K steps (all its tiles and stream-K
+      // segments), with the stage, segment and group positions kept as
+      // counters: the issuing thread does as little as possible between its
+      // MMA batches.
+      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+      Seg sg;
+      const uint32_t total = wi.total_steps();
+      const int group = tp.group;
+      int seg_left = 0;  // K steps left in the current segment
       uint32_t gi = 0;            // accumulator hand-offs issued (one per K group)
       uint32_t ab = 0, abph = 0;  // accumulator buffer and its phase parity
       uint32_t dtm = tmem;
-      int kb = 0, gk = 0;      // K step within the tile / within its group
+      int gk = 0;              // K step within its group
       int s = 0;               // stage
       uint32_t ph = 0;         // stage phase parity
       for (uint32_t it = 0; it < total; ++it) {
+        if (seg_left == 0) {
+          if (!wi.next(sg)) break;
+          seg_left = sg.kb1 - sg.kb0;
+        }
         if (gk == 0) {
           if (!wait_any(&acce_bar[ab], abph ^ 1, 7)) break;
           tc_fence_after();
@@ -603,10 +743,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
         else
           mma_commit(&empty_bar[s]);
-        ++kb;
         ++gk;
-        const bool tile_end = kb == num_kb;
-        if (gk == group || tile_end) {
+        const bool seg_end = --seg_left == 0;
+        if (gk == group || seg_end) {
           if (PAIR)
             mma_commit_pair(&accf_bar[ab]);
           else
@@ -618,7 +757,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             abph ^= 1u;
           }
         }
-        if (tile_end) kb = 0;
         if (++s == STAGES) {
           s = 0;
           ph ^= 1u;
@@ -769,7 +907,13 @@ struct TcState {
   bool packed_rows = false;    // staged_x is row-packed (pack_rows_kernel)
   ConvGeo src;                 // geometry of the original input (relayout source)
   const void *amap_base = nullptr, *ymap_base = nullptr, *rmap_base = nullptr;  // pointers the maps were encoded for
-  ~TcState() { device_free(staged_x); }
+  int *sk_cnt = nullptr;   // stream-K arrival counters [stream-K tiles][epilogue warps]
+  size_t sk_cnt_bytes = 0;
+  size_t sk_ws_bytes = 0;  // workspace the launch needs for partial tiles (two slots per CTA)
+  ~TcState() {
+    device_free(staged_x);
+    device_free(sk_cnt);
+  }
 };
 
 bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
@@ -794,13 +938,14 @@ struct Maps {
 
 template <int BN, bool SPLIT3, int AMODE, bool EPI, bool PAIR = false>
 int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
-               int *status, cudaStream_t s) {
+               float *sk_ws, int *status, cudaStream_t s) {
   constexpr PipeShape ps = pipe_shape(BN, SPLIT3, AMODE, PAIR);
   auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI, PAIR>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   if (!PAIR) {
-    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, status);
+    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, sk_ws,
+                                                      st.sk_cnt, status);
     return cuda_status(cudaGetLastError());
   }
   cudaLaunchConfig_t cfg = {};
@@ -815,34 +960,35 @@ int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, cons
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, status));
+  return cuda_status(
+      cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, sk_ws, st.sk_cnt, status));
 }
 
 template <int BN, bool SPLIT3>
 int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, const float *bias, const float *res,
-                 int *status, cudaStream_t s) {
+                 float *w, int *status, cudaStream_t s) {
   if constexpr (BN >= 128) {
     if (st.pair) {
       if (st.epi_tma)
-        return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, true, true>(st, mp, x, y, bias, res, status, s)
-                             : launch_cfg<BN, SPLIT3, 2, true, true>(st, mp, x, y, bias, res, status, s);
-      return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, false, true>(st, mp, x, y, bias, res, status, s)
-                           : launch_cfg<BN, SPLIT3, 2, false, true>(st, mp, x, y, bias, res, status, s);
+        return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, true, true>(st, mp, x, y, bias, res, w, status, s)
+                             : launch_cfg<BN, SPLIT3, 2, true, true>(st, mp, x, y, bias, res, w, status, s);
+      return st.amode == 3 ? launch_cfg<BN, SPLIT3, 3, false, true>(st, mp, x, y, bias, res, w, status, s)
+                           : launch_cfg<BN, SPLIT3, 2, false, true>(st, mp, x, y, bias, res, w, status, s);
     }
   }
   if (st.epi_tma) {
     switch (st.amode) {
-      case 4: return launch_cfg<BN, SPLIT3, 4, true>(st, mp, x, y, bias, res, status, s);
-      case 3: return launch_cfg<BN, SPLIT3, 3, true>(st, mp, x, y, bias, res, status, s);
-      case 2: return launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, status, s);
-      default: return launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, status, s);
+      case 4: return launch_cfg<BN, SPLIT3, 4, true>(st, mp, x, y, bias, res, w, status, s);
+      case 3: return launch_cfg<BN, SPLIT3, 3, true>(st, mp, x, y, bias, res, w, status, s);
+      case 2: return launch_cfg<BN, SPLIT3, 2, true>(st, mp, x, y, bias, res, w, status, s);
+      default: return launch_cfg<BN, SPLIT3, 1, true>(st, mp, x, y, bias, res, w, status, s);
     }
   }
   switch (st.amode) {
-    case 4: return launch_cfg<BN, SPLIT3, 4, false>(st, mp, x, y, bias, res, status, s);
-    case 3: return launch_cfg<BN, SPLIT3, 3, false>(st, mp, x, y, bias, res, status, s);
-    case 2: return launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, status, s);
-    default: return launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, status, s);
+    case 4: return launch_cfg<BN, SPLIT3, 4, false>(st, mp, x, y, bias, res, w, status, s);
+    case 3: return launch_cfg<BN, SPLIT3, 3, false>(st, mp, x, y, bias, res, w, status, s);
+    case 2: return launch_cfg<BN, SPLIT3, 2, false>(st, mp, x, y, bias, res, w, status, s);
+    default: return launch_cfg<BN, SPLIT3, 1, false>(st, mp, x, y, bias, res, w, status, s);
   }
 }
 
@@ -978,6 +1124,28 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   if (ok && st->amode != 1) ok = encode_a(*st, &st->amap, x_dev);
   if (ok && st->epi_tma) ok = encode_y(*st, &st->ymap, y_dev);
   if (ok && tp.res_tma) ok = encode_y(*st, &st->rmap, r_dev);  // same geometry as the output
+  // Stream-K for the tiles past the last full wave when that shortens the
+  // critical path (each CTA gets an even share of their K steps; a tile
+  // split across CTAs is finished by the last epilogue warp to arrive).
+  // 3xTF32 only: measured on B200, TF32 main loops are short enough that
+  // writing and re-reading the partial tiles costs more than it saves.
+  tp.dp_tiles = tp.tiles;
+  tp.sk_units = 0;
+  if (ok && st->split3 && !st->pair && !getenv("SPKV2_TC_NO_STREAMK")) {
+    const int64_t nk = tp.num_kb, rounds = tp.tiles / sms, tail = tp.tiles % sms;
+    const double dp_steps = double(rounds + (tail ? 1 : 0)) * nk;
+    const double sk_share = double(tail) * nk / sms;  // K steps per CTA for the tail
+    const double sk_steps = double(rounds) * nk + ceil(sk_share) + 4;  // + fix-up, in K steps
+    if (tail > 0 && sk_share >= 2 && sk_steps < 0.9 * dp_steps) {
+      tp.dp_tiles = rounds * sms;
+      tp.sk_units = tail * nk;
+      st->grid = sms;
+      st->sk_cnt_bytes = size_t(tail) * kEpiWarps * sizeof(int);
+      st->sk_cnt = static_cast<int *>(device_alloc(st->sk_cnt_bytes));
+      ok = st->sk_cnt && cudaMemsetAsync(st->sk_cnt, 0, st->sk_cnt_bytes, s) == cudaSuccess;
+      st->sk_ws_bytes = size_t(sms) * 2 * size_t(bn) * kBM * sizeof(float);
+    }
+  }
   st->rmap_base = r_dev;
   st->amap_base = x_dev;
   st->ymap_base = y_dev;
@@ -992,11 +1160,11 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   p.tc_block_n = bn;
   p.tc_kpad = tp.Kpad;
   st->set_attr_only = true;
-  rc = conv_tc_launch(p, nullptr, nullptr, nullptr, nullptr, s);
+  rc = conv_tc_launch(p, nullptr, nullptr, nullptr, nullptr, s, nullptr);
   st->set_attr_only = false;
   if (rc) return rc;
-  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + (st->pair ? "_pair" : "") + "_bn" +
-              std::to_string(bn) +
+  p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + (st->pair ? "_pair" : "") +
+              (tp.sk_units ? "_sk" : "") + "_bn" + std::to_string(bn) +
               (st->amode == 4 ? "_im2col4" : st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
               (st->packed_rows ? "_rowpack" : st->staged_x ? "_relayout" : "");
   return 0;
@@ -1009,8 +1177,20 @@ int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const
 
 void conv_tc_release(void *state) { delete static_cast<TcState *>(state); }
 
-int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s) {
+size_t conv_tc_sk_workspace_bytes(const ConvPlan &p) {
+  return p.tc_state ? static_cast<const TcState *>(p.tc_state)->sk_ws_bytes : 0;
+}
+
+void *conv_tc_sk_counters(const ConvPlan &p, size_t *bytes) {
+  const TcState *st = static_cast<const TcState *>(p.tc_state);
+  *bytes = st ? st->sk_cnt_bytes : 0;
+  return st ? st->sk_cnt : nullptr;
+}
+
+int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s,
+                   float *sk_ws) {
   const TcState &st = *static_cast<const TcState *>(p.tc_state);
+  if (st.sk_ws_bytes && !sk_ws && !st.set_attr_only) return SPKV2_ERR_UNSUPPORTED;  // stream-K needs its workspace
   const float *xf = static_cast<const float *>(x);
   if (st.staged_x && !st.set_attr_only) {
     const ConvGeo &o = st.src;
@@ -1041,16 +1221,16 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
   }
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_modes<32, true>(st, mp, xf, yf, bias, rf, status, s);
-      case 64: return launch_modes<64, true>(st, mp, xf, yf, bias, rf, status, s);
-      default: return launch_modes<128, true>(st, mp, xf, yf, bias, rf, status, s);
+      case 32: return launch_modes<32, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+      case 64: return launch_modes<64, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+      default: return launch_modes<128, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
     }
   }
   switch (st.bn) {
-    case 32: return launch_modes<32, false>(st, mp, xf, yf, bias, rf, status, s);
-    case 64: return launch_modes<64, false>(st, mp, xf, yf, bias, rf, status, s);
-    case 256: return launch_modes<256, false>(st, mp, xf, yf, bias, rf, status, s);
-    default: return launch_modes<128, false>(st, mp, xf, yf, bias, rf, status, s);
+    case 32: return launch_modes<32, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+    case 64: return launch_modes<64, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+    case 256: return launch_modes<256, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+    default: return launch_modes<128, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
   }
 }
 

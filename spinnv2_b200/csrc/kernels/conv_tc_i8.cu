@@ -340,33 +340,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc =
           (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-      uint32_t it = 0;
-      int ti = 0;
-      bool ok = true;
-      for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x, ++ti) {
-        const int ab = ti & 1;
-        ok = mbar_wait(&acce_bar[ab], ((ti >> 1) & 1) ^ 1, &abort_flag, status, 7);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t dtm = tmem + uint32_t(ab * BN);
-        for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          ok = mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3);
-          if (ok && AMODE == 1) ok = mbar_wait(&full_bar[s], ph, &abort_flag, status, 3);
-          if (!ok) break;
+      // One flat loop over this CTA's K steps (all its tiles) with the stage,
+      // K-step and buffer positions kept as counters, so the issuing thread
+      // spends little time between MMA batches.
+      const int64_t my_tiles =
+          int64_t(blockIdx.x) < tp.tiles ? (tp.tiles - 1 - int64_t(blockIdx.x)) / int64_t(gridDim.x) + 1 : 0;
+      const uint32_t total = uint32_t(my_tiles) * uint32_t(tp.num_kb);
+      const int num_kb = tp.num_kb;
+      int ti = 0;                 // tiles handed to the epilogue
+      uint32_t ab = 0, abph = 0;  // accumulator buffer and its phase parity
+      uint32_t dtm = tmem;
+      int kb = 0, s = 0;
+      uint32_t ph = 0;
+      for (uint32_t it = 0; it < total; ++it) {
+        if (kb == 0) {
+          if (!mbar_wait(&acce_bar[ab], abph ^ 1, &abort_flag, status, 7)) break;
           tc_fence_after();
-          uint8_t *a_st = smem + s * STAGE;
-          const uint64_t da = smem_desc(a_st), db = smem_desc(a_st + kABytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t step = uint64_t(kk * 32) >> 4;  // 32 int8 = 32 bytes along K
-            mma_i8(dtm, da + step, db + step, idesc, (kb == 0 && kk == 0) ? 0u : 1u);
-          }
-          mma_commit(&empty_bar[s]);
+          dtm = tmem + ab * uint32_t(BN);
         }
-        if (!ok) break;
-        mma_commit(&accf_bar[ab]);
+        if (!mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3)) break;
+        if (AMODE == 1 && !mbar_wait(&full_bar[s], ph, &abort_flag, status, 3)) break;
+        tc_fence_after();
+        uint8_t *a_st = smem + s * STAGE;
+        const uint64_t da = smem_desc(a_st), db = smem_desc(a_st + kABytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t step = uint64_t(kk * 32) >> 4;  // 32 int8 = 32 bytes along K
+          mma_i8(dtm, da + step, db + step, idesc, (kb | kk) ? 1u : 0u);
+        }
+        mma_commit(&empty_bar[s]);
+        if (++kb == num_kb) {
+          mma_commit(&accf_bar[ab]);
+          ++ti;
+          kb = 0;
+          ab ^= 1u;
+          if (ab == 0) abph ^= 1u;
+        }
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       // Every issued MMA must finish before TMEM is freed (also on abort).
       if (ti > 0) {

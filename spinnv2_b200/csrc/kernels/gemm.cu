@@ -225,7 +225,8 @@ int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
       c->math = math;
       c->bias_f = g.has_bias ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
       if (g.has_bias && elem_count(ctx->tensors[node->inputs[2]].record) != size_t(p->N)) g.has_bias = 0;
-      const int trc = conv_tc_prepare_ex(*c, tb.data, ta.data, ty.data, true, ctx->stream);
+      int trc = conv_tc_prepare_ex(*c, tb.data, ta.data, ty.data, true, ctx->stream);
+      if (trc == 0) trc = conv_tc_attach(ctx, *c);
       if (trc == 0) {
         p->tc = c;
         p->launches = c->launches;
@@ -253,7 +254,7 @@ int gemm_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   const float *A = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
   const float *B = reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data);
   const float *bias = node->input_count > 2 ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
-  if (p->tc) return conv_tc_launch(*p->tc, A, Y, nullptr, ctx->d_status, ctx->stream);
+  if (p->tc) return conv_tc_launch(*p->tc, A, Y, nullptr, ctx->d_status, ctx->stream, ctx->d_sk_ws);
   if (p->partials) {
     const int kpb = int(ceil_div(p->K, p->ksplit));
     dim3 grid(unsigned(ceil_div(p->N, 32)), unsigned(p->ksplit));

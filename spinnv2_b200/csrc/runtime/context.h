@@ -87,6 +87,11 @@ struct Spkv2Context {
   int math_mode = SPKV2_CUDA_MATH_SPEC;
   int graph_mode = 1;
   int *d_status = nullptr;  // device-side status word written by bounded waits
+  // Stream-K workspace shared by the tcgen05 convs (grown at prepare; they
+  // run in stream order) and the arrival counters of each plan that uses it.
+  float *d_sk_ws = nullptr;
+  size_t sk_ws_bytes = 0;
+  std::vector<std::pair<void *, size_t>> sk_counters;
   int last_device_code = 0; // code of the last bounded wait that gave up
 
   // ---- per-node cache (reference context.h:46-48) ----

@@ -146,6 +146,7 @@ void release_device_state(Spkv2Context *ctx) {
   if (ctx->graph) cudaGraphDestroy(ctx->graph);
   ctx->graph_exec = nullptr;
   ctx->graph = nullptr;
+  ctx->sk_counters.clear();  // owned by the plans released below
   for (size_t i = 0; i < ctx->node_cache.size(); ++i) {
     if (!ctx->node_cache[i]) continue;
     if (ctx->node_cache_dtors[i])
@@ -163,6 +164,9 @@ void release_device_state(Spkv2Context *ctx) {
   if (ctx->owns_scratch) device_free(ctx->d_scratch);
   device_free(ctx->d_weights);
   device_free(ctx->d_status);
+  device_free(ctx->d_sk_ws);
+  ctx->d_sk_ws = nullptr;
+  ctx->sk_ws_bytes = 0;
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   ctx->d_arena = ctx->d_scratch = ctx->d_weights = nullptr;
   ctx->d_status = nullptr;
@@ -367,6 +371,8 @@ int take_device_status(Spkv2Context *ctx) {
   if (st != 0) {
     ctx->last_device_code = st;
     cudaMemset(ctx->d_status, 0, sizeof(int));
+    // A launch that gave up mid-way may leave stream-K arrival counts behind.
+    for (const auto &c : ctx->sk_counters) cudaMemset(c.first, 0, c.second);
     return SPKV2_ERR_DEVICE_STATUS;
   }
   return 0;

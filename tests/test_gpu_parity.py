@@ -183,3 +183,69 @@ def test_sweep_batch32_on_cta_pairs_matches_reference(gpu, case, math, monkeypat
         np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
     else:
         assert float(np.max(np.abs(out[0] - ref))) < 2e-2 * float(np.max(np.abs(ref)))
+
+
+def _tail_tolerance(out, ref, math):
+    if math == "3xtf32":
+        np.testing.assert_allclose(out, ref, atol=ATOL, rtol=RTOL)
+    else:
+        assert float(np.max(np.abs(out - ref))) < 2e-2 * float(np.max(np.abs(ref)))
+
+
+@pytest.mark.parametrize("case", ["conv3x3_256_14", "conv3x3_512_7", "conv1x1_1024_256_14"])
+@pytest.mark.parametrize("math", ["3xtf32"])
+def test_stream_k_tail_matches_reference_and_repeats_bit_exact(gpu, case, math):
+    """Batch 32 leaves fewer tiles than SMs, so the tiles' K steps are spread
+    evenly over all CTAs (two to four segments per tile; 3xTF32 math, the
+    mode that uses stream-K).  The partials are
+    added in segment order by whichever epilogue warp arrives last, so a
+    second context reproduces the output bit for bit."""
+    from spinnv2_b200.runtime import MATH_3XTF32, MATH_TF32
+    from spinnv2_b200.spk import read_spk
+
+    mode = MATH_3XTF32 if math == "3xtf32" else MATH_TF32
+    spk = compile_pair(case, 32)
+    x = seeded_input(read_spk(spk["cuda_b200"]).inputs[0].shape)
+    ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
+    out, variants = _run_gpu(spk["cuda_b200"], [x], math_mode=mode)
+    assert any("_sk_" in v for v in variants), variants
+    _tail_tolerance(out[0], ref, math)
+    again, _ = _run_gpu(spk["cuda_b200"], [x], math_mode=mode)
+    np.testing.assert_array_equal(out[0], again[0])
+
+
+def test_stream_k_off_agrees_with_stream_k(gpu, monkeypatch):
+    """SPKV2_TC_NO_STREAMK=1 keeps whole tiles per CTA: same result up to the
+    order of the fp32 adds."""
+    from spinnv2_b200.spk import read_spk
+
+    spk = compile_pair("conv3x3_512_7", 32)
+    x = seeded_input(read_spk(spk["cuda_b200"]).inputs[0].shape)
+    on, v_on = _run_gpu(spk["cuda_b200"], [x])
+    monkeypatch.setenv("SPKV2_TC_NO_STREAMK", "1")
+    off, v_off = _run_gpu(spk["cuda_b200"], [x])
+    assert any("_sk_" in v for v in v_on) and not any("_sk_" in v for v in v_off), (v_on, v_off)
+    np.testing.assert_allclose(on[0], off[0], atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("math", ["3xtf32"])
+def test_stream_k_with_residual_and_relu_matches_reference(gpu, math):
+    """Residual add + Relu fused into a stream-K conv: the warp that finishes
+    a split tile loads the residual tile and applies the activation."""
+    import copy
+
+    from spinnv2_b200.compiler import builders, pipeline
+    from spinnv2_b200.runtime import MATH_3XTF32, MATH_TF32
+
+    net = builders._Net("sk_residual", 3)
+    x_id = net.b.input("input", [32, 256, 14, 14])
+    y = net.conv(x_id, 256, 3, s=1, p=1, bias=True)
+    net.b.mark_output(net.relu(net.add(y, x_id)))
+    graph = pipeline.fuse(net.b.graph)
+    spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+    spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+    x = seeded_input((32, 256, 14, 14), seed=5)
+    ref = reference_outputs(spk_cpu, [x])[0]
+    out, variants = _run_gpu(spk_gpu, [x], math_mode=MATH_3XTF32 if math == "3xtf32" else MATH_TF32)
+    assert any("_sk_" in v for v in variants), variants
+    _tail_tolerance(out[0], ref, math)
