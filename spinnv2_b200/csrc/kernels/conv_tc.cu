@@ -100,13 +100,16 @@ struct Seg {
 // The static schedule every role of a CTA walks in the same order: whole
 // tiles tile0, tile0 + tstep, ... below dp_tiles, then this CTA's contiguous
 // share [u0, u1) of the remaining tiles' K steps (unit u = K step u % nk of
-// stream-K tile u / nk), cut at tile boundaries.
+// stream-K tile u / nk), cut at tile boundaries.  SK = false compiles the
+// whole-tile schedule only (kernels that never use stream-K).
+template <bool SK>
 struct WorkIter {
   int64_t t, tstep, dp_tiles;
   int64_t u, u0, u1, U;
   int nk, G, b;
   __device__ WorkIter(const TcParams &tp, int64_t tile0, int64_t step, int cta, int grid)
-      : t(tile0), tstep(step), dp_tiles(tp.dp_tiles), U(tp.sk_units), nk(tp.num_kb), G(grid), b(cta) {
+      : t(tile0), tstep(step), dp_tiles(SK ? tp.dp_tiles : tp.tiles), U(SK ? tp.sk_units : 0), nk(tp.num_kb),
+        G(grid), b(cta) {
     u0 = U ? int64_t(b) * U / G : 0;
     u1 = U ? int64_t(b + 1) * U / G : 0;
     u = u0;
@@ -130,7 +133,7 @@ struct WorkIter {
       t += tstep;
       return true;
     }
-    if (u >= u1) return false;
+    if (!SK || u >= u1) return false;
     const int64_t tt = u / nk;
     s.tt = int(tt);
     s.tile = dp_tiles + tt;
@@ -211,6 +214,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int TILE_ROWS = PAIR ? 2 * kBM : kBM;
   constexpr int B_BYTES = BROWS * 128;
   constexpr int STAGE = stage_bytes(BROWS, SPLIT3);
+  // Stream-K tails exist only in single-CTA 3xTF32 kernels.
+  constexpr bool SK = SPLIT3 && !PAIR;
+  using Iter = WorkIter<SK>;
   constexpr int B_OFF = (SPLIT3 ? 2 : 1) * kABytes;  // B hi within a stage
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
   // for gathers (copied from the landing ring), for 3xTF32 (low parts) and,
@@ -302,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);  // this warp's TMEM lanes
     const uint32_t tsum = trow + uint32_t(Acc::sum_col);            // promoted sums (3xTF32)
     float4 *const ws4 = reinterpret_cast<float4 *>(sk_ws);
-    WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+    Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
     Seg sg;
     while (wi.next(sg)) {
       const int64_t t = sg.tile;
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       bool finish = true;
       int64_t blo = 0;
-      if (sg.nseg > 1) {
+      if (SK && sg.nseg > 1) {
         // Stream-K segment: park this warp's part of the tile in the CTA's
         // workspace slot ([chunk][4-column group][row] float4s, so a warp's
         // stores are contiguous) and count the arrival; the segment's last
@@ -521,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int cb = col0; cb < col0 + ncol; cb += 32) {
         issue_res(cb);
         uint32_t acc[32];
-        if (sg.nseg == 1) {
+        if (!SK || sg.nseg == 1) {
           read_acc(cb, acc);
         } else {
 #pragma unroll
@@ -550,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     if constexpr (AMODE != 1) {
       if (RELAY) {  // 3xTF32: the low parts of the TMA-landed tile; pairs: tell the leader
-        const uint32_t total = WorkIter(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x)).total_steps();
+        const uint32_t total = Iter(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x)).total_steps();
         for (; it < total; ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5)) break;
@@ -574,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&full_bar[s]);
         return true;
       };
-      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+      Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
       Seg sg;
       while (ok && wi.next(sg)) {
         const int64_t m0 = (sg.tile / tp.n_tiles) * kBM;
@@ -626,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE != 1 ? kABytes : 0);
       uint32_t it = 0;
       bool ok = true;
-      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
+      Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
       Seg sg;
       while (ok && wi.next(sg)) {
         const int64_t t = sg.tile;
@@ -641,8 +647,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           bh = int(q % g.OH) * g.sh - g.ph;
           bn = int(q / g.OH);
         }
+        // AMODE 3 position of K step kb (C % 32 == 0: one filter tap per K
+        // step), advanced incrementally so no division sits between the
+        // stage becoming free and the loads.
+        int c0 = 0, sx = 0, r = 0;
+        if (AMODE == 3) {
+          const int k0 = sg.kb0 * kBK, tap = k0 / g.C;
+          c0 = k0 - tap * g.C;
+          r = tap / g.KW;
+          sx = tap - r * g.KW;
+        }
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
+          const uint16_t woff = uint16_t(sx * g.dw), hoff = uint16_t(r * g.dh);
           ok = wait_any(&empty_bar[s], ((it / STAGES) & 1) ^ 1, 2);
           if (!ok) break;
           uint8_t *a_hi = smem + s * STAGE;
@@ -652,10 +669,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + brow, &raw_bar[s]);
           if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
           if (AMODE == 3) {
-            const int k0 = kb * kBK;
-            const int tap = k0 / g.C, c0 = k0 - tap * g.C;  // C % 32 == 0: one tap per K step
-            const int r = tap / g.KW, sx = tap - r * g.KW;
-            tma_load_im2col_4d(a_hi, &amap, c0, bw, bh, bn, uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+            tma_load_im2col_4d(a_hi, &amap, c0, bw, bh, bn, woff, hoff, &raw_bar[s]);
+            if ((c0 += kBK) == g.C) {
+              c0 = 0;
+              if (++sx == g.KW) {
+                sx = 0;
+                ++r;
+              }
+            }
           }
           if (AMODE == 4) {
             // C == 4: eight taps per K step, one 128 pixel x 16 byte column
@@ -682,10 +703,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // segments), with the stage, segment and group positions kept as
       // counters: the issuing thread does as little as possible between its
       // MMA batches.
-      WorkIter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
-      Seg sg;
+      // Segment lengths only: whole tiles (nk steps), then this CTA's
+      // stream-K share cut at tile boundaries (32-bit: units < 2^31).
+      const Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
       const uint32_t total = wi.total_steps();
       const int group = tp.group;
+      const uint32_t nk = uint32_t(tp.num_kb);
+      uint32_t dp_left = total - uint32_t(wi.u1 - wi.u0);  // steps of whole tiles
+      uint32_t u = uint32_t(wi.u0);
+      const uint32_t uend = uint32_t(wi.u1);
       int seg_left = 0;  // K steps left in the current segment
       uint32_t gi = 0;            // accumulator hand-offs issued (one per K group)
       uint32_t ab = 0, abph = 0;  // accumulator buffer and its phase parity
@@ -695,8 +721,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;         // stage phase parity
       for (uint32_t it = 0; it < total; ++it) {
         if (seg_left == 0) {
-          if (!wi.next(sg)) break;
-          seg_left = sg.kb1 - sg.kb0;
+          if (dp_left > 0) {
+            seg_left = int(nk);
+            dp_left -= nk;
+          } else {
+            const uint32_t r = nk - u % nk;
+            seg_left = int(r < uend - u ? r : uend - u);
+            u += uint32_t(seg_left);
+          }
         }
         if (gk == 0) {
           if (!wait_any(&acce_bar[ab], abph ^ 1, 7)) break;
