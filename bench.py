@@ -53,32 +53,75 @@ def peaks() -> tuple[dict, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and clock-event reasons sampled DURING the timed region: NVML
+    polled every 10 ms from a thread (the device found by the UUID CUDA
+    reports, so it is the GPU this rank runs on even under
+    CUDA_VISIBLE_DEVICES), else `nvidia-smi -lms 200`.  Read-only."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int) -> None:
-        self.gpu = gpu_index
+    def __init__(self, cuda_device: int, period_s: float = 0.01) -> None:
+        self.dev = cuda_device
+        self.period = period_s
         self.proc = None
+        self.nvml = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self.stop_evt = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
 
     def start(self) -> None:
         try:
+            self.nvml, handle = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, args=(handle,), daemon=True)
+            self.thread.start()
+            return
+        except Exception:  # noqa: BLE001 - no NVML binding or device: fall back to nvidia-smi
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                          "-lms", "200", "-i", str(self.dev)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
 
+    def _poll(self, handle) -> None:
+        nv = self.nvml
+        while not self.stop_evt.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)),
+                                     float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)),
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+            except Exception:  # noqa: BLE001
+                break
+            self.stop_evt.wait(self.period)
+
     def _read(self) -> None:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            sm = [x[0] for x in self.samples]
+            reasons = {name for _, _, bits in self.samples for name, bit in self.REASONS if bits & bit}
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": max(x[1] for x in self.samples) if sm else None,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 10 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -101,7 +144,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 def conv_flops(pkg, int8_only: bool = False) -> tuple[float, list[int]]:
@@ -336,7 +379,7 @@ def run_gpu_arm(args, group) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)  # ~0.5 s timed at bs64 3xTF32
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="resnet101")

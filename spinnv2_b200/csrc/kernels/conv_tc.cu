@@ -291,6 +291,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_holder;
+  // Everything above touches only this CTA's shared memory and TMEM; the
+  // next layer may start launching now, and this one waits here for the
+  // previous layer's outputs (and for its reads of buffers this one writes).
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp < kEpiWarps) {
     // ------------------------------------------------------------ epilogue
@@ -975,25 +980,8 @@ int launch_cfg(const TcState &st, const Maps &mp, const float *x, float *y, cons
   auto kern = conv_tc_kernel<BN, ps.stages, ps.land, SPLIT3, AMODE, EPI, PAIR>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  if (!PAIR) {
-    kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, sk_ws,
-                                                      st.sk_cnt, status);
-    return cuda_status(cudaGetLastError());
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(st.grid), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = st.smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cuda_status(
-      cudaLaunchKernelEx(&cfg, kern, st.wmap, mp.a, mp.y, mp.r, x, bias, res, y, st.tp, sk_ws, st.sk_cnt, status));
+  return cuda_status(launch_kernel(kern, unsigned(st.grid), kThreads, st.smem, s, PAIR ? 2 : 1, st.wmap, mp.a, mp.y,
+                                   mp.r, x, bias, res, y, st.tp, sk_ws, st.sk_cnt, status));
 }
 
 template <int BN, bool SPLIT3>

@@ -119,6 +119,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_holder;
+  // Shared memory and TMEM only above; the next layer may start launching,
+  // and this one waits here for the previous layer.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp < EPIW) {
     // ------------------------------------------------------------ epilogue
@@ -450,10 +454,9 @@ int launch_cfg(const I8State &st, const Maps &mp, const ConvPlan &p, const void 
   auto kern = conv_i8_kernel<BN, stages_of(BN), AMODE>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  kern<<<unsigned(st.grid), kThreads, st.smem, s>>>(st.wmap, mp.a, mp.y, mp.r, static_cast<const int8_t *>(x),
-                                                    p.bias_q, p.scale_m, static_cast<const int8_t *>(res), y, st.tp,
-                                                    status);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_kernel(kern, unsigned(st.grid), kThreads, st.smem, s, 1, st.wmap, mp.a, mp.y, mp.r,
+                                   static_cast<const int8_t *>(x), p.bias_q, p.scale_m,
+                                   static_cast<const int8_t *>(res), y, st.tp, status));
 }
 
 template <int BN>

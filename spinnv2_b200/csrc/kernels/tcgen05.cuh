@@ -6,7 +6,9 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 namespace spkv2 {
 namespace tc {
@@ -67,6 +69,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
                                           int code) {
   return mbar_wait_limit(bar, parity, abort_flag, status, code, kWaitCycles);
 }
+
+// Programmatic dependent launch: let the stream's next kernel begin
+// launching, and wait until the previous kernel has completed with its
+// writes visible.  Both are no-ops when the launch did not allow it.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -357,6 +367,43 @@ inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint
   return encode_im2col_fn()(map, dtype, 4, const_cast<void *>(base), dims, strides, lower, upper, channels, pixels,
                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- launches
+// Launch with programmatic stream serialisation (the kernel's prologue may
+// overlap the previous kernel's tail; the kernel calls pdl_wait() before its
+// first global access) unless SPKV2_NO_PDL is set; optionally as clusters of
+// `cluster` CTAs.
+inline bool pdl_enabled() {
+  static const bool on = getenv("SPKV2_NO_PDL") == nullptr;
+  return on;
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_kernel(void (*kern)(Params...), unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                          int cluster, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = unsigned(cluster);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
 }
 
 }  // namespace tc
