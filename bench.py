@@ -259,6 +259,96 @@ def run_reference_arm(args, group) -> None:
     print(json.dumps(line), flush=True)
 
 
+def latency_bs1(args, local: int, math_mode: int) -> dict:
+    """bs1 latency through the public API, the reference's `spkv2_bench`
+    protocol: warm-up runs, then `runs` timed spkv2_run calls, each copying the
+    input from pinned host memory, replaying the captured graph and copying
+    the output back (spkv2_run synchronises); p50/p90 of the per-run wall
+    time."""
+    import torch
+
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import Runtime
+
+    spk1 = pipeline.compile_config(args.config, 1, targets=("cuda_b200",), seed=0, int8=args.int8)["cuda_b200"]
+    rt = Runtime(spk1, device=local, math_mode=math_mode, graph=True)
+    in_t, out_t = rt.package.inputs[0], rt.package.outputs[0]
+    x1 = np.random.default_rng(2).standard_normal(in_t.shape, dtype=np.float32)
+    h_in = torch.from_numpy(x1).pin_memory()
+    h_out = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory()
+    rt.bind_input(0, h_in.data_ptr())
+    rt.bind_output(0, h_out.data_ptr())
+    for _ in range(20):
+        rt._check(rt.lib.spkv2_run(rt.ctx), "run")
+    times = []
+    for _ in range(args.latency_runs):
+        t0 = time.perf_counter()
+        rt._check(rt.lib.spkv2_run(rt.ctx), "run")
+        times.append(time.perf_counter() - t0)
+    rt.close()
+    times.sort()
+    return {"p50_ms": 1000.0 * statistics.median(times), "p90_ms": 1000.0 * times[int(0.9 * (len(times) - 1))],
+            "min_ms": 1000.0 * times[0], "runs": len(times), "batch": 1,
+            "path": "spkv2_run: pinned host input -> graph replay -> pinned host output"}
+
+
+def run_memory_bound(args, group) -> None:
+    """Memory-bound ops (every node that is not a Conv/Gemm) of the
+    YOLOv10n-style config at `--mb-batch`: per node, algorithmic bytes (every
+    input and output tensor read/written once) / device time (per-node CUDA
+    events, mean of 5 passes), aggregated per op type, against the measured
+    HBM copy bandwidth.  Rank 0 prints one JSON line."""
+    if group.rank != 0:
+        return
+    import torch
+
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import Runtime
+
+    torch.cuda.set_device(group.local_rank)
+    spk = pipeline.compile_config("yolo_style", args.mb_batch, targets=("cuda_b200",), seed=0)["cuda_b200"]
+    with Runtime(spk, device=group.local_rank, graph=False) as rt:
+        pkg = rt.package
+        x = np.random.default_rng(3).random(pkg.inputs[0].shape, dtype=np.float32)
+        rt.set_input(0, x)
+        rt.run()
+        ms = np.mean([rt.profile_nodes() for _ in range(5)], axis=0)
+        per_op: dict[str, list[float]] = {}
+        nodes = []
+        for n in pkg.nodes:
+            if n.op_type in ("Conv", "Gemm"):
+                continue
+            nbytes = 0
+            for t in list(n.inputs) + list(n.outputs):
+                if t >= 0 and pkg.tensors[t].role_name != "weight":
+                    ten = pkg.tensors[t]
+                    nbytes += int(np.prod(ten.shape)) * np.dtype(ten.np_dtype).itemsize
+            if ms[n.id] <= 0:
+                continue
+            acc = per_op.setdefault(n.op_type, [0, 0.0, 0.0])
+            acc[0] += 1
+            acc[1] += nbytes
+            acc[2] += float(ms[n.id])
+            nodes.append((nbytes / (ms[n.id] * 1e-3) / 1e9, n.op_type, n.id, nbytes, float(ms[n.id]), rt.node_variant(n.id)))
+    pk, basis = peaks()
+    tot_b = sum(v[1] for v in per_op.values())
+    tot_ms = sum(v[2] for v in per_op.values())
+    big = [r for r in nodes if r[3] >= 64 * 2**20]  # tensors well above L2
+    line = {
+        "metric": "memory-bound op GB/s (YOLOv10n-style, non-conv nodes)", "unit": "GB/s",
+        "value": tot_b / (tot_ms * 1e-3) / 1e9, "higher_is_better": True, "n_gpus": 1, "data": "synthetic",
+        "config": {"workload": f"yolo_style 640x640 fp32 forward, batch {args.mb_batch}", "nodes": len(nodes)},
+        "peak": {"value": pk["hbm_gbs"], "unit": "GB/s", "basis": f"HBM copy, {basis}"},
+        "frac": tot_b / (tot_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+        "per_op": {k: {"nodes": v[0], "bytes": int(v[1]), "ms": v[2], "gbs": v[1] / (v[2] * 1e-3) / 1e9}
+                   for k, v in sorted(per_op.items(), key=lambda kv: -kv[1][2])},
+        "nodes_over_64MiB_gbs": (sum(r[3] for r in big) / (sum(r[4] for r in big) * 1e-3) / 1e9) if big else None,
+        "top_nodes": [{"op": r[1], "node": r[2], "bytes": r[3], "ms": r[4], "gbs": r[0], "variant": r[5]}
+                      for r in sorted(nodes, key=lambda r: -r[4])[:12]],
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_gpu_arm(args, group) -> None:
     import torch
 
@@ -343,6 +433,7 @@ def run_gpu_arm(args, group) -> None:
     e2e_value = world * args.batch * args.steps / e2e_s
     launches = rt.launches_per_run() * args.steps
     rt2.close()
+    lat = latency_bs1(args, local, math_mode)  # every rank, so the ranks stay in step
 
     if rank == 0:
         line = {
@@ -359,6 +450,7 @@ def run_gpu_arm(args, group) -> None:
             "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(np.prod(out_t.shape) * 4)},
             "gpu_launches": int(launches),
+            "latency_bs1": lat,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": peak_unit,
                          "frac": achieved / peak, "traffic": traffic,
                          "algorithmic_bytes_per_step": alg_bytes,
@@ -371,7 +463,8 @@ def run_gpu_arm(args, group) -> None:
             cb = timer(args.config, 1, seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": cb["value"], "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
                                     "kind": "port" if args.int8 else "reference",
-                                    "sample": f"batch 1, {cb['steps']} runs over ~{args.cpu_seconds:.0f} s"}
+                                    "sample": f"batch 1, {cb['steps']} runs over ~{args.cpu_seconds:.0f} s",
+                                    "p50_ms_bs1": 1000.0 * cb["step_s"]}
         print(json.dumps(line), flush=True)
     rt.close()
 
@@ -388,6 +481,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--reference-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--latency-runs", type=int, default=200, help="timed spkv2_run calls for the bs1 latency")
+    ap.add_argument("--memory-bound", action="store_true", help="GB/s of the YOLOv10n-style non-conv ops instead")
+    ap.add_argument("--mb-batch", type=int, default=64)
     ap.add_argument("--int8", action="store_true", help="INT8 quantised network (use with --config resnet50)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -403,6 +499,8 @@ def main() -> None:
     try:
         if args.impl == "reference":
             run_reference_arm(args, group)
+        elif args.memory_bound:
+            run_memory_bound(args, group)
         else:
             run_gpu_arm(args, group)
     finally:

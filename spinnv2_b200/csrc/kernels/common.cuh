@@ -94,6 +94,28 @@ inline IterSpace<NOPS> make_iter(const View &out, const View *ins, int nin) {
 
 __host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Division by a run-time-invariant 32-bit divisor d >= 1 as a multiply-high
+// and shifts (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", 1994, round-up variant): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (t + ((n - t) >> 1)) >> (l - 1)
+// where t = mulhi(m, n), for every 32-bit n; d = 1 is handled apart.
+struct FastDiv {
+  uint32_t d = 1, m = 0, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div) {
+    if (d <= 1) return;
+    uint32_t l = 0;
+    while ((uint64_t(1) << l) < d) ++l;
+    m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+    s = l - 1;
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    if (d == 1) return n;
+    const uint32_t t = __umulhi(m, n);
+    return (t + ((n - t) >> 1)) >> s;
+  }
+};
+
 inline int grid_for(int64_t n, int threads) {
   int64_t blocks = ceil_div(n, threads);
   // Grid-stride beyond 148 SMs x 32 resident blocks.

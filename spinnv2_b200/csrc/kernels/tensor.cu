@@ -42,7 +42,52 @@ struct PartPlan : NodePlan {
   int vec = 1;
   int esize = 4;
   int64_t total = 0;
+  // Dense fast path: big and every part contiguous in the big tensor's
+  // physical order, so each of `rows` outer rows of the big tensor is the
+  // parts' rows side by side: part k owns elements [seg[k], seg[k+1]) of a
+  // big row of seg[parts] elements (all in 16-byte vectors).
+  bool rows_path = false;
+  uint32_t rows = 0;
+  uint32_t seg[kMaxParts + 1] = {};
 };
+
+// Segmented row copy of 16-byte vectors (32-bit indices; the plan checks the
+// sizes): vector v of the big tensor is in outer row v / row_vecs, at column
+// c = v % row_vecs, which part k holds at column c - seg[k] of its own row of
+// seg[k+1] - seg[k] vectors.  Four grid-strided vectors per thread per
+// iteration keep four independent 16-byte loads in flight.
+struct RowSegs {
+  FastDiv row_vecs;
+  uint32_t seg[kMaxParts + 1];  // in vectors
+  int parts;
+  void *ptr[kMaxParts];
+};
+
+template <bool GATHER>
+__global__ void __launch_bounds__(256) rows_kernel(uint4 *__restrict__ big, RowSegs r, uint32_t total) {
+  constexpr int U = 4;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < total; v0 += U * stride) {
+    uint4 *src[U], *dst[U];
+    uint4 val[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t v = v0 + u * stride;
+      const uint32_t vv = v < total ? v : v0;  // lanes past the end redo v0 (same value, same place)
+      const uint32_t row = r.row_vecs.div(vv), c = vv - row * r.row_vecs.d;
+      int k = 0;
+#pragma unroll
+      for (int j = 1; j < kMaxParts; ++j) k += (j < r.parts && c >= r.seg[j]) ? 1 : 0;
+      uint4 *part = static_cast<uint4 *>(r.ptr[k]) + size_t(row) * (r.seg[k + 1] - r.seg[k]) + (c - r.seg[k]);
+      src[u] = GATHER ? part : big + vv;
+      dst[u] = GATHER ? big + vv : part;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) val[u] = *src[u];
+#pragma unroll
+    for (int u = 0; u < U; ++u) *dst[u] = val[u];
+  }
+}
 
 // GATHER (Concat): big = output, parts = inputs.  Split: big = input,
 // parts = outputs.
@@ -141,6 +186,38 @@ int prepare_parts(Spkv2Context *ctx, const Spkv2NodeRecord *node, bool concat) {
   p->vec = vec ? 4 : 1;
   p->esize = int(esize);
   p->total = vb.count() / p->vec;
+  // Dense fast path (see PartPlan): every tensor contiguous in the big
+  // tensor's physical order, 16-byte rows segments, 32-bit vector indices.
+  {
+    bool dense = vb.count() * int64_t(esize) / 16 < (int64_t(1) << 31) &&
+                 reinterpret_cast<uintptr_t>(big.data) % 16 == 0;
+    int64_t expect = 1;
+    for (int j = rank - 1; j >= 0; --j) {
+      dense = dense && d.big_stride[j] == expect;
+      expect *= d.dim[j];
+    }
+    int64_t inner = 1, outer = 1;
+    for (int j = d.axis_pos + 1; j < rank; ++j) inner *= d.dim[j];
+    for (int j = 0; j < d.axis_pos; ++j) outer *= d.dim[j];
+    for (int k = 0; k < nparts && dense; ++k) {
+      const int64_t ext = d.begin[k + 1] - d.begin[k];
+      int64_t pe = 1;
+      for (int j = rank - 1; j >= 0; --j) {
+        dense = dense && d.part_stride[k][j] == pe;
+        pe *= j == d.axis_pos ? ext : d.dim[j];
+      }
+      dense = dense && (ext * inner * int64_t(esize)) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(ctx->tensors[concat ? node->inputs[k] : node->outputs[k]].data) % 16 == 0;
+    }
+    if (dense && outer > 0) {
+      p->rows_path = true;
+      p->rows = uint32_t(outer);
+      for (int k = 0; k <= nparts; ++k) p->seg[k] = uint32_t(d.begin[k] * inner * int64_t(esize) / 16);
+      p->variant = concat ? "concat_rows16" : "split_rows16";
+      set_node_plan(ctx, node, p);
+      return 0;
+    }
+  }
   p->variant = vec ? (concat ? "concat_vec4" : "split_vec4") : (concat ? "concat" : "split");
   set_node_plan(ctx, node, p);
   return 0;
@@ -154,6 +231,18 @@ int run_parts(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
   PartDesc d = p->d;
   for (int k = 0; k < d.parts; ++k) d.ptr[k] = ctx->tensors[GATHER ? node->inputs[k] : node->outputs[k]].data;
   void *big = ctx->tensors[GATHER ? node->outputs[0] : node->inputs[0]].data;
+  if (p->rows_path) {
+    RowSegs r;
+    memset(&r, 0, sizeof(r));
+    r.parts = d.parts;
+    r.row_vecs = FastDiv(p->seg[d.parts]);
+    for (int k = 0; k <= d.parts; ++k) r.seg[k] = p->seg[k];
+    for (int k = 0; k < d.parts; ++k) r.ptr[k] = d.ptr[k];
+    const uint32_t total = p->rows * r.row_vecs.d;
+    if (total == 0) return 0;
+    rows_kernel<GATHER><<<grid_for(total, 256), 256, 0, ctx->stream>>>(static_cast<uint4 *>(big), r, total);
+    return cuda_status(cudaGetLastError());
+  }
   const int g = grid_for(p->total, 256);
   if (p->esize == 1) {
     if (p->vec == 4)

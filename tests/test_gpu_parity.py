@@ -249,3 +249,32 @@ def test_stream_k_with_residual_and_relu_matches_reference(gpu, math):
     out, variants = _run_gpu(spk_gpu, [x], math_mode=MATH_3XTF32 if math == "3xtf32" else MATH_TF32)
     assert any("_sk_" in v for v in variants), variants
     _tail_tolerance(out[0], ref, math)
+
+
+@pytest.mark.parametrize("widths", [(8, 12, 4), (6, 10), (16, 16, 16, 16)])
+def test_split_and_concat_match_reference(gpu, widths):
+    """Channel Split and Concat between convs (NHWC on the device): 16-byte
+    row segments take the row-copy kernel, odd channel counts the generic
+    strided one; results are copies, so they must match exactly."""
+    import copy
+
+    from spinnv2_b200.compiler import builders, pipeline
+
+    net = builders._Net("split_concat", 4)
+    b = net.b
+    total = sum(widths)
+    x = b.input("input", [3, 8, 9, 11])
+    y = net.conv(x, total, 1, s=1, p=0, bias=True)
+    parts = list(b.node("Split", [y], [[3, w, 9, 11] for w in widths], {"axis": 1}))
+    parts = [net.conv(t, w, 3, s=1, p=1, bias=True, act="Relu") for t, w in zip(parts, widths)]
+    cat = b.op("Concat", parts[::-1], [3, total, 9, 11], {"axis": 1})
+    b.mark_output(net.conv(cat, 5, 1, s=1, p=0, bias=True))
+    graph = pipeline.fuse(net.b.graph)
+    spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+    spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+    xin = seeded_input((3, 8, 9, 11), seed=9)
+    ref = reference_outputs(spk_cpu, [xin])[0]
+    out, variants = _run_gpu(spk_gpu, [xin])
+    kinds = {v for v in variants if v.startswith(("Split:", "Concat:"))}
+    assert len(kinds) == 2, variants
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
