@@ -292,6 +292,20 @@ int copy_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   const int64_t n = int64_t(elem_count(ty.record));
   const uint32_t *is = tx.record->shape, *os = ty.record->shape;
   const int in_nhwc = tx.layout == kNHWC, out_nhwc = ty.layout == kNHWC;
+  // One side NHWC, the other row-major: the logical (row-major) element
+  // order is shared, so the copy is a [N, H*W, C] <-> [N, C, H*W] transpose of
+  // the NHWC side's dims through shared-memory tiles (both sides coalesced).
+  if (in_nhwc != out_nhwc) {
+    const Spkv2TensorRecord *r = in_nhwc ? tx.record : ty.record;
+    if (r->rank == 4) {
+      const int rc = dtype_size(ty.record->dtype) == 1
+                         ? launch_transpose_hw_c(reinterpret_cast<uint8_t *>(ty.data),
+                                                 reinterpret_cast<const uint8_t *>(tx.data), r, in_nhwc, ctx->stream)
+                         : launch_transpose_hw_c(reinterpret_cast<uint32_t *>(ty.data),
+                                                 reinterpret_cast<const uint32_t *>(tx.data), r, in_nhwc, ctx->stream);
+      if (rc != SPKV2_ERR_UNSUPPORTED) return rc;
+    }
+  }
   if (dtype_size(ty.record->dtype) == 1) {
     relayout_kernel<uint8_t><<<grid_for(n, 256), 256, 0, ctx->stream>>>(ty.data, tx.data, n, in_nhwc, is[1], is[2],
                                                                         is[3], out_nhwc, os[1], os[2], os[3]);

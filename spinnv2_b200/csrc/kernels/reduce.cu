@@ -57,6 +57,37 @@ __global__ void reduce_kernel(float *__restrict__ y, const float *__restrict__ x
       yo += c * d.keep_ystride[k];
     }
     float acc = IS_MAX ? -INFINITY : 0.0f;
+    if (d.red_rank == 1) {
+      // One reduced axis: a strided walk, four loads in flight; the
+      // accumulation order stays r = 0, 1, 2, ... as in the reference.
+      const int64_t st = d.red_xstride[0];
+      const float *p = x + xb;
+      int64_t r = 0;
+      for (; r + 4 <= red_count; r += 4) {
+        const float v0 = p[r * st], v1 = p[(r + 1) * st], v2 = p[(r + 2) * st], v3 = p[(r + 3) * st];
+        if (IS_MAX) {
+          acc = v0 > acc ? v0 : acc;
+          acc = v1 > acc ? v1 : acc;
+          acc = v2 > acc ? v2 : acc;
+          acc = v3 > acc ? v3 : acc;
+        } else {
+          acc += v0 / d.denom;
+          acc += v1 / d.denom;
+          acc += v2 / d.denom;
+          acc += v3 / d.denom;
+        }
+      }
+      for (; r < red_count; ++r) {
+        const float v = p[r * st];
+        if (IS_MAX) {
+          acc = v > acc ? v : acc;
+        } else {
+          acc += v / d.denom;
+        }
+      }
+      y[yo] = acc;
+      continue;
+    }
     for (int64_t r = 0; r < red_count; ++r) {
       int64_t rr = r, xo = xb;
       for (int k = d.red_rank - 1; k >= 0; --k) {
