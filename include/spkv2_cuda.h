@@ -37,7 +37,7 @@ extern "C" {
 #define SPKV2_ERR_LAUNCH        (-44) /* kernel launch failed */
 #define SPKV2_ERR_NOT_PREPARED  (-45) /* call requires spkv2_prepare first */
 #define SPKV2_ERR_PROTECTION    (-46) /* SPK carries a protection plan (host-only feature) */
-#define SPKV2_ERR_DEVICE_STATUS (-47) /* a kernel reported a bounded-wait timeout */
+#define SPKV2_ERR_DEVICE_STATUS (-47) /* a kernel reported a bounded-wait timeout or a bad index */
 
 /* fp32 Conv/Gemm math modes. */
 #define SPKV2_CUDA_MATH_SPEC   0 /* follow each node's KernelSpec kind (default) */
@@ -100,7 +100,9 @@ const char *spkv2_cuda_status_string(int code);
  * context stays usable.  spkv2_cuda_last_device_code returns the code of the
  * last such timeout (1 A-operand producer, 2 TMA producer, 3 MMA issuer,
  * 4 epilogue, 5/6 operand or residual landing, 7 accumulator hand-off,
- * 9 watchdog probe).
+ * 9 watchdog probe).  Gather and GatherElements use the same word for an
+ * index outside [-dim, dim) after wrapping: the element is written as 0,
+ * nothing outside the input is read, and the code is 10.
  * spkv2_cuda_watchdog_probe (no reference counterpart) exercises that path on
  * purpose: one block waits on an mbarrier that nothing completes, with a
  * limit of wait_us microseconds (1 .. 2,000,000); it returns

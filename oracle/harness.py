@@ -232,7 +232,88 @@ def run_node(pkg: SpkPackage, node, env: dict) -> list[np.ndarray]:
     if op == "Tile":
         reps = [o // i for o, i in zip(outs[0].shape, ins[0].shape)]
         return [np.tile(ins[0], reps)]
+    if op == "MatMul":
+        # reference/mm/matmul.c:3-50: leading dims broadcast, fp32 sums.
+        return [np.matmul(ins[0], ins[1]).astype(np.float32).reshape(outs[0].shape)]
+    if op == "Clip":
+        # reference/activation/clip_leakyrelu.c:5-29: min/max from inputs 1/2.
+        lo = ins[1].reshape(-1)[0] if len(ins) > 1 else np.float32(-np.inf)
+        hi = ins[2].reshape(-1)[0] if len(ins) > 2 else np.float32(np.inf)
+        v = np.where(ins[0] < lo, lo, ins[0])
+        return [np.where(v > hi, hi, v).astype(np.float32)]
+    if op == "LeakyRelu":
+        # reference/activation/clip_leakyrelu.c:31-50: v >= 0 ? v : v * alpha.
+        x = ins[0]
+        return [np.where(x >= 0, x, x * np.float32(a.alpha)).astype(np.float32)]
+    if op == "AveragePool":
+        return [_avgpool(ins[0], a, outs[0].shape)]
+    if op == "GlobalAveragePool":
+        # reference/pool/avgpool.c:49-71: sum * (1 / (H*W)).
+        x = ins[0]
+        inv = np.float32(1) / np.float32(x.shape[2] * x.shape[3])
+        s = np.sum(x, axis=(2, 3), keepdims=True, dtype=np.float32)
+        return [(s * inv).astype(np.float32)]
+    if op == "Mod":
+        # reference/math/binary.c:25-27: (float)((int)a % (int)b), C remainder
+        # (truncating division: the sign follows a).
+        av = ins[0].astype(np.int32)
+        bv = np.broadcast_to(ins[1].astype(np.int32), np.broadcast_shapes(ins[0].shape, ins[1].shape))
+        return [np.fmod(np.broadcast_to(av, bv.shape), bv).astype(np.float32)]
+    if op == "Slice":
+        return [_slice(ins, node, outs[0].shape)]
+    if op == "Gather":
+        # reference/tensor/gather.c:4-44: fp32 indices, negative ones wrap.
+        axis = a.axis % ins[0].ndim
+        idx = ins[1].astype(np.int64)
+        idx = np.where(idx < 0, idx + ins[0].shape[axis], idx)
+        return [np.take(ins[0], idx, axis=axis).reshape(outs[0].shape)]
     raise NotImplementedError(op)
+
+
+def _avgpool(x, attr, yshape):
+    """reference/pool/avgpool.c:3-47: mean over the in-range taps only
+    (padding is not counted), fp32 sums in tap order."""
+    n, c, h, w = x.shape
+    oh, ow = yshape[2], yshape[3]
+    kh, kw = attr.kernel_shape
+    sh, sw = attr.strides
+    ph, pw = attr.pads[0], attr.pads[1]
+    out = np.zeros((n, c, oh, ow), dtype=np.float32)
+    for i in range(oh):
+        for j in range(ow):
+            s = np.zeros((n, c), dtype=np.float32)
+            cnt = 0
+            for r in range(kh):
+                ih = i * sh + r - ph
+                if ih < 0 or ih >= h:
+                    continue
+                for q in range(kw):
+                    iw = j * sw + q - pw
+                    if iw < 0 or iw >= w:
+                        continue
+                    s = (s + x[:, :, ih, iw]).astype(np.float32)
+                    cnt += 1
+            out[:, :, i, j] = s / np.float32(cnt) if cnt else np.float32(0)
+    return out
+
+
+def _slice(ins, node, yshape):
+    """reference/tensor/slice.c:4-56: one axis from starts[0], ends[0],
+    axes[0] (default 0), steps[0] (default 1); negative start/end wrap,
+    end clamps to the axis size, start clamps at 0."""
+    x = ins[0]
+    start, end = int(ins[1].reshape(-1)[0]), int(ins[2].reshape(-1)[0])
+    axis = int(ins[3].reshape(-1)[0]) if len(ins) > 3 else 0
+    step = int(ins[4].reshape(-1)[0]) if len(ins) > 4 else 1
+    axis %= x.ndim
+    dim = x.shape[axis]
+    start = start + dim if start < 0 else start
+    end = end + dim if end < 0 else end
+    end = min(end, dim)
+    start = max(start, 0)
+    count = max(0, (end - start + step - 1) // step)
+    sel = start + step * np.arange(count)
+    return np.ascontiguousarray(np.take(x, sel, axis=axis)).reshape(yshape)
 
 
 def run_spk(spk: bytes | SpkPackage, inputs: list[np.ndarray], keep_all: bool = False):

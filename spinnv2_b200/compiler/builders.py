@@ -285,7 +285,99 @@ def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80
     return b.graph
 
 
+# ---------------------------------------------------------------- op coverage
+
+# Single-op graphs for the runtime ops outside the five configs (reference
+# compiler/ir/types.py:15-47 op set).  Each is  x -> Add(c) -> OP -> Add(c')
+# -> y  so that the op reads and writes arena activations (NHWC on the device
+# where rank 4) rather than only the row-major graph IO; cases with a second
+# runtime input (an index tensor) take it as a graph input.
+OP_CASES = (
+    "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
+    "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
+)
+
+
+def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
+    net = _Net(f"op_{case}_b{batch}", seed)
+    b = net.b
+    rng = net.init.rng
+
+    def pre(shape):
+        x = b.input("input", shape)
+        return b.op("Add", [x, net.const("pre_c", [0.125])], shape)
+
+    def post(y):
+        y = b.op("Add", [y, net.const("post_c", [-0.25])], b.shape(y))
+        b.mark_output(y)
+        return b.graph
+
+    n = batch
+    if case == "matmul":
+        x = pre([n, 3, 40, 24])
+        w = b.weight("mm_b", rng.standard_normal((24, 36), dtype=np.float32))
+        return post(b.op("MatMul", [x, w], [n, 3, 40, 36]))
+    if case == "matmul_bcast":
+        x = pre([n, 1, 33, 20])
+        w = b.weight("mm_b", rng.standard_normal((3, 20, 70), dtype=np.float32))
+        return post(b.op("MatMul", [x, w], [n, 3, 33, 70]))
+    if case == "clip":
+        x = pre([n, 8, 13, 11])
+        return post(b.op("Clip", [x, net.const("lo", [-0.5]), net.const("hi", [0.7])], [n, 8, 13, 11]))
+    if case == "leakyrelu":
+        x = pre([n, 8, 13, 11])
+        return post(b.op("LeakyRelu", [x], [n, 8, 13, 11], {"alpha": 0.1}))
+    if case == "avgpool":
+        x = pre([n, 8, 15, 15])
+        return post(b.op("AveragePool", [x], [n, 8, 8, 8], {"kernel_shape": [3, 3], "strides": [2, 2],
+                                                             "pads": [1, 1, 1, 1]}))
+    if case == "globalavgpool":
+        x = pre([n, 16, 7, 9])
+        return post(b.op("GlobalAveragePool", [x], [n, 16, 1, 1]))
+    if case == "mod":
+        x = b.input("input", [n, 8, 6, 5])
+        y = b.op("Mul", [x, net.const("scale", [7.0])], [n, 8, 6, 5])
+        return post(b.op("Mod", [y, net.const("m", [3.0])], [n, 8, 6, 5]))
+    if case == "sub":
+        x = pre([n, 8, 6, 5])
+        c = b.weight("sub_c", rng.standard_normal((8, 1, 1), dtype=np.float32))
+        return post(b.op("Sub", [x, c], [n, 8, 6, 5]))
+    if case == "div":
+        x = pre([n, 8, 6, 5])
+        c = b.weight("div_c", rng.uniform(0.5, 2.0, (1, 1, 5)).astype(np.float32))
+        return post(b.op("Div", [x, c], [n, 8, 6, 5]))
+    if case == "transpose":
+        x = pre([n, 8, 5, 6])
+        return post(b.op("Transpose", [x], [n, 5, 6, 8], {"perm": [0, 2, 3, 1]}))
+    if case == "tile":
+        x = pre([n, 3, 4, 5])
+        return post(b.op("Tile", [x, net.const("reps", [1, 2, 1, 3])], [n, 6, 4, 15]))
+    if case == "slice_axis1":
+        x = pre([n, 16, 10, 12])
+        ins = [x, net.const("starts", [3]), net.const("ends", [14]), net.const("axes", [1]), net.const("steps", [2])]
+        return post(b.op("Slice", ins, [n, 6, 10, 12]))
+    if case == "slice_axis3":
+        x = pre([n, 16, 10, 12])
+        ins = [x, net.const("starts", [-8]), net.const("ends", [100]), net.const("axes", [-1]),
+               net.const("steps", [3])]
+        return post(b.op("Slice", ins, [n, 16, 10, 3]))
+    if case == "gather_const":
+        x = pre([n, 10, 6, 7])
+        idx = net.const("idx", np.array([[1, 9], [-1, 0], [4, 4]], dtype=np.float32))
+        return post(b.op("Gather", [x, idx], [n, 3, 2, 6, 7], {"axis": 1}))
+    if case == "gather_input":
+        x = pre([n, 10, 6, 7])
+        idx = b.input("indices", [4])
+        return post(b.op("Gather", [x, idx], [n, 10, 6, 4], {"axis": 3}))
+    if case == "unsqueeze":
+        x = pre([n, 8, 6])
+        return post(b.op("Unsqueeze", [x], [n, 8, 1, 6], {"axes": [2]}))
+    raise KeyError(case)
+
+
 def build_config(name: str, batch: int, seed: int = 0) -> Graph:
+    if name.startswith("op_") and name[3:] in OP_CASES:
+        return op_case(name[3:], batch, seed)
     if name == "lenet5":
         return lenet5(batch, seed)
     if name == "resnet101":
@@ -299,5 +391,6 @@ def build_config(name: str, batch: int, seed: int = 0) -> Graph:
     raise KeyError(name)
 
 
-__all__ = ["lenet5", "conv_sweep", "resnet", "yolo_style", "build_config", "SWEEP_CASES", "sweep_flops",
+__all__ = ["lenet5", "conv_sweep", "resnet", "yolo_style", "op_case", "build_config", "SWEEP_CASES", "OP_CASES",
+           "sweep_flops",
            "resnet_gflop_per_image", "DTYPE_FP32"]

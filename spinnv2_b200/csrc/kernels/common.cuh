@@ -116,6 +116,17 @@ struct FastDiv {
   }
 };
 
+// A small constant fp32 tensor (axes, k, slice bounds, constant indices)
+// read from the package's host copy of the weights; nullptr if the tensor is
+// not an fp32 weight inside the weight section.
+inline const float *host_weight_f32(const Spkv2Context *ctx, uint32_t tid, size_t *count) {
+  const Spkv2TensorRecord *r = ctx->tensors[tid].record;
+  if (r->role != SPKV2_ROLE_WEIGHT || r->dtype != SPKV2_DTYPE_FP32) return nullptr;
+  if (r->data_offset + r->size_bytes > ctx->weights_size) return nullptr;
+  *count = elem_count(r);
+  return reinterpret_cast<const float *>(ctx->weights + r->data_offset);
+}
+
 inline int grid_for(int64_t n, int threads) {
   int64_t blocks = ceil_div(n, threads);
   // Grid-stride beyond 148 SMs x 32 resident blocks.

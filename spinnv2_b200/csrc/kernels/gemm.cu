@@ -9,6 +9,11 @@
 //     second kernel sums the partial results in a fixed order (deterministic).
 //   otherwise, no transposes - 64x64x16 shared-memory tiles, 4x4 per thread.
 //   with transposes        - one thread per output, strided loads.
+// MatMul (reference/mm/matmul.c:3-50): Y[..., M, N] = A[..., M, K] *
+// B[..., K, N] with numpy-style broadcasting of the leading (batch) dims
+// (a size-1 or missing dim repeats); no bias, no alpha.  Device design: the
+// 64x64x16 tiled kernel over element strides (any operand may be an NHWC
+// rank-4 activation), one grid z-slice per batch matrix.
 #include <string.h>
 
 #include "conv.h"
@@ -122,6 +127,136 @@ __global__ void __launch_bounds__(256) sgemm_tile_kernel(float *__restrict__ Y, 
   }
 }
 
+// Batched strided matmul.  Batch index b (blockIdx.z + k * gridDim.z)
+// decomposes over the output's leading dims; each operand's stride per
+// leading dim is 0 where it broadcasts.
+struct MatmulDesc {
+  int M, K, N;
+  int nb;                 // leading (batch) dims of the output
+  int64_t bdim[kMaxRank];
+  int64_t as[kMaxRank], bs[kMaxRank], ys[kMaxRank];  // per-batch-dim strides
+  int64_t a_m, a_k, b_k, b_n, y_m, y_n;              // matrix strides
+  int64_t batches;
+};
+
+struct MatmulPlan : NodePlan {
+  MatmulDesc d;
+};
+
+__global__ void __launch_bounds__(256) matmul_tile_kernel(float *__restrict__ Y, const float *__restrict__ A,
+                                                          const float *__restrict__ B, MatmulDesc d) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  for (int64_t bi = blockIdx.z; bi < d.batches; bi += gridDim.z) {
+    int64_t rem = bi, oa = 0, ob = 0, oy = 0;
+    for (int k = d.nb - 1; k >= 0; --k) {
+      const int64_t c = rem % d.bdim[k];
+      rem /= d.bdim[k];
+      oa += c * d.as[k];
+      ob += c * d.bs[k];
+      oy += c * d.ys[k];
+    }
+    const float *a = A + oa;
+    const float *b = B + ob;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < d.K; k0 += 16) {
+      for (int e = tid; e < 64 * 16; e += 256) {
+        const int mm = e / 16, kk = e % 16;
+        const int m = m0 + mm, k = k0 + kk;
+        As[kk][mm] = (m < d.M && k < d.K) ? a[m * d.a_m + k * d.a_k] : 0.0f;
+        const int kb = e / 64, nn = e % 64;
+        const int kg = k0 + kb, n = n0 + nn;
+        Bs[kb][nn] = (kg < d.K && n < d.N) ? b[kg * d.b_k + n * d.b_n] : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        float av[4], bv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = m0 + ty * 4 + i;
+      if (m >= d.M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = n0 + tx * 4 + j;
+        if (n < d.N) Y[oy + m * d.y_m + n * d.y_n] = acc[i][j];
+      }
+    }
+  }
+}
+
+int matmul_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  const TensorState &ta = ctx->tensors[node->inputs[0]];
+  const TensorState &tb = ctx->tensors[node->inputs[1]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (ta.record->dtype != SPKV2_DTYPE_FP32 || tb.record->dtype != SPKV2_DTYPE_FP32 ||
+      ty.record->dtype != SPKV2_DTYPE_FP32)
+    return SPKV2_ERR_UNSUPPORTED;
+  const View va = make_view(ta), vb = make_view(tb), vy = make_view(ty);
+  if (va.rank < 2 || vb.rank < 2 || vy.rank < 2) return -11;
+  const int ar = va.rank, br = vb.rank, yr = vy.rank;
+  MatmulPlan *p = new MatmulPlan();
+  MatmulDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  d.M = int(vy.dim[yr - 2]);
+  d.N = int(vy.dim[yr - 1]);
+  d.K = int(va.dim[ar - 1]);
+  bool ok = va.dim[ar - 2] == d.M && vb.dim[br - 2] == d.K && vb.dim[br - 1] == d.N && yr - 2 <= kMaxRank;
+  d.nb = yr - 2;
+  d.batches = 1;
+  for (int k = 0; k < d.nb && ok; ++k) {
+    d.bdim[k] = vy.dim[k];
+    d.ys[k] = vy.stride[k];
+    d.batches *= vy.dim[k];
+    // Right-aligned operand dims; a size-1 or missing dim broadcasts.
+    const int ad = k - (yr - ar), bd = k - (yr - br);
+    d.as[k] = (ad < 0 || va.dim[ad] == 1) ? 0 : va.stride[ad];
+    d.bs[k] = (bd < 0 || vb.dim[bd] == 1) ? 0 : vb.stride[bd];
+    if (ad >= 0 && va.dim[ad] != 1 && va.dim[ad] != vy.dim[k]) ok = false;
+    if (bd >= 0 && vb.dim[bd] != 1 && vb.dim[bd] != vy.dim[k]) ok = false;
+  }
+  if (!ok) {
+    delete p;
+    return -11;
+  }
+  d.a_m = va.stride[ar - 2];
+  d.a_k = va.stride[ar - 1];
+  d.b_k = vb.stride[br - 2];
+  d.b_n = vb.stride[br - 1];
+  d.y_m = vy.stride[yr - 2];
+  d.y_n = vy.stride[yr - 1];
+  p->variant = "matmul_tile64_fp32";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int matmul_run(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  MatmulPlan *p = node_plan<MatmulPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  const MatmulDesc &d = p->d;
+  if (d.M == 0 || d.N == 0 || d.batches == 0) return 0;
+  dim3 grid(unsigned(ceil_div(d.N, 64)), unsigned(ceil_div(d.M, 64)), unsigned(std::min<int64_t>(d.batches, 65535)));
+  matmul_tile_kernel<<<grid, 256, 0, ctx->stream>>>(reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data),
+                                                    reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data),
+                                                    reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data),
+                                                    d);
+  return cuda_status(cudaGetLastError());
+}
+
 __global__ void gemm_naive_kernel(float *__restrict__ Y, const float *__restrict__ A, const float *__restrict__ B,
                                   const float *__restrict__ bias, int M, int K, int N, int ta, int tb, float alpha) {
   const int64_t total = int64_t(M) * N;
@@ -179,6 +314,7 @@ int noalloc_scratch(float **out) {
 
 int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
   if (node->input_count < 2 || node->output_count < 1) return -3;
+  if (node->op_type == SPKV2_OP_MATMUL) return matmul_prepare(ctx, node);
   if (node->op_type != SPKV2_OP_GEMM) return SPKV2_ERR_UNSUPPORTED;
   Spkv2AttrRecord a;
   int rc = get_attr(ctx, node, &a);
@@ -247,6 +383,7 @@ int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
 }
 
 int gemm_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  if (node->op_type == SPKV2_OP_MATMUL) return matmul_run(ctx, node);
   GemmPlan *p = node_plan<GemmPlan>(ctx, node);
   if (!p) return SPKV2_ERR_NOT_PREPARED;
   if (p->M == 0 || p->N == 0) return 0;

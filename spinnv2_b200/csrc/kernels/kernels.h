@@ -28,6 +28,8 @@ SPKV2_DECLARE_OP(split)
 SPKV2_DECLARE_OP(transpose)
 SPKV2_DECLARE_OP(tile)
 SPKV2_DECLARE_OP(gather_elements)
+SPKV2_DECLARE_OP(slice)
+SPKV2_DECLARE_OP(gather)
 SPKV2_DECLARE_OP(reduce)
 SPKV2_DECLARE_OP(softmax)
 SPKV2_DECLARE_OP(topk)

@@ -231,15 +231,6 @@ __global__ void topk_kernel(float *__restrict__ values, float *__restrict__ indi
   }
 }
 
-// Reads a small constant tensor (axes, k) from the package's host weights.
-const float *host_weight_f32(const Spkv2Context *ctx, uint32_t tid, size_t *count) {
-  const Spkv2TensorRecord *r = ctx->tensors[tid].record;
-  if (r->role != SPKV2_ROLE_WEIGHT || r->dtype != SPKV2_DTYPE_FP32) return nullptr;
-  if (r->data_offset + r->size_bytes > ctx->weights_size) return nullptr;
-  *count = elem_count(r);
-  return reinterpret_cast<const float *>(ctx->weights + r->data_offset);
-}
-
 }  // namespace
 
 int reduce_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {

@@ -9,6 +9,17 @@
 //   Tile    reference/shape/tile.c            x coord = y coord mod x dim
 //   GatherElements reference/tensor/gather_elements.c:3-25  fp32 indices,
 //           negative indices wrap by the axis size
+//   Slice   reference/tensor/slice.c:4-56   one axis: starts[0], ends[0],
+//           axes[0] (default 0), steps[0] (default 1) read from constant
+//           inputs; negative start/end wrap by the axis size, end clamps to
+//           it, start clamps at 0; out extent (end - start + step - 1) / step
+//   Gather  reference/tensor/gather.c:4-44  y = data[..., idx[j], ...] along
+//           `axis`, output shape data[:axis] + idx.shape + data[axis+1:],
+//           fp32 indices, negative indices wrap by the axis size
+// An index that is still out of range after wrapping (the reference reads
+// outside the tensor) writes 0 and records device code 10 in the context's
+// status word, so the run returns SPKV2_ERR_DEVICE_STATUS instead of
+// touching memory outside the input.
 // Device design: every kernel walks one tensor in physical order and reaches
 // the others through per-dim strides, so NHWC and NCHW operands mix freely;
 // Concat/Split move four elements per thread when the innermost physical dim
@@ -272,6 +283,7 @@ struct GatherPlan : NodePlan {
   GatherDesc d;
   int esize = 4;
   int64_t total = 0;
+  int64_t x_offset = 0;  // elements: Slice's start along its axis
 };
 
 template <typename T>
@@ -289,7 +301,10 @@ __global__ void gather_copy_kernel(T *__restrict__ y, const T *__restrict__ x, G
 }
 
 // perm[d] = input dim feeding output dim d; tile=true uses the modulus.
-int prepare_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node, const int *perm, bool tile, const char *name) {
+// Slice: output coordinate c of dim `step_dim` reads input coordinate
+// start + c * step (step >= 1).
+int prepare_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node, const int *perm, bool tile, const char *name,
+                   int step_dim = -1, int64_t start = 0, int64_t step = 1) {
   const TensorState &tx = ctx->tensors[node->inputs[0]];
   const TensorState &ty = ctx->tensors[node->outputs[0]];
   if (tx.record->dtype != ty.record->dtype || tx.record->rank != ty.record->rank) return SPKV2_ERR_UNSUPPORTED;
@@ -311,9 +326,10 @@ int prepare_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node, const int *pe
     }
     d.dim[j] = vy.dim[od];
     d.ostride[j] = vy.stride[od];
-    d.istride[j] = vx.stride[id];
+    d.istride[j] = vx.stride[id] * (od == step_dim ? step : 1);
     d.imod[j] = tile ? std::max<int64_t>(vx.dim[id], 1) : std::max<int64_t>(vy.dim[od], 1);
   }
+  if (step_dim >= 0) p->x_offset = start * vx.stride[perm[step_dim]];
   p->esize = int(dtype_size(ty.record->dtype));
   p->total = vy.count();
   p->variant = name;
@@ -326,14 +342,13 @@ int run_gather(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
   if (!p) return SPKV2_ERR_NOT_PREPARED;
   if (p->total == 0) return 0;
   void *y = ctx->tensors[node->outputs[0]].data;
-  const void *x = ctx->tensors[node->inputs[0]].data;
+  const uint8_t *x = ctx->tensors[node->inputs[0]].data + p->x_offset * p->esize;
   const int g = grid_for(p->total, 256);
   if (p->esize == 1)
-    gather_copy_kernel<uint8_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint8_t *>(y), static_cast<const uint8_t *>(x),
-                                                            p->d, p->total);
+    gather_copy_kernel<uint8_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint8_t *>(y), x, p->d, p->total);
   else
     gather_copy_kernel<uint32_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint32_t *>(y),
-                                                             static_cast<const uint32_t *>(x), p->d, p->total);
+                                                             reinterpret_cast<const uint32_t *>(x), p->d, p->total);
   return cuda_status(cudaGetLastError());
 }
 
@@ -354,8 +369,10 @@ struct GEPlan : NodePlan {
   int64_t total = 0;
 };
 
+constexpr int kIndexRangeCode = 10;  // device status code: an index outside [-dim, dim)
+
 __global__ void gather_elements_kernel(float *__restrict__ y, const float *__restrict__ data,
-                                       const float *__restrict__ idx, GEDesc d, int64_t total) {
+                                       const float *__restrict__ idx, GEDesc d, int64_t total, int *status) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     int64_t rem = i, oy = 0, oi = 0, od = 0;
     int64_t coord[kMaxRank];
@@ -365,11 +382,57 @@ __global__ void gather_elements_kernel(float *__restrict__ y, const float *__res
       oy += coord[k] * d.ystride[k];
       oi += coord[k] * d.istride[k];
     }
-    int g = int(idx[oi]);
-    if (g < 0) g += int(d.axis_dim);
+    int64_t g = int64_t(idx[oi]);
+    if (g < 0) g += d.axis_dim;
+    if (g < 0 || g >= d.axis_dim) {
+      y[oy] = 0.0f;
+      atomicCAS(status, 0, kIndexRangeCode);
+      continue;
+    }
     coord[d.axis] = g;
     for (int k = 0; k < d.rank; ++k) od += coord[k] * d.dstride[k];
     y[oy] = data[od];
+  }
+}
+
+// ---------------- Gather (one index tensor along one axis) ----------------
+
+struct GatherIdxDesc {
+  int rank;                   // output rank (data rank - 1 + index rank)
+  int64_t dim[kMaxRank];      // output dims in output physical order
+  int64_t ystride[kMaxRank];  // output strides
+  int64_t dstride[kMaxRank];  // data strides of the data dims (0 on index dims)
+  int64_t istride[kMaxRank];  // index-tensor strides of the index dims (0 elsewhere)
+  int64_t axis_stride;        // data stride along the gather axis
+  int64_t axis_dim;
+};
+
+struct GatherIdxPlan : NodePlan {
+  GatherIdxDesc d;
+  int esize = 4;
+  int64_t total = 0;
+};
+
+template <typename T>
+__global__ void gather_index_kernel(T *__restrict__ y, const T *__restrict__ data, const float *__restrict__ idx,
+                                    GatherIdxDesc d, int64_t total, int *status) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i, oy = 0, od = 0, oi = 0;
+    for (int k = d.rank - 1; k >= 0; --k) {
+      const int64_t c = rem % d.dim[k];
+      rem /= d.dim[k];
+      oy += c * d.ystride[k];
+      od += c * d.dstride[k];
+      oi += c * d.istride[k];
+    }
+    int64_t g = int64_t(idx[oi]);
+    if (g < 0) g += d.axis_dim;
+    if (g < 0 || g >= d.axis_dim) {
+      y[oy] = T(0);
+      atomicCAS(status, 0, kIndexRangeCode);
+      continue;
+    }
+    y[oy] = data[od + g * d.axis_stride];
   }
 }
 
@@ -447,7 +510,137 @@ int gather_elements_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) 
   gather_elements_kernel<<<grid_for(p->total, 256), 256, 0, ctx->stream>>>(
       reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data),
       reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data),
-      reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data), p->d, p->total);
+      reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data), p->d, p->total, ctx->d_status);
+  return cuda_status(cudaGetLastError());
+}
+
+namespace {
+
+// Optional input k of a node is present when the node lists it and the slot
+// is not the 0xFFFF "absent" marker (reference tensor/slice.c:20-30).
+bool has_input(const Spkv2NodeRecord *node, int k) { return node->input_count > k && node->inputs[k] != 0xFFFF; }
+
+// First value of a constant fp32 input, if it is one.
+bool first_const(const Spkv2Context *ctx, uint32_t tid, float *v) {
+  size_t n = 0;
+  const float *p = host_weight_f32(ctx, tid, &n);
+  if (!p || n < 1) return false;
+  *v = p[0];
+  return true;
+}
+
+}  // namespace
+
+int slice_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 3 || node->output_count < 1) return -3;
+  const TensorState &tx = ctx->tensors[node->inputs[0]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  const int rank = tx.record->rank;
+  if (ty.record->rank != rank || rank < 1 || rank > kMaxRank) return -11;
+  float fs = 0, fe = 0, fa = 0, fst = 1;
+  // starts / ends / axes / steps must be package constants: the kernel's
+  // geometry is fixed at prepare.
+  if (!first_const(ctx, node->inputs[1], &fs) || !first_const(ctx, node->inputs[2], &fe)) return SPKV2_ERR_UNSUPPORTED;
+  if (has_input(node, 3) && !first_const(ctx, node->inputs[3], &fa)) return SPKV2_ERR_UNSUPPORTED;
+  if (has_input(node, 4) && !first_const(ctx, node->inputs[4], &fst)) return SPKV2_ERR_UNSUPPORTED;
+  int64_t start = int64_t(fs), end = int64_t(fe), step = int64_t(int(fst));
+  int axis = int(fa);
+  if (axis < 0) axis += rank;
+  if (axis < 0 || axis >= rank) return -11;
+  if (step < 1) return SPKV2_ERR_UNSUPPORTED;  // the reference's extent formula assumes a positive step
+  const int64_t dim = tx.record->shape[axis];
+  if (start < 0) start += dim;
+  if (end < 0) end += dim;
+  if (end > dim) end = dim;
+  if (start < 0) start = 0;
+  const int64_t out = std::max<int64_t>(0, (end - start + step - 1) / step);
+  for (int k = 0; k < rank; ++k)
+    if (int64_t(ty.record->shape[k]) != (k == axis ? out : int64_t(tx.record->shape[k]))) return -3;
+  if (out > 0 && start + (out - 1) * step >= dim) return -3;
+  if (tx.record->dtype != ty.record->dtype) return SPKV2_ERR_UNSUPPORTED;
+  int perm[kMaxRank];
+  for (int i = 0; i < rank; ++i) perm[i] = i;
+  return prepare_gather(ctx, node, perm, false, "slice", axis, start, step);
+}
+int slice_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) { return run_gather(ctx, node); }
+
+int gather_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *) {
+  if (node->input_count < 2 || node->output_count < 1) return -3;
+  Spkv2AttrRecord a;
+  int rc = get_attr(ctx, node, &a);
+  if (rc) return rc;
+  const TensorState &td = ctx->tensors[node->inputs[0]];
+  const TensorState &ti = ctx->tensors[node->inputs[1]];
+  const TensorState &ty = ctx->tensors[node->outputs[0]];
+  if (ti.record->dtype != SPKV2_DTYPE_FP32 || td.record->dtype != ty.record->dtype) return SPKV2_ERR_UNSUPPORTED;
+  const size_t esize = dtype_size(td.record->dtype);
+  if (esize != 1 && esize != 4) return SPKV2_ERR_UNSUPPORTED;
+  const int dr = td.record->rank, ir = ti.record->rank, yr = ty.record->rank;
+  const int axis = a.axis < 0 ? a.axis + dr : a.axis;
+  if (axis < 0 || axis >= dr || yr != dr - 1 + ir || yr > kMaxRank || yr < 1) return -11;
+  const View vd = make_view(td), vi = make_view(ti), vy = make_view(ty);
+  // Logical output dim k: data dim k (k < axis), index dim k - axis, or data
+  // dim k - ir + 1.
+  int64_t dstr[kMaxRank] = {}, istr[kMaxRank] = {};
+  for (int k = 0; k < yr; ++k) {
+    int64_t want;
+    if (k < axis) {
+      want = vd.dim[k];
+      dstr[k] = vd.stride[k];
+    } else if (k < axis + ir) {
+      want = vi.dim[k - axis];
+      istr[k] = vi.stride[k - axis];
+    } else {
+      want = vd.dim[k - ir + 1];
+      dstr[k] = vd.stride[k - ir + 1];
+    }
+    if (vy.dim[k] != want) return -3;
+  }
+  // Constant indices are checked here, once; activations on the device.
+  size_t n = 0;
+  if (const float *iv = host_weight_f32(ctx, node->inputs[1], &n)) {
+    for (size_t j = 0; j < n; ++j) {
+      int64_t g = int64_t(iv[j]);
+      if (g < 0) g += vd.dim[axis];
+      if (g < 0 || g >= vd.dim[axis]) return -3;
+    }
+  }
+  int order[kMaxRank];
+  for (int i = 0; i < yr; ++i) order[i] = i;
+  std::stable_sort(order, order + yr, [&](int x, int y) { return vy.stride[x] > vy.stride[y]; });
+  GatherIdxPlan *p = new GatherIdxPlan();
+  GatherIdxDesc &d = p->d;
+  memset(&d, 0, sizeof(d));
+  d.rank = yr;
+  for (int j = 0; j < yr; ++j) {
+    d.dim[j] = vy.dim[order[j]];
+    d.ystride[j] = vy.stride[order[j]];
+    d.dstride[j] = dstr[order[j]];
+    d.istride[j] = istr[order[j]];
+  }
+  d.axis_stride = vd.stride[axis];
+  d.axis_dim = vd.dim[axis];
+  p->esize = int(esize);
+  p->total = vy.count();
+  p->variant = "gather_index";
+  set_node_plan(ctx, node, p);
+  return 0;
+}
+
+int gather_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
+  GatherIdxPlan *p = node_plan<GatherIdxPlan>(ctx, node);
+  if (!p) return SPKV2_ERR_NOT_PREPARED;
+  if (p->total == 0) return 0;
+  void *y = ctx->tensors[node->outputs[0]].data;
+  const void *x = ctx->tensors[node->inputs[0]].data;
+  const float *idx = reinterpret_cast<const float *>(ctx->tensors[node->inputs[1]].data);
+  const int g = grid_for(p->total, 256);
+  if (p->esize == 1)
+    gather_index_kernel<uint8_t><<<g, 256, 0, ctx->stream>>>(static_cast<uint8_t *>(y), static_cast<const uint8_t *>(x),
+                                                             idx, p->d, p->total, ctx->d_status);
+  else
+    gather_index_kernel<uint32_t><<<g, 256, 0, ctx->stream>>>(
+        static_cast<uint32_t *>(y), static_cast<const uint32_t *>(x), idx, p->d, p->total, ctx->d_status);
   return cuda_status(cudaGetLastError());
 }
 

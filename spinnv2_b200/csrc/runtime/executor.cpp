@@ -844,7 +844,7 @@ const char *spkv2_cuda_status_string(int code) {
     case SPKV2_ERR_LAUNCH: return "kernel launch failed";
     case SPKV2_ERR_NOT_PREPARED: return "context not prepared";
     case SPKV2_ERR_PROTECTION: return "protection plans are not supported on the CUDA target";
-    case SPKV2_ERR_DEVICE_STATUS: return "device kernel reported a timeout";
+    case SPKV2_ERR_DEVICE_STATUS: return "device kernel reported a timeout or an out-of-range index";
     default: return (code <= -20 && code >= -26) ? "fault or protection error" : "unknown";
   }
 }

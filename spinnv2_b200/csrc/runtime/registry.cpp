@@ -63,6 +63,8 @@ const Builtin kBuiltins[] = {
     {SPKV2_OP_TRANSPOSE, transpose_run, transpose_prepare},
     {SPKV2_OP_TILE, tile_run, tile_prepare},
     {SPKV2_OP_GATHERELEMENTS, gather_elements_run, gather_elements_prepare},
+    {SPKV2_OP_SLICE, slice_run, slice_prepare},
+    {SPKV2_OP_GATHER, gather_run, gather_prepare},
     {SPKV2_OP_REDUCEMEAN, reduce_run, reduce_prepare},
     {SPKV2_OP_REDUCEMAX, reduce_run, reduce_prepare},
     {SPKV2_OP_SOFTMAX, softmax_run, softmax_prepare},

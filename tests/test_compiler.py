@@ -90,11 +90,19 @@ def test_resnet_flops_match_survey():
 
 
 def test_unsupported_op_fails_loudly_for_cuda():
-    g = Graph(model_name="matmul")
+    g = Graph(model_name="nms")
     g.add_tensor(Tensor(0, "a", DTYPE_FP32, [2, 2], ROLE_INPUT))
     g.add_tensor(Tensor(1, "b", DTYPE_FP32, [2, 2], ROLE_INPUT))
     g.add_tensor(Tensor(2, "y", DTYPE_FP32, [2, 2], ROLE_OUTPUT))
     g.inputs, g.outputs = [0, 1], [2]
-    g.add_node(Node(0, "MatMul", [0, 1], [2]))
+    g.add_node(Node(0, "NonMaxSuppression", [0, 1], [2]))
     with pytest.raises(ValueError):
         select_kernel_specs(g, load_target_profile("cuda_b200"))
+
+
+def test_cuda_profile_covers_every_runtime_op():
+    from spinnv2_b200.compiler.ir import RUNTIME_OPS
+
+    ops = load_target_profile("cuda_b200")["ops"]
+    assert RUNTIME_OPS <= set(ops)
+    assert not any("ref" in toks for toks in ops.values())  # no CPU fallback spec anywhere
