@@ -36,7 +36,7 @@ extern "C" {
 #define SPKV2_ERR_UNSUPPORTED   (-43) /* node variant has no CUDA kernel */
 #define SPKV2_ERR_LAUNCH        (-44) /* kernel launch failed */
 #define SPKV2_ERR_NOT_PREPARED  (-45) /* call requires spkv2_prepare first */
-#define SPKV2_ERR_PROTECTION    (-46) /* SPK carries a protection plan (host-only feature) */
+#define SPKV2_ERR_PROTECTION    (-46) /* reserved; protection plans run (range guard, DMR) */
 #define SPKV2_ERR_DEVICE_STATUS (-47) /* a kernel reported a bounded-wait timeout or a bad index */
 
 /* fp32 Conv/Gemm math modes. */

@@ -18,6 +18,25 @@ from . import REF_LIB
 _lib = None
 
 
+class FaultEventC(ctypes.Structure):
+    """Spkv2FaultEvent (reference runtime/include/spkv2_runtime.h)."""
+    _fields_ = [("node_id", ctypes.c_uint32), ("tensor_id", ctypes.c_uint32), ("element_index", ctypes.c_uint64),
+                ("bit_index", ctypes.c_uint8), ("invocation_index", ctypes.c_uint32), ("seed", ctypes.c_uint64),
+                ("enabled", ctypes.c_int)]
+
+
+class StatsC(ctypes.Structure):
+    """Spkv2ReliabilityStats."""
+    _fields_ = [(n, ctypes.c_uint64) for n in ("injected_faults", "detected_faults", "recovered_faults",
+                                                "unrecovered_faults", "rerun_count")]
+
+
+class RangeObsC(ctypes.Structure):
+    """Spkv2RangeObservation."""
+    _fields_ = [("node_id", ctypes.c_uint32), ("tensor_id", ctypes.c_uint32), ("observed_min", ctypes.c_float),
+                ("observed_max", ctypes.c_float), ("observations", ctypes.c_uint64)]
+
+
 def library(path: str | Path | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None and path is None:
@@ -35,6 +54,12 @@ def library(path: str | Path | None = None) -> ctypes.CDLL:
         ("spkv2_get_output", i32, [vp, i32, vp, sz]),
         ("spkv2_run", i32, [vp]),
         ("spkv2_free", None, [vp]),
+        ("spkv2_set_fault_event", i32, [vp, ctypes.POINTER(FaultEventC)]),
+        ("spkv2_clear_fault_event", None, [vp]),
+        ("spkv2_get_reliability_stats", i32, [vp, ctypes.POINTER(StatsC)]),
+        ("spkv2_reset_reliability_stats", None, [vp]),
+        ("spkv2_get_range_observation", i32, [vp, ctypes.c_uint32, ctypes.POINTER(RangeObsC)]),
+        ("spkv2_reset_range_observations", None, [vp]),
     ]:
         fn = getattr(lib, name)
         fn.restype = res
@@ -76,6 +101,29 @@ class RefRuntime:
                 raise RuntimeError(f"reference get_output failed: {rc}")
             outs.append(o)
         return outs
+
+    def run_reliability(self, inputs: list[np.ndarray], event: dict | None, node_ids: list[int]):
+        """One run with reset statistics and an optional fault event
+        (dict of Spkv2FaultEvent fields); returns (outputs, stats dict,
+        {node_id: (min, max, observations)} for the nodes observed)."""
+        self.lib.spkv2_reset_reliability_stats(self.ctx)
+        self.lib.spkv2_reset_range_observations(self.ctx)
+        if event is None:
+            self.lib.spkv2_clear_fault_event(self.ctx)
+        else:
+            ev = FaultEventC(**{**event, "enabled": 1})
+            rc = self.lib.spkv2_set_fault_event(self.ctx, ctypes.byref(ev))
+            if rc:
+                raise RuntimeError(f"reference set_fault_event failed: {rc}")
+        outs = self.run(*inputs)
+        st = StatsC()
+        self.lib.spkv2_get_reliability_stats(self.ctx, ctypes.byref(st))
+        obs = {}
+        for nid in node_ids:
+            o = RangeObsC()
+            if self.lib.spkv2_get_range_observation(self.ctx, nid, ctypes.byref(o)) == 0 and o.observations:
+                obs[nid] = (float(o.observed_min), float(o.observed_max), int(o.observations))
+        return outs, {n: int(getattr(st, n)) for n, _ in st._fields_}, obs
 
     def close(self):
         if self.ctx:

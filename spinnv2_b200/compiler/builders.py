@@ -375,6 +375,26 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
     raise KeyError(case)
 
 
+# Protection plan over the FUSED LeNet-5 graph (node ids after the pass
+# pipeline: 0 Conv+Relu, 2 Conv+Relu, 5 Gemm, 9 Gemm): range guards on the
+# first conv (a Relu output, so [0, 60]) and on the first Gemm (infinite
+# bounds: only non-finite values trip it), DMR on the second conv and on
+# the logits.  Entries: (node_id, mode, lower, upper).
+LENET5_PROTECTION = ((0, "range_guard_rerun", 0.0, 60.0), (2, "dmr_compare_rerun", None, None),
+                     (5, "range_guard_rerun", None, None), (9, "dmr_compare_rerun", None, None))
+
+
+def lenet5_protection_entries(graph: Graph) -> list[dict]:
+    """LENET5_PROTECTION as plan entries for the fused LeNet-5 `graph`."""
+    out = []
+    for nid, mode, lo, hi in LENET5_PROTECTION:
+        e = {"node_id": nid, "tensor_id": graph.nodes[nid].outputs[0], "mode": mode}
+        if lo is not None:
+            e["lower_bound"], e["upper_bound"] = lo, hi
+        out.append(e)
+    return out
+
+
 def build_config(name: str, batch: int, seed: int = 0) -> Graph:
     if name.startswith("op_") and name[3:] in OP_CASES:
         return op_case(name[3:], batch, seed)
@@ -392,5 +412,6 @@ def build_config(name: str, batch: int, seed: int = 0) -> Graph:
 
 
 __all__ = ["lenet5", "conv_sweep", "resnet", "yolo_style", "op_case", "build_config", "SWEEP_CASES", "OP_CASES",
+           "LENET5_PROTECTION", "lenet5_protection_entries",
            "sweep_flops",
            "resnet_gflop_per_image", "DTYPE_FP32"]

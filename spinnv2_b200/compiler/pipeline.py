@@ -31,9 +31,9 @@ def fuse(graph: Graph) -> Graph:
     return graph
 
 
-def package(graph: Graph, profile: str | dict, quant_params: list | None = None) -> bytes:
+def package(graph: Graph, profile: str | dict, quant_params: list | None = None, protection_plan=None) -> bytes:
     prof = load_target_profile(profile) if isinstance(profile, str) else profile
-    data, _ = build_spk(graph, prof, quant_params=quant_params)
+    data, _ = build_spk(graph, prof, quant_params=quant_params, protection_plan=protection_plan)
     return data
 
 

@@ -134,8 +134,12 @@ def attr_bytes(node: Node) -> bytes:
 
 
 def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = None,
-              kernel_plan: KernelPlan | None = None, quant_params: list | None = None) -> tuple[bytes, dict]:
-    """Serialise `graph` for `profile`; returns (package bytes, debug dict)."""
+              kernel_plan: KernelPlan | None = None, quant_params: list | None = None,
+              protection_plan=None) -> tuple[bytes, dict]:
+    """Serialise `graph` for `profile`; returns (package bytes, debug dict).
+    `protection_plan` (compiler.protection.ProtectionPlan) adds the protection
+    section after the quantisation section and grows the scratch arena by
+    its DMR copies (reference compiler/packager/spk_writer.py:147-149,187)."""
     unknown = sorted({n.op_type for n in graph.nodes if n.op_type not in OP_CODES})
     if unknown:
         raise ValueError(f"graph still contains unsupported runtime op(s): {', '.join(unknown)}")
@@ -207,6 +211,11 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
     ]
     if quant_params:
         sections.append((SECTION_QUANTIZATION, quantization_section(quant_params), 4))
+    prot_scratch = 0
+    if protection_plan is not None:
+        sections.append((SECTION_PROTECTION_PLAN,
+                         protection_plan.section(graph, scratch_offset=kernel_plan.scratch_arena_bytes), 8))
+        prot_scratch = protection_plan.scratch_bytes(graph)
     sections.append((SECTION_STRING_TABLE, bytes(strings), 1))
     sections.append((SECTION_CHECKSUM, b"\x00\x00\x00\x00", 4))
 
@@ -226,7 +235,7 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
     header = HEADER.pack(SPKV2_MAGIC, VERSION_MAJOR, VERSION_MINOR, 0, HEADER.size, len(sections), 0,
                          len(graph.tensors), len(graph.nodes), len(graph.inputs), len(graph.outputs),
                          sum(t.size_bytes for t in graph.tensors if t.role == ROLE_WEIGHT),
-                         memory_plan.planned_activation_bytes, kernel_plan.scratch_arena_bytes,
+                         memory_plan.planned_activation_bytes, kernel_plan.scratch_arena_bytes + prot_scratch,
                          fnv1a32(json.dumps(profile, sort_keys=True).encode("utf-8")), 1)
     package = bytearray(header + directory + payload)
     package[checksum_at:checksum_at + 4] = struct.pack("<I", fnv1a32(memoryview(package)[:checksum_at]))

@@ -43,6 +43,18 @@ int watchdog_probe(int *d_status, uint32_t wait_us, cudaStream_t stream);
 // XOR `mask` into one 32-bit word on the device (fault-event injection).
 int launch_bit_flip(uint32_t *word, uint32_t mask, cudaStream_t stream);
 
+// Protection-plan checks (protect.cu); both synchronise the stream.
+struct GuardRange {
+  uint64_t out_of_range = 0;  // elements non-finite or outside [lo, hi]
+  bool any = false;           // some element is not NaN (min / max valid)
+  bool first_nan = false;     // element 0 is NaN
+  float min = 0.0f, max = 0.0f;
+};
+int guard_range_scan(const float *x, uint64_t n, float lo, float hi, uint32_t *d_out, GuardRange *res,
+                     cudaStream_t stream);
+int guard_bytes_differ(const void *a, const void *b, uint64_t bytes, uint32_t *d_out, bool *differ,
+                       cudaStream_t stream);
+
 // Copy a tensor between host memory in logical order and its device storage
 // in the tensor's physical layout; synchronises the stream.
 int copy_tensor_to_host(const TensorState &t, void *host, cudaStream_t stream);

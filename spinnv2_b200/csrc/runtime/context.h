@@ -110,6 +110,13 @@ struct Spkv2Context {
   Spkv2ReliabilityStats reliability_stats{};
   std::vector<Spkv2RangeObservation> range_observations;
   std::vector<uint32_t> node_invocation_counts;
+  // Protection plan: record index per node (-1: none; the first record
+  // naming the node, as the reference's linear lookup), whether any record
+  // is active (runs then go node by node, eagerly), and a small device
+  // buffer for the range-scan / compare results.
+  std::vector<int32_t> protection_of_node;
+  bool protected_run = false;
+  uint32_t *d_guard = nullptr;
 };
 
 namespace spkv2 {

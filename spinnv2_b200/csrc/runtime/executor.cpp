@@ -164,6 +164,8 @@ void release_device_state(Spkv2Context *ctx) {
   if (ctx->owns_scratch) device_free(ctx->d_scratch);
   device_free(ctx->d_weights);
   device_free(ctx->d_status);
+  device_free(ctx->d_guard);
+  ctx->d_guard = nullptr;
   device_free(ctx->d_sk_ws);
   ctx->d_sk_ws = nullptr;
   ctx->sk_ws_bytes = 0;
@@ -282,6 +284,105 @@ int maybe_inject_fault(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
   return 0;
 }
 
+int execute_once(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  int rc = execute_node(ctx, node);
+  return rc ? rc : maybe_inject_fault(ctx, node);
+}
+
+// Range scan of the protected output; records the observation when asked
+// (reference record_output_range, first execution only) and returns in
+// *ok whether every element is finite and inside [lower, upper] (reference
+// output_in_range).
+int check_range(Spkv2Context *ctx, const Spkv2ProtectionRecord &r, bool record, bool *ok) {
+  const TensorState &t = ctx->tensors[r.tensor_id];
+  const uint64_t n = t.record->size_bytes / sizeof(float);
+  GuardRange g;
+  int rc = guard_range_scan(reinterpret_cast<const float *>(t.data), n, r.lower_bound, r.upper_bound, ctx->d_guard,
+                            &g, ctx->stream);
+  if (rc) return rc;
+  if (record && n > 0 && r.node_id < ctx->range_observations.size()) {
+    // Reference semantics: min = max = element 0, then `<` / `>` updates;
+    // a NaN element 0 stays NaN, later NaNs never win a comparison.
+    const float mn = g.first_nan ? NAN : g.min, mx = g.first_nan ? NAN : g.max;
+    Spkv2RangeObservation &o = ctx->range_observations[r.node_id];
+    o.node_id = r.node_id;
+    o.tensor_id = r.tensor_id;
+    if (o.observations == 0) {
+      o.observed_min = mn;
+      o.observed_max = mx;
+    } else {
+      if (mn < o.observed_min) o.observed_min = mn;
+      if (mx > o.observed_max) o.observed_max = mx;
+    }
+    o.observations++;
+  }
+  *ok = g.out_of_range == 0;
+  return 0;
+}
+
+int device_copy(void *dst, const void *src, size_t bytes, cudaStream_t s) {
+  return cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s));
+}
+
+// One node under its protection record (reference core/executor.c:445-498):
+// range_guard_rerun runs once, scans, and reruns once when the output is
+// out of range; dmr_compare_rerun runs twice into two scratch copies and,
+// when they differ, a third run votes.  Statistics as the reference.  Each
+// check synchronises the stream, so protected runs go node by node.
+int execute_protected(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
+  const int32_t idx = node->id < ctx->protection_of_node.size() ? ctx->protection_of_node[node->id] : -1;
+  if (idx < 0 || ctx->protection_records[idx].mode == SPKV2_PROTECT_NONE) return execute_once(ctx, node);
+  const Spkv2ProtectionRecord &r = ctx->protection_records[idx];
+  if (r.tensor_id >= ctx->header.num_tensors || node->output_count != 1 || node->outputs[0] != r.tensor_id)
+    return -24;
+  Spkv2ReliabilityStats &st = ctx->reliability_stats;
+  if (r.mode == SPKV2_PROTECT_RANGE_GUARD_RERUN) {
+    int rc = execute_once(ctx, node);
+    bool ok = false;
+    if (rc == 0) rc = check_range(ctx, r, true, &ok);
+    if (rc != 0 || ok) return rc;
+    st.detected_faults++;
+    st.rerun_count++;
+    if ((rc = execute_once(ctx, node))) return rc;
+    if ((rc = check_range(ctx, r, false, &ok))) return rc;
+    if (ok)
+      st.recovered_faults++;
+    else
+      st.unrecovered_faults++;
+    return 0;
+  }
+  if (r.mode == SPKV2_PROTECT_DMR_COMPARE_RERUN) {
+    TensorState &t = ctx->tensors[r.tensor_id];
+    const size_t bytes = size_t(t.record->size_bytes);
+    if (!ctx->d_scratch || r.scratch_offset > ctx->scratch_size || bytes * 2u > ctx->scratch_size - r.scratch_offset)
+      return -25;
+    uint8_t *first = ctx->d_scratch + r.scratch_offset;
+    uint8_t *second = first + bytes;
+    int rc = execute_once(ctx, node);
+    if (rc == 0) rc = device_copy(first, t.data, bytes, ctx->stream);
+    if (rc == 0) rc = execute_once(ctx, node);
+    if (rc == 0) rc = device_copy(second, t.data, bytes, ctx->stream);
+    bool differ = false;
+    if (rc == 0) rc = guard_bytes_differ(first, second, bytes, ctx->d_guard, &differ, ctx->stream);
+    if (rc != 0 || !differ) return rc;
+    st.detected_faults++;
+    st.rerun_count++;
+    if ((rc = execute_once(ctx, node))) return rc;
+    if ((rc = guard_bytes_differ(first, t.data, bytes, ctx->d_guard, &differ, ctx->stream))) return rc;
+    if (!differ) {
+      st.recovered_faults++;  // the output already holds the agreeing bytes
+      return 0;
+    }
+    if ((rc = guard_bytes_differ(second, t.data, bytes, ctx->d_guard, &differ, ctx->stream))) return rc;
+    if (!differ)
+      st.recovered_faults++;
+    else
+      st.unrecovered_faults++;
+    return 0;
+  }
+  return -26;
+}
+
 int run_nodes_eager(Spkv2Context *ctx, uint32_t first, uint32_t last, bool profile) {
   std::vector<cudaEvent_t> ev;
   if (profile) {
@@ -292,8 +393,7 @@ int run_nodes_eager(Spkv2Context *ctx, uint32_t first, uint32_t last, bool profi
   int rc = 0;
   for (uint32_t i = first; i < last && rc == 0; ++i) {
     const Spkv2NodeRecord *node = &ctx->node_records[i];
-    rc = execute_node(ctx, node);
-    if (rc == 0) rc = maybe_inject_fault(ctx, node);
+    rc = ctx->protected_run ? execute_protected(ctx, node) : execute_once(ctx, node);
     if (rc == 0) rc = cuda_status(cudaGetLastError());
     if (profile) cudaEventRecord(ev[i - first + 1], ctx->stream);
   }
@@ -352,7 +452,7 @@ int launch_all(Spkv2Context *ctx) {
   prof_init();
   g_prof_ctx = ctx;
   std::fill(ctx->node_invocation_counts.begin(), ctx->node_invocation_counts.end(), 0u);
-  if (g_prof_enabled || ctx->fault_event.enabled || !ctx->graph_mode)
+  if (g_prof_enabled || ctx->fault_event.enabled || ctx->protected_run || !ctx->graph_mode)
     return run_nodes_eager(ctx, 0, ctx->header.num_nodes, g_prof_enabled > 0);
   if (ctx->graph_dirty && !ctx->validated) {
     int rc = run_nodes_eager(ctx, 0, ctx->header.num_nodes, false);
@@ -454,8 +554,14 @@ int spkv2_prepare_with_scratch(Spkv2Context *ctx, void *arena, size_t arena_size
   int major = 0;
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, ctx->device);
   if (major != 10) return SPKV2_ERR_NO_DEVICE;  // kernels are built for sm_100a only
-  for (size_t i = 0; i < ctx->protection_count; ++i)
-    if (ctx->protection_records[i].mode != SPKV2_PROTECT_NONE) return SPKV2_ERR_PROTECTION;
+  ctx->protection_of_node.assign(ctx->header.num_nodes, -1);
+  ctx->protected_run = false;
+  for (size_t i = 0; i < ctx->protection_count; ++i) {
+    const Spkv2ProtectionRecord &r = ctx->protection_records[i];
+    if (r.node_id < ctx->header.num_nodes && ctx->protection_of_node[r.node_id] < 0)
+      ctx->protection_of_node[r.node_id] = int32_t(i);
+    ctx->protected_run |= r.mode != SPKV2_PROTECT_NONE;
+  }
 
   if ((rc = cuda_status(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)))) return rc;
 
@@ -507,6 +613,13 @@ int spkv2_prepare_with_scratch(Spkv2Context *ctx, void *arena, size_t arena_size
     return SPKV2_ERR_DEVICE_ALLOC;
   }
   cudaMemsetAsync(ctx->d_status, 0, sizeof(int) * 4, ctx->stream);
+  if (ctx->protected_run) {
+    ctx->d_guard = static_cast<uint32_t *>(device_alloc(sizeof(uint32_t) * 8));
+    if (!ctx->d_guard) {
+      release_device_state(ctx);
+      return SPKV2_ERR_DEVICE_ALLOC;
+    }
+  }
 
   for (uint32_t i = 0; i < ctx->header.num_tensors; ++i) {
     TensorState &t = ctx->tensors[i];
@@ -843,7 +956,7 @@ const char *spkv2_cuda_status_string(int code) {
     case SPKV2_ERR_UNSUPPORTED: return "node variant unsupported on the CUDA target";
     case SPKV2_ERR_LAUNCH: return "kernel launch failed";
     case SPKV2_ERR_NOT_PREPARED: return "context not prepared";
-    case SPKV2_ERR_PROTECTION: return "protection plans are not supported on the CUDA target";
+    case SPKV2_ERR_PROTECTION: return "protection plan error";
     case SPKV2_ERR_DEVICE_STATUS: return "device kernel reported a timeout or an out-of-range index";
     default: return (code <= -20 && code >= -26) ? "fault or protection error" : "unknown";
   }

@@ -61,6 +61,20 @@ def main():
             data = Path(d, "m.spk").read_bytes()
         out["packages"][f"{name}_b{batch}"] = {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data)}
         print(name, batch, len(data), flush=True)
+    # LeNet-5 with the protection plan of builders.LENET5_PROTECTION, through
+    # the reference protection-plan encoder and writer.
+    from compiler.reliability.protection_plan import ProtectionEntry as RefEntry  # noqa: E402
+    from compiler.reliability.protection_plan import ProtectionPlan as RefPlan  # noqa: E402
+
+    rgraph = to_reference_graph(builders.build_config("lenet5", 1))
+    ref_passes(rgraph, profile=prof)
+    entries = tuple(RefEntry(**e) for e in builders.lenet5_protection_entries(rgraph))
+    with tempfile.TemporaryDirectory() as d:
+        ref_write(rgraph, d + "/m.spk", prof, kernel_plan=ref_specs(rgraph, prof),
+                  memory_plan=ref_plan(rgraph, max_arena_bytes=prof["memory"]["activation_arena_max"]),
+                  protection_plan=RefPlan(version=1, model_id="lenet5", nodes=entries))
+        data = Path(d, "m.spk").read_bytes()
+    out["protected"] = {"lenet5_b1": {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data)}}
     # Reference weight quantiser on the fused ResNet-50 graph.
     rgraph = to_reference_graph(builders.build_config("resnet50", 1))
     ref_passes(rgraph, profile=prof)
