@@ -16,6 +16,11 @@
 //   AMODE 3  im2col TMA (C % 128 == 0, square kernel): one tensor-map load
 //            per K step brings 128 output pixels x 128 channels of one
 //            filter tap, padding and image edges zero-filled by the TMA unit.
+//   AMODE 5  im2col TMA for C == 64 (square kernel): a K step is two filter
+//            taps, each loaded by its own im2col TMA (128 pixels x 64
+//            channels, 64-byte swizzle) into one half of the A stage; the
+//            MMAs read the halves through 64-byte-swizzle descriptors.  A tap
+//            past the filter reads an image past the batch (zeros).
 //   AMODE 2  tiled TMA (1x1, stride 1, no padding).
 //   AMODE 1  cp.async gathers by warps 4-7 (C % 16 == 0), 16 channels of one
 //            tap per 16-byte chunk, straight into the operand stage; each
@@ -28,9 +33,12 @@
 // epilogue overlaps the next tile's MMAs.
 // Epilogue with dense NHWC int8 output: each warp's 32 rows x CW columns go
 // through a shared-memory tile: the residual tile (if any) is TMA-loaded
-// into it when the warp starts the tile (before it waits for the
-// accumulator), the requantised bytes overwrite it, and one TMA store writes
-// it out.  Other outputs (strided, int32) use per-thread stores.
+// into it, the requantised bytes overwrite it, and one TMA store writes it
+// out.  With a residual the warp keeps two such tiles (RB = 2) and loads
+// the residual of its NEXT tile while it requantises this one, so the
+// residual's HBM latency is not paid once per tile (1x1 convs with K <= 128
+// have little MMA work to hide it behind).  Other outputs (strided, int32)
+// use per-thread stores.
 // Every wait is bounded; on timeout the CTA records a code in the status
 // word and winds down.
 #include <stdlib.h>
@@ -72,7 +80,7 @@ constexpr int epi_warps() {
   return AMODE == 1 ? 4 : 8;
 }
 
-template <int BN, int STAGES, int AMODE>
+template <int BN, int STAGES, int AMODE, int RB>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_i8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap ymap, const __grid_constant__ CUtensorMap rmap,
@@ -87,9 +95,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int STAGE = kABytes + B_BYTES;
   constexpr int kCols = 2 * BN;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
-  uint8_t *staging = smem + STAGES * STAGE;  // EPIW x (32 rows x CW bytes)
+  uint8_t *staging = smem + STAGES * STAGE;  // EPIW x RB x (32 rows x CW bytes)
   __shared__ uint64_t raw_bar[STAGES], full_bar[STAGES], empty_bar[STAGES], accf_bar[2], acce_bar[2];
-  __shared__ uint64_t res_bar[EPIW];
+  __shared__ uint64_t res_bar[EPIW * RB];
   __shared__ uint32_t tmem_base_holder;
   __shared__ volatile int abort_flag;
 
@@ -106,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&accf_bar[b], 1);
       mbar_init(&acce_bar[b], 32 * EPIW);
     }
-    for (int w = 0; w < EPIW; ++w) mbar_init(&res_bar[w], 1);
+    for (int w = 0; w < EPIW * RB; ++w) mbar_init(&res_bar[w], 1);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -132,28 +140,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool vec_out = g.ys[1] == 1 && (g.M % 16) == 0;
     const bool vec_res = g.has_res && g.rs[1] == 1 && (g.M % 16) == 0;
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
-    uint8_t *stile = staging + warp * (32 * CW);
+    const bool res_tma = tp.epi_tma && g.has_res;
+    // Residual tile of tile tt into this warp's staging buffer b (lane 0);
+    // issued[b] counts the loads into buffer b.
+    int issued[RB] = {};
+    auto load_res = [&](int64_t tt, int b) {
+      const int tn0 = int(tt % tp.n_tiles) * BN;
+      const int64_t trow0 = (tt / tp.n_tiles) * kBM + quarter * 32;
+      mbar_arrive_expect_tx(&res_bar[warp * RB + b], 32 * CW);
+      tma_load_2d(staging + (warp * RB + b) * (32 * CW), &rmap, tn0 + col0, int(trow0), &res_bar[warp * RB + b]);
+      ++issued[b];
+    };
+    if (RB == 2 && res_tma && lane == 0 && int64_t(blockIdx.x) < tp.tiles) load_res(blockIdx.x, 0);
+    __syncwarp();
     int ti = 0;
+    bool failed = false;
     for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x, ++ti) {
       const int n0 = int(t % tp.n_tiles) * BN;
       const int64_t m0 = (t / tp.n_tiles) * kBM;
       const int64_t row0 = m0 + quarter * 32;  // first output pixel of this warp
       const int ab = ti & 1;
+      const int rb = RB == 2 ? (ti & 1) : 0;  // staging buffer of this tile
+      uint8_t *stile = staging + (warp * RB + rb) * (32 * CW);
       if (tp.epi_tma) {
-        // The staging tile is free once the previous tile's store has read
-        // it; then the residual tile starts loading into it.
+        // A staging tile is free once the store that last used it has read
+        // it (only the previous tile's store can still be pending); then a
+        // residual load may start into it: this tile's (RB = 1) or the next
+        // tile's, into the other buffer (RB = 2).
         if (lane == 0) {
           tma_store_wait_read0();
-          if (g.has_res) {
-            mbar_arrive_expect_tx(&res_bar[warp], 32 * CW);
-            tma_load_2d(stile, &rmap, n0 + col0, int(row0), &res_bar[warp]);
-          }
+          if (res_tma && RB == 1) load_res(t, 0);
+          if (res_tma && RB == 2 && t + gridDim.x < tp.tiles) load_res(t + gridDim.x, rb ^ 1);
         }
         __syncwarp();
       }
-      if (!mbar_wait(&accf_bar[ab], (ti >> 1) & 1, &abort_flag, status, 4)) break;
+      if (!mbar_wait(&accf_bar[ab], (ti >> 1) & 1, &abort_flag, status, 4)) {
+        failed = true;
+        break;
+      }
       tc_fence_after();
-      if (tp.epi_tma && g.has_res && !mbar_wait(&res_bar[warp], ti & 1, &abort_flag, status, 6)) break;
+      if (res_tma && !mbar_wait(&res_bar[warp * RB + rb], (RB == 2 ? (ti >> 1) : ti) & 1, &abort_flag, status, 6)) {
+        failed = true;
+        break;
+      }
       const int64_t p = row0 + lane;
       const bool pv = p < g.P;
       int n = 0, oh = 0, ow = 0;
@@ -249,6 +278,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && row0 < g.P && n0 + col0 < g.M) tma_store_2d(&ymap, n0 + col0, int(row0), stile);
       }
     }
+    if (failed && res_tma && lane == 0) {
+      // Giving up: let this warp's residual loads that may still be in
+      // flight land (bounded) before the CTA's shared memory goes away.
+#pragma unroll
+      for (int b = 0; b < RB; ++b) {
+        if (issued[b] == 0) continue;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&res_bar[warp * RB + b], uint32_t(issued[b] - 1) & 1u) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
     if (tp.epi_tma && lane == 0) tma_store_wait_all();
   } else if (AMODE == 1 && warp < 8) {
     // ------------------------------------------------------------ A gathers
@@ -315,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = int(t % tp.n_tiles) * BN;
         const int64_t m0 = (t / tp.n_tiles) * kBM;
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
-        if (AMODE == 3) {
+        if (AMODE == 3 || AMODE == 5) {
           const int ow = int(m0 % g.OW);
           const int64_t q = m0 / g.OW;
           bw = ow * g.sw - g.pw;
@@ -335,6 +375,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tap = k0 / g.C, c0 = k0 - tap * g.C;  // C % 128 == 0: one tap per K step
             const int r = tap / g.KW, sx = tap - r * g.KW;
             tma_load_im2col_4d(a_st, &amap, c0, bw, bh, bn, uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+          }
+          if (AMODE == 5) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int tap = 2 * kb + j;
+              const bool real = tap < g.KH * g.KW;
+              const int r = real ? tap / g.KW : 0, sx = real ? tap - r * g.KW : 0;
+              tma_load_im2col_4d(a_st + j * (kABytes / 2), &amap, 0, bw, bh, real ? bn : g.N, uint16_t(sx * g.dw),
+                                 uint16_t(r * g.dh), &raw_bar[s]);
+            }
           }
         }
       }
@@ -370,7 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint64_t step = uint64_t(kk * 32) >> 4;  // 32 int8 = 32 bytes along K
-          mma_i8(dtm, da + step, db + step, idesc, (kb | kk) ? 1u : 0u);
+          // AMODE 5: slices 0-1 in the first 64-byte-row half, 2-3 in the second.
+          const uint64_t a = AMODE == 5 ? smem_desc_sw64(a_st + (kk >> 1) * (kABytes / 2)) + uint64_t((kk & 1) * 32 >> 4)
+                                        : da + step;
+          mma_i8(dtm, a, db + step, idesc, (kb | kk) ? 1u : 0u);
         }
         mma_commit(&empty_bar[s]);
         if (++kb == num_kb) {
@@ -416,13 +469,17 @@ __global__ void pack_i8_kernel(int8_t *__restrict__ dst, const int8_t *__restric
   }
 }
 
-constexpr int stages_of(int bn) { return bn == 256 ? 4 : bn == 128 ? 6 : 8; }
-constexpr size_t smem_of(int bn) { return size_t(stages_of(bn)) * (kABytes + bn * kBK) + size_t(128) * bn + 1024; }
+// Operand stages and shared memory per tile width and residual buffers.
+constexpr int stages_of(int bn, int rb) { return bn == 256 ? (rb == 2 ? 3 : 4) : bn == 128 ? 6 : 8; }
+constexpr size_t smem_of(int bn, int rb) {
+  return size_t(stages_of(bn, rb)) * (kABytes + bn * kBK) + size_t(rb) * 128 * bn + 1024;
+}
 
 struct I8State {
   CUtensorMap wmap, amap, ymap, rmap;
   I8Params tp;
   int bn = 128, amode = 1, grid = 148;
+  int rb = 1;  // epilogue staging buffers per warp (2: residual prefetch)
   size_t smem = 0;
   bool set_attr_only = false;
   const void *x_base = nullptr, *y_base = nullptr, *r_base = nullptr;  // pointers the maps were encoded for
@@ -435,6 +492,9 @@ bool encode_a(const I8State &st, CUtensorMap *map, const void *x) {
   if (st.amode == 3)
     return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
                               kBK, kBM);
+  if (st.amode == 5)
+    return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, g.N, g.H, g.W, g.C, g.KH, g.sh, g.ph, g.dh,
+                              64, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
 }
 
@@ -448,10 +508,10 @@ struct Maps {
   CUtensorMap a, y, r;
 };
 
-template <int BN, int AMODE>
+template <int BN, int AMODE, int RB>
 int launch_cfg(const I8State &st, const Maps &mp, const ConvPlan &p, const void *x, void *y, const void *res,
                int *status, cudaStream_t s) {
-  auto kern = conv_i8_kernel<BN, stages_of(BN), AMODE>;
+  auto kern = conv_i8_kernel<BN, stages_of(BN, RB), AMODE, RB>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
   return cuda_status(launch_kernel(kern, unsigned(st.grid), kThreads, st.smem, s, 1, st.wmap, mp.a, mp.y, mp.r,
@@ -462,10 +522,19 @@ int launch_cfg(const I8State &st, const Maps &mp, const ConvPlan &p, const void 
 template <int BN>
 int launch_bn(const I8State &st, const Maps &mp, const ConvPlan &p, const void *x, void *y, const void *res,
               int *status, cudaStream_t s) {
+  if (st.rb == 2) {
+    switch (st.amode) {
+      case 5: return launch_cfg<BN, 5, 2>(st, mp, p, x, y, res, status, s);
+      case 3: return launch_cfg<BN, 3, 2>(st, mp, p, x, y, res, status, s);
+      case 2: return launch_cfg<BN, 2, 2>(st, mp, p, x, y, res, status, s);
+      default: return launch_cfg<BN, 1, 2>(st, mp, p, x, y, res, status, s);
+    }
+  }
   switch (st.amode) {
-    case 3: return launch_cfg<BN, 3>(st, mp, p, x, y, res, status, s);
-    case 2: return launch_cfg<BN, 2>(st, mp, p, x, y, res, status, s);
-    default: return launch_cfg<BN, 1>(st, mp, p, x, y, res, status, s);
+    case 5: return launch_cfg<BN, 5, 1>(st, mp, p, x, y, res, status, s);
+    case 3: return launch_cfg<BN, 3, 1>(st, mp, p, x, y, res, status, s);
+    case 2: return launch_cfg<BN, 2, 1>(st, mp, p, x, y, res, status, s);
+    default: return launch_cfg<BN, 1, 1>(st, mp, p, x, y, res, status, s);
   }
 }
 
@@ -490,6 +559,8 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
     st->amode = 2;
   else if (square && g.C % kBK == 0 && encode_im2col_fn())
     st->amode = 3;
+  else if (square && g.C == 64 && encode_im2col_fn() && !getenv("SPKV2_I8_NO_IM2COL64"))
+    st->amode = 5;
   else
     st->amode = 1;
   int sms = 148, dev = 0;
@@ -540,7 +611,8 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
-  st->smem = smem_of(bn);
+  st->rb = (tp.epi_tma && g.has_res && !getenv("SPKV2_I8_NO_RES_PREFETCH")) ? 2 : 1;
+  st->smem = smem_of(bn, st->rb);
   p.w_tc = wp;
   p.tc_state = st;
   p.tc_i8 = true;
@@ -550,9 +622,9 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
   rc = conv_tc_i8_launch(p, nullptr, nullptr, nullptr, nullptr, s);
   st->set_attr_only = false;
   if (rc) return rc;
-  static const char *amodes[] = {"", "_cpasync", "_tma", "_im2col"};
+  static const char *amodes[] = {"", "_cpasync", "_tma", "_im2col", "", "_im2col64"};
   p.variant = std::string("tc_int8_bn") + std::to_string(bn) + amodes[st->amode] + (tp.epi_tma ? "_tmastore" : "") +
-              (tp.out_i32 ? "_i32out" : "");
+              (st->rb == 2 ? "_resprefetch" : "") + (tp.out_i32 ? "_i32out" : "");
   return 0;
 }
 

@@ -134,6 +134,14 @@ __device__ __forceinline__ uint64_t smem_desc(const void *p) {
   return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// K-major, 64B-swizzled operand (rows of 64 bytes): SBO = 512 B between
+// 8-row groups, layout type 4 (64-byte swizzle); the tile must start on a
+// 512-byte boundary.
+__device__ __forceinline__ uint64_t smem_desc_sw64(const void *p) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (uint64_t(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
+}
+
 // K-major operand without swizzle, in 8-row x 16-byte core matrices: `lbo`
 // bytes between core matrices along K, `sbo` bytes between 8-row groups.
 __device__ __forceinline__ uint64_t smem_desc_noswz(const void *p, uint32_t lbo, uint32_t sbo) {
