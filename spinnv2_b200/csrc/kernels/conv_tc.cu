@@ -81,7 +81,8 @@ struct TcParams {
   int out_i8;      // quantise the output: y = clamp(rne(act(v) * (1 / s_y)), -128, 127)
   int res_tma;     // residual tiles arrive by TMA in the epilogue staging tile (NHWC residual, TMA store)
   int64_t dp_tiles;  // tiles walked whole, round-robin over the CTAs (all tiles without stream-K)
-  int64_t sk_units;  // stream-K: K steps of tiles dp_tiles.. spread evenly over the CTAs (0: off)
+  int64_t sk_units;  // stream-K: K steps of tiles dp_tiles.. spread evenly over CTAs 0..sk_ctas-1 (0: off)
+  int sk_ctas;       // CTAs sharing the stream-K units (fewer CTAs: fewer segments per tile to add up)
 };
 
 // One unit of a CTA's work: K steps [kb0, kb1) of output tile `tile`.  A
@@ -100,8 +101,9 @@ struct Seg {
 // The static schedule every role of a CTA walks in the same order: whole
 // tiles tile0, tile0 + tstep, ... below dp_tiles, then this CTA's contiguous
 // share [u0, u1) of the remaining tiles' K steps (unit u = K step u % nk of
-// stream-K tile u / nk), cut at tile boundaries.  SK = false compiles the
-// whole-tile schedule only (kernels that never use stream-K).
+// stream-K tile u / nk), cut at tile boundaries; only CTAs below sk_ctas
+// take a share.  SK = false compiles the whole-tile schedule only (kernels
+// that never use stream-K).
 template <bool SK>
 struct WorkIter {
   int64_t t, tstep, dp_tiles;
@@ -109,9 +111,9 @@ struct WorkIter {
   int nk, G, b;
   __device__ WorkIter(const TcParams &tp, int64_t tile0, int64_t step, int cta, int grid)
       : t(tile0), tstep(step), dp_tiles(SK ? tp.dp_tiles : tp.tiles), U(SK ? tp.sk_units : 0), nk(tp.num_kb),
-        G(grid), b(cta) {
-    u0 = U ? int64_t(b) * U / G : 0;
-    u1 = U ? int64_t(b + 1) * U / G : 0;
+        G(SK && tp.sk_units ? tp.sk_ctas : grid), b(cta) {
+    u0 = U ? (b < G ? int64_t(b) * U / G : U) : 0;
+    u1 = U ? (b < G ? int64_t(b + 1) * U / G : U) : 0;
     u = u0;
   }
   __device__ int64_t start_of(int64_t cta) const { return cta * U / G; }
@@ -1151,14 +1153,36 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   // writing and re-reading the partial tiles costs more than it saves.
   tp.dp_tiles = tp.tiles;
   tp.sk_units = 0;
+  tp.sk_ctas = sms;
   if (ok && st->split3 && !st->pair && !getenv("SPKV2_TC_NO_STREAMK")) {
+    // Critical path in K steps: whole rounds, then the CTA's share of the
+    // tail, then the fix-up, which adds up the tile's segments (about
+    // Gs / tail + 1 of them) one L2 round trip per segment and 32-column
+    // chunk (about a K step per segment), plus a fixed cost for parking the
+    // partial and counting the arrival.  The number of CTAs Gs that share
+    // the tail trades the share against the segment count: a few tiles over
+    // all 148 SMs (batch 1) would leave each tile ~40 segments to add up.
     const int64_t nk = tp.num_kb, rounds = tp.tiles / sms, tail = tp.tiles % sms;
     const double dp_steps = double(rounds + (tail ? 1 : 0)) * nk;
-    const double sk_share = double(tail) * nk / sms;  // K steps per CTA for the tail
-    const double sk_steps = double(rounds) * nk + ceil(sk_share) + 4;  // + fix-up, in K steps
-    if (tail > 0 && sk_share >= 2 && sk_steps < 0.9 * dp_steps) {
+    constexpr double kFixPerSeg = 1.0, kFixBase = 2.0;
+    double best = 0.9 * dp_steps;
+    int best_g = 0;
+    for (int64_t segs = 2; tail > 0 && segs <= 64; ++segs) {
+      const int64_t gs = std::min<int64_t>(sms, tail * segs);
+      const double share = ceil(double(tail * nk) / double(gs));
+      const double nseg = ceil(double(gs) / double(tail)) + 1.0;
+      const double cost = double(rounds) * nk + share + kFixBase + kFixPerSeg * nseg;
+      if (share >= 1 && cost < best) {
+        best = cost;
+        best_g = int(gs);
+      }
+      if (gs == sms) break;
+    }
+    if (const char *e = getenv("SPKV2_TC_SK_CTAS")) best_g = tail > 0 ? std::min(sms, std::max(1, atoi(e))) : 0;
+    if (best_g > 0) {
       tp.dp_tiles = rounds * sms;
       tp.sk_units = tail * nk;
+      tp.sk_ctas = best_g;
       st->grid = sms;
       st->sk_cnt_bytes = size_t(tail) * kEpiWarps * sizeof(int);
       st->sk_cnt = static_cast<int *>(device_alloc(st->sk_cnt_bytes));
