@@ -295,6 +295,7 @@ def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80
 OP_CASES = (
     "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
     "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
+    "topk_ties", "topk_smallest",
 )
 
 
@@ -369,6 +370,22 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
         x = pre([n, 10, 6, 7])
         idx = b.input("indices", [4])
         return post(b.op("Gather", [x, idx], [n, 10, 6, 4], {"axis": 3}))
+    if case == "topk_ties":
+        # Integer-valued scores (Mod of a scaled input): many equal values,
+        # so the order among ties (smaller index first) is exercised.
+        x = b.input("input", [n, 4, 500])
+        y = b.op("Mul", [x, net.const("scale", [7.0])], [n, 4, 500])
+        y = b.op("Mod", [y, net.const("m", [3.0])], [n, 4, 500])
+        vals, idx = b.node("TopK", [y, net.const("k", [37])], [[n, 4, 37], [n, 4, 37]], {"axis": -1, "largest": 1})
+        b.mark_output(vals)
+        b.mark_output(idx)
+        return b.graph
+    if case == "topk_smallest":
+        x = pre([n, 3, 1000])
+        vals, idx = b.node("TopK", [x, net.const("k", [100])], [[n, 3, 100], [n, 3, 100]], {"axis": 2, "largest": 0})
+        b.mark_output(vals)
+        b.mark_output(idx)
+        return b.graph
     if case == "unsqueeze":
         x = pre([n, 8, 6])
         return post(b.op("Unsqueeze", [x], [n, 8, 1, 6], {"axes": [2]}))

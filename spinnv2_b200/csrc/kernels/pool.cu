@@ -135,6 +135,58 @@ __global__ void maxpool_nhwc4_kernel(float *__restrict__ y, const float *__restr
   }
 }
 
+// Stride-1 max pool (the SPPF 5x5 windows), NHWC fp32, C % 4 == 0: thread
+// (n, c4, ow) walks its output column down the image keeping the maxima of
+// the last KH input rows (each over the KW window columns) in registers, so
+// each output costs one new row's KW loads instead of KH x KW.  Max is
+// order-independent, so results equal the direct window scan; rows and
+// columns outside the image are skipped as there.
+template <int KH>
+__global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__restrict__ x, Geo g, int64_t columns) {
+  const int C4 = g.C / 4;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < columns; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c4 = int(r % C4);
+    r /= C4;
+    const int ow = int(r % g.OW);
+    const int n = int(r / g.OW);
+    const float *xb = x + int64_t(n) * g.H * g.W * g.C + c4 * 4;
+    float4 *yb = reinterpret_cast<float4 *>(y + int64_t(n) * g.OH * g.OW * g.C + int64_t(ow) * g.C + c4 * 4);
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    auto row_max = [&](int ih) {
+      float4 best = ninf;
+      if (ih < 0 || ih >= g.H) return best;
+      for (int s = 0; s < g.kw; ++s) {
+        const int iw = ow + s - g.pw;
+        if (iw < 0 || iw >= g.W) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(xb + (int64_t(ih) * g.W + iw) * g.C);
+        best.x = v.x > best.x ? v.x : best.x;
+        best.y = v.y > best.y ? v.y : best.y;
+        best.z = v.z > best.z ? v.z : best.z;
+        best.w = v.w > best.w ? v.w : best.w;
+      }
+      return best;
+    };
+    float4 rm[KH];  // rm[j]: max of input row oh - ph + j
+#pragma unroll
+    for (int j = 0; j + 1 < KH; ++j) rm[j + 1] = row_max(j - g.ph);
+    for (int oh = 0; oh < g.OH; ++oh) {
+#pragma unroll
+      for (int j = 0; j + 1 < KH; ++j) rm[j] = rm[j + 1];
+      rm[KH - 1] = row_max(oh - g.ph + KH - 1);
+      float4 best = rm[0];
+#pragma unroll
+      for (int j = 1; j < KH; ++j) {
+        best.x = rm[j].x > best.x ? rm[j].x : best.x;
+        best.y = rm[j].y > best.y ? rm[j].y : best.y;
+        best.z = rm[j].z > best.z ? rm[j].z : best.z;
+        best.w = rm[j].w > best.w ? rm[j].w : best.w;
+      }
+      yb[int64_t(oh) * g.OW * C4] = best;
+    }
+  }
+}
+
 // Both tensors NHWC int8, C % 16 == 0: 16 channels (one 16-byte load) per
 // thread, per-byte signed max on 32-bit words; an empty window gives -128.
 __global__ void maxpool_nhwc16_i8_kernel(int8_t *__restrict__ y, const int8_t *__restrict__ x, Geo g,
@@ -287,7 +339,9 @@ int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 16 == 0 &&
       reinterpret_cast<uintptr_t>(tx.data) % 16 == 0 && reinterpret_cast<uintptr_t>(ty.data) % 16 == 0)
     p->vec = 16;
-  p->variant = p->vec == 4 ? "maxpool_nhwc_vec4" : p->vec == 16 ? "maxpool_nhwc_i8_vec16" : "pool_generic";
+  p->variant = p->vec == 4 ? (g.sh == 1 && g.sw == 1 && (g.kh == 3 || g.kh == 5 || g.kh == 7) ? "maxpool_nhwc_vec4_s1rows"
+                                                                                             : "maxpool_nhwc_vec4")
+               : p->vec == 16 ? "maxpool_nhwc_i8_vec16" : "pool_generic";
   set_node_plan(ctx, node, p);
   return 0;
 }
@@ -303,7 +357,20 @@ int pool_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   const void *x = ctx->tensors[node->inputs[0]].data;
   // Vector paths need 16-byte aligned tensors (a rebinding may move them).
   const bool aligned = (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0;
-  if (p->vec == 4 && aligned) {
+  const bool s1 = g.sh == 1 && g.sw == 1 && (g.kh == 3 || g.kh == 5 || g.kh == 7);
+  if (p->vec == 4 && aligned && s1) {
+    const int64_t columns = int64_t(g.N) * (g.C / 4) * g.OW;
+    const int grid = grid_for(columns, 128);
+    if (g.kh == 3)
+      maxpool_nhwc4_s1_kernel<3><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
+                                                                   static_cast<const float *>(x), g, columns);
+    else if (g.kh == 5)
+      maxpool_nhwc4_s1_kernel<5><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
+                                                                   static_cast<const float *>(x), g, columns);
+    else
+      maxpool_nhwc4_s1_kernel<7><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
+                                                                   static_cast<const float *>(x), g, columns);
+  } else if (p->vec == 4 && aligned) {
     maxpool_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
         static_cast<float *>(y), static_cast<const float *>(x), g, total / 4);
   } else if (p->vec == 16 && aligned) {

@@ -13,11 +13,13 @@
 //           indices sorted (descending if largest), ties to the smaller index,
 //           equal values at the k-th place keep the earlier indices
 // Device design: reductions run one thread per output element looping over
-// the reduced index space in the reference's order (bit-exact with it); the
+// the reduced index space in the reference's order (bit-exact with it;
+// adjacent reduced axes forming one strided run are walked as one); the
 // threads of a warp take adjacent outputs, so NHWC global pooling reads
 // coalesce along C.  Softmax uses a warp per row when the axis is innermost.
-// TopK sorts each row's (value, index) keys with a shared-memory bitonic
-// sort, one block per row.
+// TopK (one block per row) radix-selects the k smallest (value, index) keys
+// and sorts those (k <= 2048), else bitonic-sorts the whole row in shared
+// memory.
 #include <string.h>
 
 #include "common.cuh"
@@ -58,23 +60,22 @@ __global__ void reduce_kernel(float *__restrict__ y, const float *__restrict__ x
     }
     float acc = IS_MAX ? -INFINITY : 0.0f;
     if (d.red_rank == 1) {
-      // One reduced axis: a strided walk, four loads in flight; the
-      // accumulation order stays r = 0, 1, 2, ... as in the reference.
+      // One reduced axis (adjacent reduced axes are merged at prepare): a
+      // strided walk, eight loads in flight; the accumulation order stays
+      // r = 0, 1, 2, ... as in the reference.
       const int64_t st = d.red_xstride[0];
       const float *p = x + xb;
       int64_t r = 0;
-      for (; r + 4 <= red_count; r += 4) {
-        const float v0 = p[r * st], v1 = p[(r + 1) * st], v2 = p[(r + 2) * st], v3 = p[(r + 3) * st];
-        if (IS_MAX) {
-          acc = v0 > acc ? v0 : acc;
-          acc = v1 > acc ? v1 : acc;
-          acc = v2 > acc ? v2 : acc;
-          acc = v3 > acc ? v3 : acc;
-        } else {
-          acc += v0 / d.denom;
-          acc += v1 / d.denom;
-          acc += v2 / d.denom;
-          acc += v3 / d.denom;
+      for (; r + 8 <= red_count; r += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[(r + j) * st];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (IS_MAX)
+            acc = v[j] > acc ? v[j] : acc;
+          else
+            acc += v[j] / d.denom;
         }
       }
       for (; r < red_count; ++r) {
@@ -116,6 +117,22 @@ __global__ void reduce_mean_i8_kernel(float *__restrict__ y, const int8_t *__res
       yo += c * d.keep_ystride[k];
     }
     int32_t acc = 0;
+    if (d.red_rank == 1) {
+      // Integer sums are exact in any order: eight loads in flight.
+      const int64_t st = d.red_xstride[0];
+      const int8_t *p = x + xb;
+      int64_t r = 0;
+      for (; r + 8 <= red_count; r += 8) {
+        int v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[(r + j) * st];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc += v[j];
+      }
+      for (; r < red_count; ++r) acc += p[r * st];
+      y[yo] = __fmul_rn(float(acc), factor);
+      continue;
+    }
     for (int64_t r = 0; r < red_count; ++r) {
       int64_t rr = r, xo = xb;
       for (int k = d.red_rank - 1; k >= 0; --k) {
@@ -182,6 +199,8 @@ struct TopkPlan : NodePlan {
   int64_t outer = 1, dim = 1, inner = 1, k = 0;
   int largest = 1;
   int pow2 = 1;
+  bool select = false;  // radix select + sort of k keys (k <= kSelectMax)
+  int sel_pow2 = 1;
   int64_t x_axis_stride = 1;
 };
 
@@ -226,6 +245,110 @@ __global__ void topk_kernel(float *__restrict__ values, float *__restrict__ indi
   for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
     const unsigned long long key = keys[j];
     const uint32_t idx = static_cast<uint32_t>(key & 0xffffffffu);
+    values[(o * k + j) * inner + in] = xr[int64_t(idx) * inner];
+    indices[(o * k + j) * inner + in] = float(idx);
+  }
+}
+
+// TopK by radix select, for k <= kSelectMax: the same (value, index) keys
+// as topk_kernel (unique, so the k smallest keys are exactly the answer),
+// the k-th smallest key found byte by byte from the top with 256-bin
+// histograms over the keys that still share the chosen prefix (stopping as
+// soon as the chosen bin holds exactly the keys still needed), then only
+// the selected keys sorted (bitonic, next power of two >= k).
+constexpr int kSelectMax = 2048;
+
+__global__ void __launch_bounds__(1024) topk_select_kernel(float *__restrict__ values, float *__restrict__ indices,
+                                                           const float *__restrict__ x, int64_t dim, int64_t inner,
+                                                           int k, int largest, int sel_pow2) {
+  extern __shared__ unsigned long long keys[];  // dim keys
+  __shared__ unsigned long long sel[kSelectMax];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_bin, s_before, s_cnt, s_count;
+  const int64_t row = blockIdx.x;
+  const int64_t o = row / inner, in = row % inner;
+  const float *xr = x + o * dim * inner + in;
+  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+    uint32_t hi = float_order_key(xr[i * inner]);
+    if (largest) hi = ~hi;
+    keys[i] = (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(i);
+  }
+  unsigned long long hi_mask = 0, hi_val = 0;  // top bits fixed so far
+  uint32_t remaining = uint32_t(k);             // rank of the k-th key among the candidates
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+      const unsigned long long key = keys[i];
+      if ((key & hi_mask) == hi_val) atomicAdd(&hist[uint32_t(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // Warp 0: bin b with before(b) < remaining <= before(b) + hist[b].
+      const int lane = threadIdx.x;
+      uint32_t c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[lane * 8 + j];
+        tot += c[j];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      uint32_t before = incl - tot;
+      if (before < remaining && remaining <= incl) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (before < remaining && remaining <= before + c[j]) {
+            s_bin = uint32_t(lane * 8 + j);
+            s_before = before;
+            s_cnt = c[j];
+          }
+          before += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    remaining -= s_before;
+    hi_mask |= 0xffull << shift;
+    hi_val |= static_cast<unsigned long long>(s_bin) << shift;
+    const bool done = s_cnt == remaining;  // the whole bin is selected
+    __syncthreads();                       // everyone has read s_* before the next pass writes them
+    if (done) break;
+  }
+  // Every key whose fixed top bits are <= the chosen prefix is selected: k keys.
+  if (threadIdx.x == 0) s_count = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+    const unsigned long long key = keys[i];
+    if ((key & hi_mask) <= hi_val) {
+      const uint32_t pos = atomicAdd(&s_count, 1u);
+      if (pos < uint32_t(kSelectMax)) sel[pos] = key;
+    }
+  }
+  __syncthreads();
+  for (int i = k + threadIdx.x; i < sel_pow2; i += blockDim.x) sel[i] = ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= sel_pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < sel_pow2 / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool ascending = (lo & size) == 0;
+        const unsigned long long a = sel[lo], b = sel[hi];
+        if ((a > b) == ascending) {
+          sel[lo] = b;
+          sel[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const uint32_t idx = static_cast<uint32_t>(sel[j] & 0xffffffffu);
     values[(o * k + j) * inner + in] = xr[int64_t(idx) * inner];
     indices[(o * k + j) * inner + in] = float(idx);
   }
@@ -293,6 +416,20 @@ int reduce_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Ke
     }
   }
   d.denom = denom;
+  // Adjacent reduced axes that are one strided run in memory (H, W of an
+  // NHWC or NCHW tensor) merge into one axis: the row-major walk over them
+  // visits the same elements in the same order.
+  for (int k = d.red_rank - 2; k >= 0; --k) {
+    if (d.red_xstride[k] == d.red_dim[k + 1] * d.red_xstride[k + 1]) {
+      d.red_dim[k] *= d.red_dim[k + 1];
+      d.red_xstride[k] = d.red_xstride[k + 1];
+      for (int j = k + 1; j + 1 < d.red_rank; ++j) {
+        d.red_dim[j] = d.red_dim[j + 1];
+        d.red_xstride[j] = d.red_xstride[j + 1];
+      }
+      d.red_rank--;
+    }
+  }
   p->outputs = 1;
   for (int k = 0; k < d.keep_rank; ++k) p->outputs *= d.keep_dim[k];
   if (p->int8_in) {
@@ -390,10 +527,20 @@ int topk_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     delete p;
     return SPKV2_ERR_UNSUPPORTED;
   }
-  const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  p->variant = "topk_bitonic";
+  if (p->k <= kSelectMax && !getenv("SPKV2_TOPK_FULL_SORT")) {
+    p->select = true;
+    p->sel_pow2 = 1;
+    while (p->sel_pow2 < p->k) p->sel_pow2 <<= 1;
+    const size_t smem = size_t(p->dim) * sizeof(unsigned long long);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    p->variant = "topk_radix_select";
+  } else {
+    const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    p->variant = "topk_bitonic";
+  }
   set_node_plan(ctx, node, p);
   return 0;
 }
@@ -404,6 +551,14 @@ int topk_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   if (p->k == 0 || p->dim == 0) return 0;
   const int64_t rows = p->outer * p->inner;
   if (rows == 0) return 0;
+  float *vals = reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data);
+  float *idx = reinterpret_cast<float *>(ctx->tensors[node->outputs[1]].data);
+  const float *xin = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
+  if (p->select) {
+    topk_select_kernel<<<unsigned(rows), 1024, size_t(p->dim) * sizeof(unsigned long long), ctx->stream>>>(
+        vals, idx, xin, p->dim, p->inner, int(p->k), p->largest, p->sel_pow2);
+    return cuda_status(cudaGetLastError());
+  }
   const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
   topk_kernel<<<unsigned(rows), 1024, smem, ctx->stream>>>(
       reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data),
