@@ -172,12 +172,18 @@ def conv_bytes(pkg, ids: list[int]) -> int:
     return total
 
 
-# DRAM bytes (read + write) of all Conv launches of one step, from one ncu
-# capture of `bench.py --steps 2 --warmup 3` (dram__bytes_read.sum +
-# dram__bytes_write.sum over the 105 conv launches of a step; the command is in
-# profiles/launches_resnet101_bs64_3xtf32.md).  Keyed by the workload it was
-# measured on; other workloads report null.
-MEASURED_CONV_TRAFFIC = {("resnet101", 64, "3xtf32", False): 6590.0e6 + 1538.7e6}
+# DRAM bytes (read + write) of the conv launches of one step, each from one
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
+# pass through the network:
+#   fp32: ncu ... -k regex:conv_tc_kernel -s 105 -c 105 python bench.py --steps 2 --warmup 3 --no-cpu-baseline
+#   int8: ncu ... -k regex:conv_i8 -s 52 -c 52 python bench.py --config resnet50 --int8 --batch 256
+#         --steps 2 --warmup 3 --no-cpu-baseline --latency-runs 5
+# Keyed by the workload it was measured on; other workloads report null.
+MEASURED_CONV_TRAFFIC = {
+    ("resnet101", 64, "3xtf32", False): 6590.0e6 + 1538.7e6,
+    # the 52 int8 conv launches of one ResNet-50 bs256 step
+    ("resnet50", 256, "int8", True): 3861.2e6 + 1179.7e6,
+}
 
 
 def use_all_host_threads() -> None:
