@@ -26,11 +26,13 @@
 //            tap per 16-byte chunk, straight into the operand stage; each
 //            thread publishes step it-(STAGES-1) (wait_group, proxy fence,
 //            mbarrier arrive) before it waits for the stage of step it.
-// Warp roles: warp 8 TMA producer (weights, and A in AMODE 2/3), warp 9 TMEM
-// allocation and the single-thread MMA issuer, epilogue warps 0-3 (AMODE 1)
-// or 0-7 (AMODE 2/3: warps w and w+4 share TMEM lanes 32(w%4).. and split
-// the tile's columns).  TMEM holds two accumulator buffers, so a tile's
-// epilogue overlaps the next tile's MMAs.
+// Warp roles: epilogue warps 0-3 (AMODE 1), 0-7, or 0-15 for TMA-fed A with
+// BN >= 128 (warps w, w+4, ... share TMEM lanes 32(w%4).. and split the
+// tile's columns); then the TMA producer warp (weights, and A in the TMA
+// modes) and the warp that allocates TMEM and issues the MMAs from one
+// thread (warps 8 and 9 with 4 or 8 epilogue warps, 16 and 17 with 16).
+// TMEM holds two accumulator buffers, so a tile's epilogue overlaps the
+// next tile's MMAs.
 // Epilogue with dense NHWC int8 output: each warp's 32 rows x CW columns go
 // through a shared-memory tile: the residual tile (if any) is TMA-loaded
 // into it, the requantised bytes overwrite it, and one TMA store writes it
@@ -56,7 +58,6 @@ using namespace tc;
 constexpr int kBM = 128;           // tile rows (pixels) = UMMA M
 constexpr int kBK = 128;           // int8 elements (bytes) per K step
 constexpr int kABytes = kBM * kBK;
-constexpr int kThreads = 320;
 
 struct I8Params {
   ConvGeo g;
@@ -75,13 +76,18 @@ __device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, in
          (uint32_t(uint8_t(sat_rne_i8(c, lo))) << 16) | (uint32_t(uint8_t(sat_rne_i8(d, lo))) << 24);
 }
 
-template <int AMODE>
-constexpr int epi_warps() {
-  return AMODE == 1 ? 4 : 8;
-}
+// Epilogue warps: 4 with gathered A (warps 4-7 gather), else 8, or 16 for
+// tiles of 128+ columns.  The requantising epilogue of a 1x1 conv with
+// K <= 128 runs longer than the tile's MMAs and is bound by instruction
+// latency; four warps per TMEM lane quarter (each with a quarter of the
+// columns) keep more of it in flight.  The TMA producer and the MMA warp
+// follow the epilogue (and gather) warps.
+constexpr int epi_warps(int bn, int amode) { return amode == 1 ? 4 : bn >= 128 ? 16 : 8; }
+constexpr int producer_warp(int bn, int amode) { return amode == 1 ? 8 : epi_warps(bn, amode); }
+constexpr int threads_of(int bn, int amode) { return (producer_warp(bn, amode) + 2) * 32; }
 
 template <int BN, int STAGES, int AMODE, int RB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
     conv_i8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap ymap, const __grid_constant__ CUtensorMap rmap,
                    const int8_t *__restrict__ x, const int32_t *__restrict__ bias_q,
@@ -89,7 +95,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    I8Params tp, int *status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int EPIW = epi_warps<AMODE>();
+  constexpr int EPIW = epi_warps(BN, AMODE);
+  constexpr int PROD_WARP = producer_warp(BN, AMODE), MMA_WARP = PROD_WARP + 1;
   constexpr int CW = BN * 4 / EPIW;  // columns (bytes) per epilogue warp
   constexpr int B_BYTES = BN * kBK;
   constexpr int STAGE = kABytes + B_BYTES;
@@ -118,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 9) {
+  if (warp == MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_holder)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -345,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t pit = first; pit < it; ++pit) publish(pit);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == PROD_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint32_t bytes = B_BYTES + (AMODE != 1 ? kABytes : 0);
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc =
@@ -449,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -485,7 +492,7 @@ struct I8State {
   const void *x_base = nullptr, *y_base = nullptr, *r_base = nullptr;  // pointers the maps were encoded for
 };
 
-int epi_cols(const I8State &st) { return st.bn * 4 / (st.amode == 1 ? 4 : 8); }
+int epi_cols(const I8State &st) { return st.bn * 4 / epi_warps(st.bn, st.amode); }
 
 bool encode_a(const I8State &st, CUtensorMap *map, const void *x) {
   const ConvGeo &g = st.tp.g;
@@ -514,7 +521,8 @@ int launch_cfg(const I8State &st, const Maps &mp, const ConvPlan &p, const void 
   auto kern = conv_i8_kernel<BN, stages_of(BN, RB), AMODE, RB>;
   if (st.set_attr_only)
     return cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(st.smem)));
-  return cuda_status(launch_kernel(kern, unsigned(st.grid), kThreads, st.smem, s, 1, st.wmap, mp.a, mp.y, mp.r,
+  return cuda_status(launch_kernel(kern, unsigned(st.grid), threads_of(BN, AMODE), st.smem, s, 1, st.wmap, mp.a,
+                                   mp.y, mp.r,
                                    static_cast<const int8_t *>(x), p.bias_q, p.scale_m,
                                    static_cast<const int8_t *>(res), y, st.tp, status));
 }
