@@ -175,12 +175,13 @@ def conv_bytes(pkg, ids: list[int]) -> int:
 # DRAM bytes (read + write) of the conv launches of one step, each from one
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
 # pass through the network:
-#   fp32: ncu ... -k regex:conv_tc_kernel -s 105 -c 105 python bench.py --steps 2 --warmup 3 --no-cpu-baseline
+#   fp32: ncu ... -c 560 python bench.py --steps 2 --warmup 3 --no-cpu-baseline --latency-runs 5
+#         (the 105 conv launches of launches 433..541)
 #   int8: ncu ... -k regex:conv_i8 -s 52 -c 52 python bench.py --config resnet50 --int8 --batch 256
 #         --steps 2 --warmup 3 --no-cpu-baseline --latency-runs 5
 # Keyed by the workload it was measured on; other workloads report null.
 MEASURED_CONV_TRAFFIC = {
-    ("resnet101", 64, "3xtf32", False): 6590.0e6 + 1538.7e6,
+    ("resnet101", 64, "3xtf32", False): 6591.0e6 + 1543.6e6,
     # the 52 int8 conv launches of one ResNet-50 bs256 step
     ("resnet50", 256, "int8", True): 3861.2e6 + 1179.7e6,
 }
