@@ -71,9 +71,24 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// Four requantised codes, a in the lowest byte: round to nearest even, then
+// clamp to [lo, 127] (lo = 0 with Relu, else -128).  Relu is applied as
+// max(v, 0) before rounding (the same code), the int8 saturation and the
+// byte packing by cvt.pack.sat (two values per instruction: the first
+// source lands in bits 15:8, the second in bits 7:0, the third operand's
+// low half in bits 31:16).
 __device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, int lo) {
-  return (uint32_t(uint8_t(sat_rne_i8(a, lo)))) | (uint32_t(uint8_t(sat_rne_i8(b, lo))) << 8) |
-         (uint32_t(uint8_t(sat_rne_i8(c, lo))) << 16) | (uint32_t(uint8_t(sat_rne_i8(d, lo))) << 24);
+  if (lo == 0) {
+    a = fmaxf(a, 0.0f);
+    b = fmaxf(b, 0.0f);
+    c = fmaxf(c, 0.0f);
+    d = fmaxf(d, 0.0f);
+  }
+  const int qa = __float2int_rn(a), qb = __float2int_rn(b), qc = __float2int_rn(c), qd = __float2int_rn(d);
+  uint32_t hi, w;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(qd), "r"(qc), "r"(0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(qb), "r"(qa), "r"(hi));
+  return w;
 }
 
 // Epilogue warps: 4 with gathered A (warps 4-7 gather), else 8, or 16 for
