@@ -155,19 +155,34 @@ struct WorkIter {
   }
 };
 
-// One pipeline stage: [A (hi)][A lo (3xTF32)][B hi][B lo (3xTF32)].
-constexpr int stage_bytes(int brows, bool split3) { return (split3 ? 2 : 1) * (kABytes + brows * 128); }
+// A-low-in-TMEM variant (single-CTA 3xTF32, BN = 128, TMA-fed A): the A
+// warps write A's low part into a TMEM ring (one 32-column slot per stage)
+// instead of shared memory and the A_lo * B_hi MMAs read A from TMEM.  The
+// stage shrinks to [A hi][B hi][B lo] (48 KB), so four stages fit instead of
+// three: the tensor pipe idles about half the time on the hand-off chain
+// with three.  Two accumulator buffers (promotion every few K steps leaves
+// the epilogue a group's time per add) free the TMEM for the ring.
+constexpr bool alo_tmem(int bn, bool split3, int amode, bool pair) {
+  return split3 && !pair && bn == 128 && (amode == 2 || amode == 3);
+}
+
+// One pipeline stage: [A (hi)][A lo (3xTF32)][B hi][B lo (3xTF32)], or
+// [A hi][B hi][B lo] when A's low part lives in TMEM.
+constexpr int stage_bytes(int brows, bool split3, bool alo = false) {
+  return alo ? kABytes + 2 * brows * 128 : (split3 ? 2 : 1) * (kABytes + brows * 128);
+}
 
 // TMEM accumulator buffers the MMA rotates through.  3xTF32 hands a partial
 // buffer to the epilogue every `group` K steps to be added into the fp32
 // sums; with three buffers the epilogue has two groups' time to do it before
 // the MMA needs the buffer again.  TF32 hands off once per tile (two buffers:
 // tile t's epilogue overlaps tile t+1's MMAs).
-template <int BN, bool SPLIT3>
+template <int BN, bool SPLIT3, bool ALO = false, int STAGES = 0>
 struct AccLayout {
-  static constexpr int nbuf = SPLIT3 && 4 * BN <= 512 ? 3 : 2;
+  static constexpr int nbuf = ALO ? 2 : SPLIT3 && 4 * BN <= 512 ? 3 : 2;
   static constexpr int sum_col = nbuf * BN;                     // promoted sums (3xTF32)
-  static constexpr int cols = sum_col + (SPLIT3 ? BN : 0);
+  static constexpr int alo_col = sum_col + (SPLIT3 ? BN : 0);  // A low-part ring (ALO)
+  static constexpr int cols = alo_col + (ALO ? 32 * STAGES : 0);
 };
 
 // Row / chunk mapping shared by the A loads and the conversion pass: thread t
@@ -215,11 +230,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int BROWS = PAIR ? BN / 2 : BN;  // weight rows held by this CTA
   constexpr int TILE_ROWS = PAIR ? 2 * kBM : kBM;
   constexpr int B_BYTES = BROWS * 128;
-  constexpr int STAGE = stage_bytes(BROWS, SPLIT3);
+  constexpr bool ALO = alo_tmem(BN, SPLIT3, AMODE, PAIR);
+  constexpr int STAGE = stage_bytes(BROWS, SPLIT3, ALO);
   // Stream-K tails exist only in single-CTA 3xTF32 kernels.
   constexpr bool SK = SPLIT3 && !PAIR;
   using Iter = WorkIter<SK>;
-  constexpr int B_OFF = (SPLIT3 ? 2 : 1) * kABytes;  // B hi within a stage
+  constexpr int B_OFF = (SPLIT3 && !ALO ? 2 : 1) * kABytes;  // B hi within a stage
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
   // for gathers (copied from the landing ring), for 3xTF32 (low parts) and,
   // in a CTA pair, to tell the leader that this CTA's operands have landed.
@@ -228,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool RELAY = CONVERT || PAIR;
   // TMEM: the accumulator buffers + the promoted sums for 3xTF32, rounded
   // up to a power of two >= 32 columns.
-  using Acc = AccLayout<BN, SPLIT3>;
+  using Acc = AccLayout<BN, SPLIT3, ALO, STAGES>;
   constexpr int NBUF = Acc::nbuf;
   constexpr int kCols = Acc::cols;
   constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
@@ -568,8 +584,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           if (!mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5)) break;
           uint8_t *a_hi = smem + s * STAGE;
-          if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
-          fence_proxy_async();
+          if constexpr (ALO) {
+            // Row r = this warp's TMEM lane quarter + lane: its 32 K values
+            // (eight swizzled 16-byte chunks) -> low parts -> TMEM slot s.
+            const int r = (warp & 3) * 32 + lane;
+            uint32_t lo[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const float4 v = *reinterpret_cast<const float4 *>(a_hi + swz_off(r, c));
+              lo[4 * c] = __float_as_uint(v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u));
+              lo[4 * c + 1] = __float_as_uint(v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u));
+              lo[4 * c + 2] = __float_as_uint(v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u));
+              lo[4 * c + 3] = __float_as_uint(v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+            }
+            tmem_st32(tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(Acc::alo_col + s * 32), lo);
+            tmem_wait_st();
+            tc_fence_before();
+          } else {
+            if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
+            fence_proxy_async();
+          }
           arrive_leader(&full_bar[s]);
         }
       }
@@ -770,6 +804,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, acc);
             }
+          } else if (ALO) {
+            // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
+            mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), dbh + step, idesc, acc);
+            mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
+            mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
           } else if (SPLIT3) {
             mma_tf32(dtm, dal + astep, dbh + step, idesc, acc);
             mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
@@ -912,7 +951,7 @@ struct PipeShape {
 // a BN/2-wide single-CTA tile.
 constexpr PipeShape pipe_shape(int bn, bool split3, int amode, bool pair = false) {
   return pair ? pipe_shape(bn / 2, split3, amode)
-              : amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? 3 : 4, 0}
+              : amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? (alo_tmem(bn, split3, amode, false) ? 4 : 3) : 4, 0}
                                      : PipeShape{bn == 256 ? 4 : 6, 0})
                            : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
                                      : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
@@ -921,7 +960,7 @@ constexpr PipeShape pipe_shape(int bn, bool split3, int amode, bool pair = false
 size_t smem_bytes(int bn, bool split3, int amode, bool pair) {
   const PipeShape ps = pipe_shape(bn, split3, amode, pair);
   const int brows = pair ? bn / 2 : bn;
-  return size_t(ps.stages) * size_t(stage_bytes(brows, split3)) +
+  return size_t(ps.stages) * size_t(stage_bytes(brows, split3, alo_tmem(bn, split3, amode, pair))) +
          size_t(ps.land) * kABytes + kStagingBytes + 1024;
 }
 
