@@ -295,7 +295,7 @@ def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80
 OP_CASES = (
     "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
     "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
-    "topk_ties", "topk_smallest",
+    "topk_ties", "topk_smallest", "topk_long",
 )
 
 
@@ -383,6 +383,13 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
     if case == "topk_smallest":
         x = pre([n, 3, 1000])
         vals, idx = b.node("TopK", [x, net.const("k", [100])], [[n, 3, 100], [n, 3, 100]], {"axis": 2, "largest": 0})
+        b.mark_output(vals)
+        b.mark_output(idx)
+        return b.graph
+    if case == "topk_long":
+        # A row longer than the shared-memory sort (40000 scores).
+        x = pre([n, 40000])
+        vals, idx = b.node("TopK", [x, net.const("k", [50])], [[n, 50], [n, 50]], {"axis": 1, "largest": 1})
         b.mark_output(vals)
         b.mark_output(idx)
         return b.graph

@@ -18,8 +18,9 @@
 // threads of a warp take adjacent outputs, so NHWC global pooling reads
 // coalesce along C.  Softmax uses a warp per row when the axis is innermost.
 // TopK (one block per row) radix-selects the k smallest (value, index) keys
-// and sorts those (k <= 2048), else bitonic-sorts the whole row in shared
-// memory.
+// and sorts those (k <= 2048; rows of any length, keys in shared memory up
+// to 16384 elements, recomputed from global memory beyond), else
+// bitonic-sorts the whole row in shared memory (up to 16384 elements).
 #include <string.h>
 
 #include "common.cuh"
@@ -199,7 +200,8 @@ struct TopkPlan : NodePlan {
   int64_t outer = 1, dim = 1, inner = 1, k = 0;
   int largest = 1;
   int pow2 = 1;
-  bool select = false;  // radix select + sort of k keys (k <= kSelectMax)
+  bool select = false;     // radix select + sort of k keys (k <= kSelectMax)
+  bool smem_keys = true;   // select with the row's keys in shared memory (dim <= 16384)
   int sel_pow2 = 1;
   int64_t x_axis_stride = 1;
 };
@@ -258,28 +260,34 @@ __global__ void topk_kernel(float *__restrict__ values, float *__restrict__ indi
 // the selected keys sorted (bitonic, next power of two >= k).
 constexpr int kSelectMax = 2048;
 
+// SMEM_KEYS: the row's keys are built once in shared memory (dim <= 16384);
+// otherwise every pass recomputes them from the input in global memory.
+template <bool SMEM_KEYS>
 __global__ void __launch_bounds__(1024) topk_select_kernel(float *__restrict__ values, float *__restrict__ indices,
                                                            const float *__restrict__ x, int64_t dim, int64_t inner,
                                                            int k, int largest, int sel_pow2) {
-  extern __shared__ unsigned long long keys[];  // dim keys
+  extern __shared__ unsigned long long keys[];  // dim keys (SMEM_KEYS)
   __shared__ unsigned long long sel[kSelectMax];
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_bin, s_before, s_cnt, s_count;
   const int64_t row = blockIdx.x;
   const int64_t o = row / inner, in = row % inner;
   const float *xr = x + o * dim * inner + in;
-  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
+  auto make_key = [&](int64_t i) {
     uint32_t hi = float_order_key(xr[i * inner]);
     if (largest) hi = ~hi;
-    keys[i] = (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(i);
-  }
+    return (static_cast<unsigned long long>(hi) << 32) | static_cast<uint32_t>(i);
+  };
+  auto key_of = [&](int64_t i) { return SMEM_KEYS ? keys[i] : make_key(i); };
+  if (SMEM_KEYS)
+    for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) keys[i] = make_key(i);
   unsigned long long hi_mask = 0, hi_val = 0;  // top bits fixed so far
   uint32_t remaining = uint32_t(k);             // rank of the k-th key among the candidates
   for (int shift = 56; shift >= 0; shift -= 8) {
     for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
     __syncthreads();
     for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
-      const unsigned long long key = keys[i];
+      const unsigned long long key = key_of(i);
       if ((key & hi_mask) == hi_val) atomicAdd(&hist[uint32_t(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -323,7 +331,7 @@ __global__ void __launch_bounds__(1024) topk_select_kernel(float *__restrict__ v
   if (threadIdx.x == 0) s_count = 0;
   __syncthreads();
   for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) {
-    const unsigned long long key = keys[i];
+    const unsigned long long key = key_of(i);
     if ((key & hi_mask) <= hi_val) {
       const uint32_t pos = atomicAdd(&s_count, 1u);
       if (pos < uint32_t(kSelectMax)) sel[pos] = key;
@@ -522,19 +530,23 @@ int topk_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (p->k > p->dim) p->k = p->dim;
   p->largest = a.largest;
   p->pow2 = 1;
-  while (p->pow2 < p->dim) p->pow2 <<= 1;
-  if (p->pow2 > kTopkMaxPow2) {
+  while (p->pow2 < p->dim && p->pow2 <= kTopkMaxPow2) p->pow2 <<= 1;  // stops past the sort limit
+  // Rows longer than the shared-memory sort take the radix select with keys
+  // recomputed from global memory (k <= 2048); longer rows with a larger k
+  // have no kernel.
+  if (p->pow2 > kTopkMaxPow2 && (p->k > kSelectMax || p->dim > INT32_MAX)) {
     delete p;
     return SPKV2_ERR_UNSUPPORTED;
   }
-  if (p->k <= kSelectMax && !getenv("SPKV2_TOPK_FULL_SORT")) {
+  if (p->k <= kSelectMax && (p->pow2 > kTopkMaxPow2 || !getenv("SPKV2_TOPK_FULL_SORT"))) {
     p->select = true;
+    p->smem_keys = p->pow2 <= kTopkMaxPow2;
     p->sel_pow2 = 1;
     while (p->sel_pow2 < p->k) p->sel_pow2 <<= 1;
-    const size_t smem = size_t(p->dim) * sizeof(unsigned long long);
+    const size_t smem = p->smem_keys ? size_t(p->dim) * sizeof(unsigned long long) : 0;
     if (smem > 48 * 1024)
-      cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    p->variant = "topk_radix_select";
+      cudaFuncSetAttribute(topk_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    p->variant = p->smem_keys ? "topk_radix_select" : "topk_radix_select_global";
   } else {
     const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
     if (smem > 48 * 1024)
@@ -555,8 +567,12 @@ int topk_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   float *idx = reinterpret_cast<float *>(ctx->tensors[node->outputs[1]].data);
   const float *xin = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
   if (p->select) {
-    topk_select_kernel<<<unsigned(rows), 1024, size_t(p->dim) * sizeof(unsigned long long), ctx->stream>>>(
-        vals, idx, xin, p->dim, p->inner, int(p->k), p->largest, p->sel_pow2);
+    if (p->smem_keys)
+      topk_select_kernel<true><<<unsigned(rows), 1024, size_t(p->dim) * sizeof(unsigned long long), ctx->stream>>>(
+          vals, idx, xin, p->dim, p->inner, int(p->k), p->largest, p->sel_pow2);
+    else
+      topk_select_kernel<false><<<unsigned(rows), 1024, 0, ctx->stream>>>(vals, idx, xin, p->dim, p->inner,
+                                                                         int(p->k), p->largest, p->sel_pow2);
     return cuda_status(cudaGetLastError());
   }
   const size_t smem = size_t(p->pow2) * sizeof(unsigned long long);
