@@ -295,7 +295,7 @@ def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80
 OP_CASES = (
     "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
     "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
-    "topk_ties", "topk_smallest", "topk_long",
+    "topk_ties", "topk_smallest", "topk_long", "softmax_channels",
 )
 
 
@@ -385,6 +385,13 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
         vals, idx = b.node("TopK", [x, net.const("k", [100])], [[n, 3, 100], [n, 3, 100]], {"axis": 2, "largest": 0})
         b.mark_output(vals)
         b.mark_output(idx)
+        return b.graph
+    if case == "softmax_channels":
+        # Softmax over the channels of a rank-4 activation (stored channels-
+        # last on the device) into a row-major graph output.
+        x = pre([n, 21, 12, 10])
+        y = b.op("Softmax", [x], [n, 21, 12, 10], {"axis": 1})
+        b.mark_output(y)
         return b.graph
     if case == "topk_long":
         # A row longer than the shared-memory sort (40000 scores).

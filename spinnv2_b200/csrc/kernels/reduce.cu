@@ -16,7 +16,8 @@
 // the reduced index space in the reference's order (bit-exact with it;
 // adjacent reduced axes forming one strided run are walked as one); the
 // threads of a warp take adjacent outputs, so NHWC global pooling reads
-// coalesce along C.  Softmax uses a warp per row when the axis is innermost.
+// coalesce along C.  Softmax uses a warp per row when the axis is innermost in
+// row-major tensors, else one thread per row over any layouts.
 // TopK (one block per row) radix-selects the k smallest (value, index) keys
 // and sorts those (k <= 2048; rows of any length, keys in shared memory up
 // to 16384 elements, recomputed from global memory beyond), else
@@ -148,9 +149,43 @@ __global__ void reduce_mean_i8_kernel(float *__restrict__ y, const int8_t *__res
 
 // ---------------- Softmax ----------------
 
+// Softmax over any layouts (a channels-last rank-4 input, an output in
+// another layout): one thread per row, the row's other coordinates walked
+// in the output's physical order so neighbouring threads write
+// neighbouring outputs.
+struct SoftmaxView {
+  int rank;                   // other (non-axis) dims
+  int64_t dim[kMaxRank];      // in the output's physical order
+  int64_t xs[kMaxRank], ys[kMaxRank];
+  int64_t n, sxa, sya;        // axis extent and strides
+};
+
 struct SoftmaxPlan : NodePlan {
   int64_t outer = 1, dim = 1, inner = 1;
+  bool view = false;
+  SoftmaxView v;
 };
+
+__global__ void softmax_view_kernel(float *__restrict__ y, const float *__restrict__ x, SoftmaxView d, int64_t rows) {
+  for (int64_t r = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; r < rows; r += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = r, bx = 0, by = 0;
+    for (int k = d.rank - 1; k >= 0; --k) {
+      const int64_t c = rem % d.dim[k];
+      rem /= d.dim[k];
+      bx += c * d.xs[k];
+      by += c * d.ys[k];
+    }
+    float m = -INFINITY;
+    for (int64_t j = 0; j < d.n; ++j) m = fmaxf(m, x[bx + j * d.sxa]);
+    float s = 0.0f;
+    for (int64_t j = 0; j < d.n; ++j) {
+      const float e = expf(x[bx + j * d.sxa] - m);
+      y[by + j * d.sya] = e;
+      s += e;
+    }
+    for (int64_t j = 0; j < d.n; ++j) y[by + j * d.sya] = y[by + j * d.sya] / s;
+  }
+}
 
 __global__ void softmax_rows_kernel(float *__restrict__ y, const float *__restrict__ x, int64_t rows, int64_t dim) {
   const int lane = threadIdx.x & 31;
@@ -479,12 +514,35 @@ int softmax_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2K
   if (rc) return rc;
   const TensorState &tx = ctx->tensors[node->inputs[0]];
   const TensorState &ty = ctx->tensors[node->outputs[0]];
-  if (tx.layout != kRowMajor || ty.layout != kRowMajor) return SPKV2_ERR_UNSUPPORTED;
-  if (tx.record->dtype != SPKV2_DTYPE_FP32) return SPKV2_ERR_UNSUPPORTED;
+  if (tx.record->dtype != SPKV2_DTYPE_FP32 || ty.record->dtype != SPKV2_DTYPE_FP32) return SPKV2_ERR_UNSUPPORTED;
   const int rank = tx.record->rank;
   const int axis = a.axis < 0 ? a.axis + rank : a.axis;
-  if (axis < 0 || axis >= rank) return -11;
+  if (axis < 0 || axis >= rank || ty.record->rank != rank) return -11;
   SoftmaxPlan *p = new SoftmaxPlan();
+  if (tx.layout != kRowMajor || ty.layout != kRowMajor) {
+    const View vx = make_view(tx), vy = make_view(ty);
+    int order[kMaxRank], n = 0;
+    for (int i = 0; i < rank; ++i)
+      if (i != axis) order[n++] = i;
+    std::stable_sort(order, order + n, [&](int u, int w) { return vy.stride[u] > vy.stride[w]; });
+    SoftmaxView &v = p->v;
+    memset(&v, 0, sizeof(v));
+    v.rank = n;
+    for (int j = 0; j < n; ++j) {
+      v.dim[j] = vy.dim[order[j]];
+      v.xs[j] = vx.stride[order[j]];
+      v.ys[j] = vy.stride[order[j]];
+    }
+    v.n = vy.dim[axis];
+    v.sxa = vx.stride[axis];
+    v.sya = vy.stride[axis];
+    p->view = true;
+    p->outer = vy.count() / std::max<int64_t>(v.n, 1);
+    p->dim = v.n;
+    p->variant = "softmax_view";
+    set_node_plan(ctx, node, p);
+    return 0;
+  }
   for (int i = 0; i < axis; ++i) p->outer *= tx.record->shape[i];
   p->dim = tx.record->shape[axis];
   for (int i = axis + 1; i < rank; ++i) p->inner *= tx.record->shape[i];
@@ -499,6 +557,10 @@ int softmax_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   float *y = reinterpret_cast<float *>(ctx->tensors[node->outputs[0]].data);
   const float *x = reinterpret_cast<const float *>(ctx->tensors[node->inputs[0]].data);
   if (p->outer * p->inner == 0 || p->dim == 0) return 0;
+  if (p->view) {
+    softmax_view_kernel<<<grid_for(p->outer, 128), 128, 0, ctx->stream>>>(y, x, p->v, p->outer);
+    return cuda_status(cudaGetLastError());
+  }
   if (p->inner == 1)
     softmax_rows_kernel<<<grid_for(p->outer * 32, 256), 256, 0, ctx->stream>>>(y, x, p->outer, p->dim);
   else

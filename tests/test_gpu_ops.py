@@ -21,7 +21,7 @@ from test_ops import GATHER_INDICES, _case_ids, op_inputs
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 1e-3, 1e-4
-SUMMING = {"matmul", "matmul_bcast", "avgpool", "globalavgpool"}
+SUMMING = {"matmul", "matmul_bcast", "avgpool", "globalavgpool", "softmax_channels"}
 SPKV2_ERR_DEVICE_STATUS = -47
 INDEX_RANGE_CODE = 10
 
