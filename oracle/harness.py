@@ -44,6 +44,7 @@ def oracle_lib() -> ctypes.CDLL:
         lib.oracle_conv2d_f32.argtypes = [vp, vp, vp, vp, vp, ctypes.POINTER(_ConvShape)]
         lib.oracle_conv2d_f32_to_i8.argtypes = [vp, vp, vp, vp, ctypes.POINTER(_ConvShape), ctypes.c_float]
         lib.oracle_conv2d_i8.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, vp, vp, ctypes.POINTER(_ConvShape)]
+        lib.oracle_dequant_w8.argtypes = [vp, vp, vp, vp, vp, ctypes.POINTER(_ConvShape)]
         lib.oracle_sat_rne.argtypes = [ctypes.c_float, ctypes.c_int]
         lib.oracle_sat_rne.restype = ctypes.c_int
         _olib = lib
@@ -88,7 +89,24 @@ def run_conv(pkg: SpkPackage, node, env: dict, acc_out: np.ndarray | None = None
     b = np.ascontiguousarray(pkg.weight(node.inputs[2])) if len(node.inputs) > 2 else None
     res = np.ascontiguousarray(env[node.inputs[3]]) if len(node.inputs) > 3 else None
     y = np.empty(yt.shape, dtype=yt.np_dtype)
-    if x.dtype == np.float32 and y.dtype == np.float32:
+    if x.dtype == np.float32 and w.dtype == np.int8 and y.dtype == np.float32:
+        # Weights-only INT8 (the reference compiler's format, reference
+        # kernels/optimized/conv/conv_int8.c:22-56,86-119): x quantised per
+        # tensor, q = sat8(rne(x * fp32(1 / s_x))) (the reference's vector
+        # lanes; its scalar tail uses round-half-away and only runs for
+        # images whose C*H*W is not a multiple of 16), int8 conv to int32,
+        # then the fused dequantise.
+        sx = np.float32(pkg.quant[node.inputs[0]].scales[0])
+        inv = np.float32(np.float32(1.0) / sx)
+        xq = np.ascontiguousarray(np.clip(np.rint((x * inv).astype(np.float32)), -128, 127).astype(np.int8))
+        acc = np.empty(yt.shape, dtype=np.int32)
+        ones = np.ones(s.M, dtype=np.float32)
+        scratch = np.empty(yt.shape, dtype=np.int8)
+        lib.oracle_conv2d_i8(_ptr(xq), _ptr(w), None, _ptr(ones), None, 0.0, _ptr(scratch), _ptr(acc),
+                             ctypes.byref(s))
+        cs = np.ascontiguousarray((pkg.quant[node.inputs[1]].scales.astype(np.float32) * sx).astype(np.float32))
+        lib.oracle_dequant_w8(_ptr(acc), _ptr(cs), _ptr(b), _ptr(res), _ptr(y), ctypes.byref(s))
+    elif x.dtype == np.float32 and y.dtype == np.float32:
         lib.oracle_conv2d_f32(_ptr(x), _ptr(w), _ptr(b), _ptr(res), _ptr(y), ctypes.byref(s))
     elif x.dtype == np.float32 and y.dtype == np.int8:
         inv = np.float32(1.0) / np.float32(pkg.quant[node.outputs[0]].scales[0])

@@ -136,3 +136,24 @@ void oracle_conv2d_i8(const int8_t *x, const int8_t *w, const int32_t *bq, const
 
 /* Round-half-even saturation of one value, exported for known-answer tests. */
 int oracle_sat_rne(float v, int lo) { return (int)sat_rne(v, lo); }
+
+/* Weights-only INT8 conv (the reference compiler's own INT8 format; its
+ * kernel is reference runtime/kernels/optimized/conv/conv_int8.c:86-119):
+ * from the int32 accumulators of the int8 conv over the on-the-fly
+ * quantised input, y = act(fmaf((float)acc, cs[m], b[m]) + res), cs[m] =
+ * fp32(s_w[m] * s_x); the multiply-add fused as in the reference's vector
+ * path, then the residual add and the activation (Relu, or SiLU with
+ * expf).  NCHW order. */
+void oracle_dequant_w8(const int32_t *acc, const float *cs, const float *b, const float *res, float *y,
+                       const ConvShape *s) {
+    const long spatial = (long)s->OH * s->OW;
+    const long total = (long)s->N * s->M * spatial;
+    for (long i = 0; i < total; i++) {
+        const int m = (int)((i / spatial) % s->M);
+        float v = fmaf((float)acc[i], cs[m], b ? b[m] : 0.0f);
+        if (res) v = v + res[i];
+        if (s->act == 1) v = v > 0.0f ? v : 0.0f;
+        else if (s->act == 2) v = v / (1.0f + expf(-v));
+        y[i] = v;
+    }
+}

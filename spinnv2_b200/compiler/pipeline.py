@@ -47,10 +47,14 @@ def _compiler_hash() -> str:
     return h.hexdigest()[:16]
 
 
-def compile_config(name: str, batch: int, targets=("cuda_b200",), *, seed: int = 0, int8: bool = False,
+def compile_config(name: str, batch: int, targets=("cuda_b200",), *, seed: int = 0, int8: bool | str = False,
                    calib_images: int = 32, use_cache: bool = True) -> dict[str, bytes]:
-    """Build config `name` at `batch` and package it for each target profile."""
-    key = f"{name}_b{batch}_s{seed}{'_int8' if int8 else ''}_{_compiler_hash()}"
+    """Build config `name` at `batch` and package it for each target profile.
+    int8=True: int8 activations between convs (the INT8 contract of this
+    target); int8="weights": the reference compiler's own format, int8 conv
+    weights with fp32 activations quantised by the runtime."""
+    tag = "_int8w" if int8 == "weights" else "_int8" if int8 else ""
+    key = f"{name}_b{batch}_s{seed}{tag}_{_compiler_hash()}"
     out: dict[str, bytes] = {}
     missing = []
     for t in targets:
@@ -63,7 +67,10 @@ def compile_config(name: str, batch: int, targets=("cuda_b200",), *, seed: int =
         return out
     graph = fuse(builders.build_config(name, batch, seed))
     quant = None
-    if int8:
+    if int8 == "weights":
+        from .quantize import quantize_weights_only
+        graph, quant = quantize_weights_only(graph, calib_images=calib_images, seed=seed + 1000)
+    elif int8:
         from .quantize import quantize_int8_model
         graph, quant = quantize_int8_model(graph, calib_images=calib_images, seed=seed + 1000)
     for t in missing:

@@ -156,3 +156,33 @@ def quantize_int8_model(graph: Graph, calib_images: int = 32, seed: int = 1000) 
 
 __all__ = ["QuantParam", "quantize_int8_model", "quantize_weights_per_channel", "quantize_bias",
            "round_range_up"]
+
+
+def quantize_weights_only(graph: Graph, calib_images: int = 32, seed: int = 1000) -> tuple[Graph, list[QuantParam]]:
+    """The reference compiler's own INT8 format (reference quantize_weights.py:
+    24-120): every group-1 conv weight becomes int8 per output channel (the
+    same quantiser as above) and every conv input gets a per-tensor scale;
+    activations, biases and residuals stay fp32 and the runtime quantises
+    each conv input on the fly.  The scales come from the max-abs calibration
+    above (the reference takes them from onnxruntime's calibrator)."""
+    ranges = max_abs_ranges(graph, images=calib_images, seed=seed)
+    params: list[QuantParam] = []
+    done_w: set[int] = set()
+    done_x: set[int] = set()
+    for n in graph.nodes:
+        if n.op_type != "Conv" or len(n.inputs) < 2 or int(n.attrs.get("group", 1)) != 1:
+            continue
+        wt = graph.tensors[n.inputs[1]]
+        if n.inputs[1] not in done_w and wt.dtype == DTYPE_FP32 and wt.data is not None:
+            w_q, s_w = quantize_weights_per_channel(wt.array())
+            wt.data = w_q.tobytes()
+            wt.dtype = DTYPE_INT8
+            params.append(QuantParam(wt.id, "per_channel", 0, int(s_w.size), [float(v) for v in s_w],
+                                     [0] * int(s_w.size)))
+            done_w.add(wt.id)
+        x = n.inputs[0]
+        if x not in done_x and x in ranges:
+            s = float(np.float32(round_range_up(ranges[x]) / np.float32(127.0)))
+            params.append(QuantParam(x, "per_tensor", 0, 1, [s], [0]))
+            done_x.add(x)
+    return graph, params

@@ -228,6 +228,108 @@ int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res,
   return cuda_status(cudaGetLastError());
 }
 
+// ---------------- weights-only INT8 (the reference compiler's format) ----------------
+//
+// Reference runtime/kernels/optimized/conv/conv_int8.c:22-56,86-119: the
+// fp32 input is quantised per tensor, q = sat8(rne(x * fp32(1 / s_x))) (its
+// vector lanes; the scalar tail rounds half away from zero and is only
+// reached when an image's C*H*W is not a multiple of 16), the int8 conv
+// accumulates in int32, and y = act(fma(acc, s_w[c] * s_x, b[c]) + res).
+
+namespace {
+
+// x (any layout, strides g.xs) -> dense NHWC int8.
+__global__ void quantize_w8_kernel(int8_t *__restrict__ xq, const float *__restrict__ x, ConvGeo g, float inv,
+                                   int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = int(i % g.C);
+    const int64_t pix = i / g.C;
+    const int w = int(pix % g.W), h = int((pix / g.W) % g.H), n = int(pix / (int64_t(g.W) * g.H));
+    const float v = __fmul_rn(x[n * g.xs[0] + c * g.xs[1] + h * g.xs[2] + w * g.xs[3]], inv);
+    int q = __float2int_rn(v);
+    q = q < -128 ? -128 : q > 127 ? 127 : q;
+    xq[i] = int8_t(q);
+  }
+}
+
+// Dense NHWC int32 accumulators -> y (strides g.ys), fused dequantisation.
+__global__ void dequant_w8_kernel(float *__restrict__ y, const int32_t *__restrict__ acc, const float *__restrict__ cs,
+                                  const float *__restrict__ bias, const float *__restrict__ res, ConvGeo g,
+                                  int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int m = int(i % g.M);
+    const int64_t pix = i / g.M;
+    const int ow = int(pix % g.OW), oh = int((pix / g.OW) % g.OH), n = int(pix / (int64_t(g.OW) * g.OH));
+    float v = fmaf(float(acc[i]), cs[m], bias ? bias[m] : 0.0f);
+    if (res) v = __fadd_rn(v, res[n * g.rs[0] + m * g.rs[1] + oh * g.rs[2] + ow * g.rs[3]]);
+    v = apply_act(v, g.act);
+    y[n * g.ys[0] + m * g.ys[1] + oh * g.ys[2] + ow * g.ys[3]] = v;
+  }
+}
+
+}  // namespace
+
+int prepare_w8(Spkv2Context *ctx, const Spkv2NodeRecord *node, ConvPlan &p, const void *w_dev) {
+  const ConvGeo &g = p.g;
+  if (g.groups != 1) return SPKV2_ERR_UNSUPPORTED;
+  bool ok = true;
+  const float sx = per_tensor_scale(ctx, node->inputs[0], &ok);
+  const Spkv2QuantParamRecord *wq = find_quant_param(ctx, node->inputs[1]);
+  const float *sw = quant_scales(ctx, wq);
+  if (!ok || !sw || wq->num_channels != uint32_t(g.M)) return SPKV2_ERR_UNSUPPORTED;
+  p.w8_inv_sx = 1.0f / sx;
+  std::vector<float> cs(size_t(ceil_div(g.M, 32) * 32), 0.0f);
+  for (int c = 0; c < g.M; ++c) cs[size_t(c)] = sw[c] * sx;
+  p.w8_cs = static_cast<float *>(device_alloc(sizeof(float) * cs.size()));
+  p.w8_xq = static_cast<int8_t *>(device_alloc(size_t(g.N) * g.C * g.H * g.W + 16));
+  p.w8_acc = static_cast<int32_t *>(device_alloc(sizeof(int32_t) * size_t(g.P) * g.M + 16));
+  if (!p.w8_cs || !p.w8_xq || !p.w8_acc) return SPKV2_ERR_DEVICE_ALLOC;
+  int rc = cuda_status(cudaMemcpyAsync(p.w8_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice,
+                                       ctx->stream));
+  if (rc == 0) rc = cuda_status(cudaStreamSynchronize(ctx->stream));  // the host vector must outlive the copy
+  if (rc) return rc;
+  // The int8 conv: dense NHWC int8 in, dense NHWC int32 out, no bias,
+  // residual or activation (those are applied by the dequantisation).
+  ConvPlan *q = new ConvPlan();
+  p.w8_inner = q;
+  q->mode = kConvI8ToI32;
+  q->g = g;
+  ConvGeo &gi = q->g;
+  gi.xs[0] = int64_t(g.H) * g.W * g.C, gi.xs[1] = 1, gi.xs[2] = int64_t(g.W) * g.C, gi.xs[3] = g.C;
+  gi.ys[0] = int64_t(g.OH) * g.OW * g.M, gi.ys[1] = 1, gi.ys[2] = int64_t(g.OW) * g.M, gi.ys[3] = g.M;
+  gi.has_bias = 0;
+  gi.has_res = 0;
+  gi.act = 0;
+  rc = SPKV2_ERR_UNSUPPORTED;
+  if (ctx->math_mode != SPKV2_CUDA_MATH_FP32) rc = conv_tc_i8_prepare(*q, w_dev, p.w8_xq, p.w8_acc, nullptr, ctx->stream);
+  if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) return rc;
+  if (!q->w_tc) {
+    q->w_simt = device_alloc(size_t(g.M) * g.K);
+    if (!q->w_simt) return SPKV2_ERR_DEVICE_ALLOC;
+    pack_simt_kernel<int8_t><<<grid_for(int64_t(g.M) * g.K, 256), 256, 0, ctx->stream>>>(
+        static_cast<int8_t *>(q->w_simt), static_cast<const int8_t *>(w_dev), g);
+    if ((rc = cuda_status(cudaGetLastError()))) return rc;
+    q->variant = "simt_int8_i32out";
+  }
+  p.launches = 2 + q->launches;
+  p.variant = "w8_" + q->variant;
+  return 0;
+}
+
+int run_w8(Spkv2Context *ctx, const ConvPlan &p, const float *x, float *y, const float *res) {
+  const ConvGeo &g = p.g;
+  const int64_t nx = int64_t(g.N) * g.C * g.H * g.W, ny = g.P * g.M;
+  quantize_w8_kernel<<<grid_for(nx, 256), 256, 0, ctx->stream>>>(p.w8_xq, x, g, p.w8_inv_sx, nx);
+  int rc = cuda_status(cudaGetLastError());
+  if (rc) return rc;
+  const ConvPlan &q = *p.w8_inner;
+  rc = q.w_tc ? conv_tc_i8_launch(q, p.w8_xq, p.w8_acc, nullptr, ctx->d_status, ctx->stream)
+              : conv_simt_launch(q, p.w8_xq, p.w8_acc, nullptr, ctx->stream);
+  if (rc) return rc;
+  dequant_w8_kernel<<<grid_for(ny, 256), 256, 0, ctx->stream>>>(y, p.w8_acc, p.w8_cs, p.bias_f, res, g, ny);
+  return cuda_status(cudaGetLastError());
+}
+
 int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *spec) {
   if (node->input_count < 2 || node->output_count < 1) return -3;
   Spkv2AttrRecord a;
@@ -282,6 +384,8 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     p->mode = kConvI8;
   else if (dx == SPKV2_DTYPE_INT8 && dw == SPKV2_DTYPE_INT8 && dy == SPKV2_DTYPE_INT32)
     p->mode = kConvI8ToI32;
+  else if (dx == SPKV2_DTYPE_FP32 && dw == SPKV2_DTYPE_INT8 && dy == SPKV2_DTYPE_FP32)
+    p->mode = kConvW8;
   else {
     delete p;
     return SPKV2_ERR_UNSUPPORTED;
@@ -349,6 +453,15 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (!ok) {
     delete p;
     return SPKV2_ERR_UNSUPPORTED;
+  }
+
+  if (p->mode == kConvW8) {
+    if ((rc = prepare_w8(ctx, node, *p, tw.data))) {
+      delete p;
+      return rc;
+    }
+    set_node_plan(ctx, node, p);
+    return 0;
   }
 
   // Math mode: the context override, else the KernelSpec kind.
@@ -422,6 +535,8 @@ int conv_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
   const void *x = ctx->tensors[node->inputs[0]].data;
   void *y = ctx->tensors[node->outputs[0]].data;
   const void *res = p->g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
+  if (p->mode == kConvW8) return run_w8(ctx, *p, static_cast<const float *>(x), static_cast<float *>(y),
+                                        static_cast<const float *>(res));
   if (p->w_tc)
     return p->tc_i8 ? conv_tc_i8_launch(*p, x, y, res, ctx->d_status, ctx->stream)
                     : conv_tc_launch(*p, x, y, res, ctx->d_status, ctx->stream, ctx->d_sk_ws);

@@ -11,6 +11,8 @@ enum ConvMode : int {
   kConvF32ToI8 = 1, // fp32 x, fp32 w -> int8 y   (quantising epilogue)
   kConvI8 = 2,      // int8 x, int8 w -> int8 y   (int32 acc, requantised)
   kConvI8ToI32 = 3, // int8 x, int8 w -> int32 y  (acc + int32 bias, no requantisation)
+  kConvW8 = 4,      // fp32 x, int8 w -> fp32 y   (weights-only int8: x quantised per tensor on
+                    //  the fly, int8 conv to int32, y = act(fma(acc, s_w[c] s_x, b) + res))
 };
 
 // Geometry and epilogue parameters, passed by value to the kernels.
@@ -67,7 +69,18 @@ struct ConvPlan : NodePlan {
   int tc_kpad = 0;         // padded K of the tcgen05 panels
   void *tc_state = nullptr;  // tensor maps + launch configuration (conv_tc.cu / conv_tc_i8.cu)
   bool tc_i8 = false;        // tc_state belongs to the kind::i8 kernel
+  // kConvW8: the int8 conv over the quantised input, its buffers and the
+  // per-channel dequantisation scale s_w[c] * s_x.
+  ConvPlan *w8_inner = nullptr;
+  int8_t *w8_xq = nullptr;
+  int32_t *w8_acc = nullptr;
+  float *w8_cs = nullptr;
+  float w8_inv_sx = 1.0f;
   ~ConvPlan() override {
+    delete w8_inner;
+    device_free(w8_xq);
+    device_free(w8_acc);
+    device_free(w8_cs);
     if (tc_state) tc_i8 ? conv_tc_i8_release(tc_state) : conv_tc_release(tc_state);
     device_free(w_simt);
     device_free(w_tc);
