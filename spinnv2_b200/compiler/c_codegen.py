@@ -90,6 +90,9 @@ def header_text(symbol: str, spk: bytes) -> str:
         f"#define {sym}_OUTPUT_COUNT {len(pkg.outputs)}",
         f"#define {sym}_INPUT_SIZE {sym}_INPUT_SIZE_0",
         f"#define {sym}_OUTPUT_SIZE {sym}_OUTPUT_SIZE_0",
+        "/* All sizes, as array initialisers (an addition to the reference's macros). */",
+        f"#define {sym}_INPUT_SIZES {{" + ", ".join(f"{sym}_INPUT_SIZE_{i}" for i in range(len(pkg.inputs))) + "}",
+        f"#define {sym}_OUTPUT_SIZES {{" + ", ".join(f"{sym}_OUTPUT_SIZE_{i}" for i in range(len(pkg.outputs))) + "}",
         f"/* Host arena bytes the wrapper reserves (0: the runtime owns device arenas). */",
         f"#define {sym}_HOST_ARENAS {0 if device else 1}",
         f"#define {sym}_ACTIVATION_ARENA_SIZE ((size_t){act}u)",

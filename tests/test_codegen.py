@@ -41,12 +41,24 @@ def _build(spk: bytes, out: Path, lib_dir: Path, lib: str) -> Path:
     return exe
 
 
-def _run(exe: Path, x: np.ndarray, out_shape, tmp: Path, runs: int = 3) -> np.ndarray:
+def _run_all(exe: Path, xs: list, outs: list, tmp: Path, runs: int = 3) -> list:
+    """Runs the driver on the inputs `xs` (written back to back); `outs` is
+    the (shape, dtype) of each output, read back to back."""
     fin, fout = tmp / "in.bin", tmp / "out.bin"
-    x.astype(np.float32).tofile(fin)
+    fin.write_bytes(b"".join(np.ascontiguousarray(x).tobytes() for x in xs))
     res = subprocess.run([str(exe), str(fin), str(fout), str(runs)], capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stderr
-    return np.fromfile(fout, dtype=np.float32).reshape(out_shape)
+    raw, got, off = fout.read_bytes(), [], 0
+    for shape, dt in outs:
+        n = int(np.prod(shape)) * np.dtype(dt).itemsize
+        got.append(np.frombuffer(raw[off:off + n], dtype=dt).reshape(shape))
+        off += n
+    assert off == len(raw)
+    return got
+
+
+def _run(exe: Path, x: np.ndarray, out_shape, tmp: Path, runs: int = 3) -> np.ndarray:
+    return _run_all(exe, [x.astype(np.float32)], [(out_shape, np.float32)], tmp, runs)[0]
 
 
 def test_header_macros_and_arenas(built):
@@ -76,6 +88,26 @@ def test_generated_c_on_reference_runtime_matches_reference(built, tmp_path):
     np.testing.assert_array_equal(_run(exe, x, ref.shape, tmp_path), ref)
 
 
+@pytest.mark.parametrize("case", ["gather_input", "topk_ties"])
+def test_generated_c_run_multi_on_reference_runtime(built, tmp_path, case):
+    """Packages with two inputs (Gather with runtime indices) or two outputs
+    (TopK values and indices) go through <sym>_run_multi, with the size
+    arrays taken from the header's <SYM>_INPUT_SIZES / <SYM>_OUTPUT_SIZES."""
+    from oracle import REF_LIB
+    from spinnv2_b200.spk import read_spk
+    from test_ops import op_inputs
+
+    spk = compile_pair(f"op_{case}", 2)
+    pkg = read_spk(spk["cpu_generic_x86"])
+    assert len(pkg.inputs) + len(pkg.outputs) == 3
+    exe = _build(spk["cpu_generic_x86"], tmp_path, Path(REF_LIB).parent, "spkv2_ref")
+    ins = op_inputs(pkg)
+    ref = reference_outputs(spk["cpu_generic_x86"], ins)
+    got = _run_all(exe, ins, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs], tmp_path)
+    for g, r in zip(got, ref):
+        np.testing.assert_array_equal(g, r)
+
+
 def test_generated_c_links_against_cuda_runtime(built, tmp_path):
     from spinnv2_b200.runtime import LIB_PATH
 
@@ -95,3 +127,22 @@ def test_generated_c_on_cuda_runtime_matches_reference(gpu, tmp_path, name, shap
     x = seeded_input(shape, kind)
     ref = reference_outputs(spk["cpu_generic_x86"], [x])[0]
     np.testing.assert_allclose(_run(exe, x, ref.shape, tmp_path), ref, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.gpu
+def test_generated_c_run_multi_on_cuda_runtime(gpu, tmp_path):
+    """TopK (two outputs, values and int indices) through <sym>_run_multi on
+    the B200: bit-exact with the reference (the scores come from one Mul and
+    one Mod, single IEEE operations, so the selection sees the same keys)."""
+    from spinnv2_b200.runtime import LIB_PATH
+    from spinnv2_b200.spk import read_spk
+    from test_ops import op_inputs
+
+    spk = compile_pair("op_topk_ties", 2)
+    pkg = read_spk(spk["cpu_generic_x86"])
+    exe = _build(spk["cuda_b200"], tmp_path, LIB_PATH.parent, "spkv2_runtime")
+    ins = op_inputs(pkg)
+    ref = reference_outputs(spk["cpu_generic_x86"], ins)
+    got = _run_all(exe, ins, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs], tmp_path)
+    for g, r in zip(got, ref):
+        np.testing.assert_array_equal(g, r)
