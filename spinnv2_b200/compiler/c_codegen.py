@@ -3,7 +3,9 @@
 Same public surface as the reference compiler's generated C (reference
 compiler/codegen/c_codegen.py:180-325): a header with the package's size
 macros (`<SYM>_INPUT_SIZE_i`, `<SYM>_OUTPUT_SIZE_i`, counts, arena sizes,
-`<SYM>_SPK_CHECKSUM`) and a source that embeds the package bytes and exports
+`<SYM>_SPK_CHECKSUM`; added here: `<SYM>_INPUT_SIZES` / `<SYM>_OUTPUT_SIZES`,
+array initialisers for <sym>_run_multi) and a source that embeds the package
+bytes and exports
 
     int  <sym>_init(void);
     int  <sym>_run(const void *input, void *output);
