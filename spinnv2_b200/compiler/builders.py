@@ -295,7 +295,8 @@ def yolo_style(batch: int = 1, seed: int = 0, size: int = 640, classes: int = 80
 OP_CASES = (
     "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
     "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
-    "topk_ties", "topk_smallest", "topk_long", "softmax_channels",
+    "topk_ties", "topk_smallest", "topk_long", "softmax_channels", "maxpool_s1_k3", "maxpool_s1_k5",
+    "maxpool_s1_k7", "resize_3x2", "resize_frac",
 )
 
 
@@ -332,6 +333,20 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
         x = pre([n, 8, 15, 15])
         return post(b.op("AveragePool", [x], [n, 8, 8, 8], {"kernel_shape": [3, 3], "strides": [2, 2],
                                                              "pads": [1, 1, 1, 1]}))
+    if case.startswith("maxpool_s1_k"):
+        # Stride-1 square windows (the SPPF form) on heights that leave a
+        # short last band of output rows, with the window's padding.
+        k = int(case[-1])
+        shape = {3: [n, 12, 11, 9], 5: [n, 8, 7, 10], 7: [n, 8, 13, 10]}[k]
+        x = pre(shape)
+        return post(b.op("MaxPool", [x], list(shape), {"kernel_shape": [k, k], "strides": [1, 1],
+                                                      "pads": [k // 2] * 4}))
+    if case in ("resize_3x2", "resize_frac"):
+        # Nearest upsampling by integer factors 3 (H) and 2 (W), and by the
+        # non-integer factors 9/6 and 11/7.
+        out = [n, 8, 15, 14] if case == "resize_3x2" else [n, 8, 9, 11]
+        x = pre([n, 8, 5, 7] if case == "resize_3x2" else [n, 8, 6, 7])
+        return post(b.op("Resize", [x], out, {"mode": "nearest"}))
     if case == "globalavgpool":
         x = pre([n, 16, 7, 9])
         return post(b.op("GlobalAveragePool", [x], [n, 16, 1, 1]))

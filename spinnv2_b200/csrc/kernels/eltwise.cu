@@ -130,33 +130,48 @@ __global__ void relayout_kernel(T *__restrict__ dst, const T *__restrict__ src, 
   }
 }
 
-// NHWC -> NCHW (and back) through a 32x32 shared-memory tile so both the
-// reads and the writes are coalesced; used for host transfers.
+// NHWC -> NCHW (and back) through a shared-memory tile of kTransP positions x
+// 32 channels, so both the reads and the writes are coalesced; used for host
+// transfers and for copies between an NHWC and a row-major view.  A block is
+// 32 x 8 threads; each thread moves kTransP / 8 elements, all its global loads
+// issued before its first shared-memory store (the loops are unrolled), so a
+// block keeps 8 KB of loads in flight.  Row stride 33 keeps both the row and
+// the column accesses of the tile free of bank conflicts.
+constexpr int kTransP = 64;
+
 template <typename T>
-__global__ void transpose_hw_c_kernel(T *__restrict__ dst, const T *__restrict__ src, int64_t N, int64_t P,
-                                      int64_t C, int to_nchw) {
-  __shared__ T tile[32][33];
+__global__ void __launch_bounds__(256) transpose_hw_c_kernel(T *__restrict__ dst, const T *__restrict__ src, int64_t N,
+                                                             int64_t P, int64_t C, int to_nchw) {
+  __shared__ T tile[kTransP][33];  // [position][channel]
+  constexpr int kRows = kTransP / 8;
+  const int tx = threadIdx.x, ty = threadIdx.y;
   const int64_t n = blockIdx.z;
-  const int64_t p0 = int64_t(blockIdx.x) * 32, c0 = int64_t(blockIdx.y) * 32;
+  const int64_t p0 = int64_t(blockIdx.x) * kTransP, c0 = int64_t(blockIdx.y) * 32;
   if (to_nchw) {  // src [N,P,C] -> dst [N,C,P]
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-      const int64_t p = p0 + r, c = c0 + threadIdx.x;
-      if (p < P && c < C) tile[r][threadIdx.x] = src[(n * P + p) * C + c];
+    const int64_t c = c0 + tx;
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int r = ty + 8 * i;  // tile position
+      if (p0 + r < P && c < C) tile[r][tx] = src[(n * P + p0 + r) * C + c];
     }
     __syncthreads();
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-      const int64_t c = c0 + r, p = p0 + threadIdx.x;
-      if (p < P && c < C) dst[(n * C + c) * P + p] = tile[threadIdx.x][r];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int j = ty + 8 * i, cl = j % 32, pl = (j / 32) * 32 + tx;
+      if (p0 + pl < P && c0 + cl < C) dst[(n * C + c0 + cl) * P + p0 + pl] = tile[pl][cl];
     }
   } else {  // src [N,C,P] -> dst [N,P,C]
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-      const int64_t c = c0 + r, p = p0 + threadIdx.x;
-      if (p < P && c < C) tile[threadIdx.x][r] = src[(n * C + c) * P + p];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int j = ty + 8 * i, cl = j % 32, pl = (j / 32) * 32 + tx;
+      if (p0 + pl < P && c0 + cl < C) tile[pl][cl] = src[(n * C + c0 + cl) * P + p0 + pl];
     }
     __syncthreads();
-    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-      const int64_t p = p0 + r, c = c0 + threadIdx.x;
-      if (p < P && c < C) dst[(n * P + p) * C + c] = tile[r][threadIdx.x];
+    const int64_t c = c0 + tx;
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int r = ty + 8 * i;
+      if (p0 + r < P && c < C) dst[(n * P + p0 + r) * C + c] = tile[r][tx];
     }
   }
 }
@@ -164,8 +179,8 @@ __global__ void transpose_hw_c_kernel(T *__restrict__ dst, const T *__restrict__
 template <typename T>
 int launch_transpose_hw_c(T *dst, const T *src, const Spkv2TensorRecord *r, int to_nchw, cudaStream_t s) {
   const int64_t N = r->shape[0], C = r->shape[1], P = int64_t(r->shape[2]) * r->shape[3];
-  if (N > 65535) return SPKV2_ERR_UNSUPPORTED;
-  dim3 grid(unsigned(ceil_div(P, 32)), unsigned(ceil_div(C, 32)), unsigned(N));
+  if (N > 65535 || ceil_div(C, 32) > 65535) return SPKV2_ERR_UNSUPPORTED;
+  dim3 grid(unsigned(ceil_div(P, kTransP)), unsigned(ceil_div(C, 32)), unsigned(N));
   transpose_hw_c_kernel<T><<<grid, dim3(32, 8), 0, s>>>(dst, src, N, P, C, to_nchw);
   return cuda_status(cudaGetLastError());
 }

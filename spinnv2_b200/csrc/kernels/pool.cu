@@ -135,28 +135,36 @@ __global__ void maxpool_nhwc4_kernel(float *__restrict__ y, const float *__restr
   }
 }
 
-// Stride-1 max pool (the SPPF 5x5 windows), NHWC fp32, C % 4 == 0: thread
-// (n, c4, ow) walks its output column down the image keeping the maxima of
-// the last KH input rows (each over the KW window columns) in registers, so
-// each output costs one new row's KW loads instead of KH x KW.  Max is
-// order-independent, so results equal the direct window scan; rows and
+// Stride-1 max pool with a square KH x KH window (the SPPF 5x5 windows), NHWC
+// fp32, C % 4 == 0: thread (n, band, ow, c4) walks its output column down a
+// band of kPoolBand output rows keeping the maxima of the last KH input rows
+// (each over the KH window columns) in registers, so an output costs one new
+// row's KH loads instead of KH x KH, and the bands give every column several
+// independent threads (a whole-height walk is a chain of dependent rows).
+// Max is order-independent, so results equal the direct window scan; rows and
 // columns outside the image are skipped as there.
+constexpr int kPoolBand = 4;
+
 template <int KH>
 __global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__restrict__ x, Geo g, int64_t columns) {
   const int C4 = g.C / 4;
+  const int bands = (g.OH + kPoolBand - 1) / kPoolBand;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < columns; i += int64_t(gridDim.x) * blockDim.x) {
     int64_t r = i;
     const int c4 = int(r % C4);
     r /= C4;
     const int ow = int(r % g.OW);
-    const int n = int(r / g.OW);
+    r /= g.OW;
+    const int band = int(r % bands);
+    const int n = int(r / bands);
     const float *xb = x + int64_t(n) * g.H * g.W * g.C + c4 * 4;
     float4 *yb = reinterpret_cast<float4 *>(y + int64_t(n) * g.OH * g.OW * g.C + int64_t(ow) * g.C + c4 * 4);
     const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     auto row_max = [&](int ih) {
       float4 best = ninf;
       if (ih < 0 || ih >= g.H) return best;
-      for (int s = 0; s < g.kw; ++s) {
+#pragma unroll
+      for (int s = 0; s < KH; ++s) {
         const int iw = ow + s - g.pw;
         if (iw < 0 || iw >= g.W) continue;
         const float4 v = *reinterpret_cast<const float4 *>(xb + (int64_t(ih) * g.W + iw) * g.C);
@@ -167,10 +175,11 @@ __global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__re
       }
       return best;
     };
+    const int oh0 = band * kPoolBand, oh1 = min(g.OH, oh0 + kPoolBand);
     float4 rm[KH];  // rm[j]: max of input row oh - ph + j
 #pragma unroll
-    for (int j = 0; j + 1 < KH; ++j) rm[j + 1] = row_max(j - g.ph);
-    for (int oh = 0; oh < g.OH; ++oh) {
+    for (int j = 0; j + 1 < KH; ++j) rm[j + 1] = row_max(oh0 + j - g.ph);
+    for (int oh = oh0; oh < oh1; ++oh) {
 #pragma unroll
       for (int j = 0; j + 1 < KH; ++j) rm[j] = rm[j + 1];
       rm[KH - 1] = row_max(oh - g.ph + KH - 1);
@@ -233,6 +242,7 @@ struct ResizeGeo {
 struct ResizePlan : NodePlan {
   ResizeGeo g;
   bool vec4 = false;
+  bool int_factor = false;  // OH % H == 0 and OW % W == 0
   int esize = 4;
 };
 
@@ -288,6 +298,28 @@ __global__ void resize_nearest_nhwc4_kernel(float4 *__restrict__ y, const float4
   }
 }
 
+// Integer scale factors (OH = fh * H, OW = fw * W), NHWC fp32, C % 4 == 0:
+// thread (n, ih, iw, c4) reads its input float4 once and writes the fh x fw
+// outputs it feeds.  For these factors floor(oh / (OH / H)) in fp32 equals
+// oh / fh, so the outputs are those of the per-output index formula.
+__global__ void resize_nearest_int_nhwc4_kernel(float4 *__restrict__ y, const float4 *__restrict__ x, ResizeGeo g,
+                                                int fh, int fw, int64_t in4) {
+  const int C4 = g.C / 4;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < in4; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int c4 = int(r % C4);
+    r /= C4;
+    const int iw = int(r % g.W);
+    r /= g.W;
+    const int ih = int(r % g.H);
+    const int n = int(r / g.H);
+    const float4 v = x[i];
+    float4 *yb = y + ((int64_t(n) * g.OH + int64_t(ih) * fh) * g.OW + int64_t(iw) * fw) * C4 + c4;
+    for (int a = 0; a < fh; ++a)
+      for (int b = 0; b < fw; ++b) yb[(int64_t(a) * g.OW + b) * C4] = v;
+  }
+}
+
 }  // namespace
 
 int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2KernelSpecRecord *spec) {
@@ -339,9 +371,10 @@ int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 16 == 0 &&
       reinterpret_cast<uintptr_t>(tx.data) % 16 == 0 && reinterpret_cast<uintptr_t>(ty.data) % 16 == 0)
     p->vec = 16;
-  p->variant = p->vec == 4 ? (g.sh == 1 && g.sw == 1 && (g.kh == 3 || g.kh == 5 || g.kh == 7) ? "maxpool_nhwc_vec4_s1rows"
-                                                                                             : "maxpool_nhwc_vec4")
-               : p->vec == 16 ? "maxpool_nhwc_i8_vec16" : "pool_generic";
+  const bool s1 = g.sh == 1 && g.sw == 1 && g.kh == g.kw && (g.kh == 3 || g.kh == 5 || g.kh == 7);
+  p->variant = p->vec == 4    ? (s1 ? "maxpool_nhwc_vec4_s1rows" : "maxpool_nhwc_vec4")
+               : p->vec == 16 ? "maxpool_nhwc_i8_vec16"
+                              : "pool_generic";
   set_node_plan(ctx, node, p);
   return 0;
 }
@@ -357,9 +390,9 @@ int pool_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   const void *x = ctx->tensors[node->inputs[0]].data;
   // Vector paths need 16-byte aligned tensors (a rebinding may move them).
   const bool aligned = (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0;
-  const bool s1 = g.sh == 1 && g.sw == 1 && (g.kh == 3 || g.kh == 5 || g.kh == 7);
+  const bool s1 = g.sh == 1 && g.sw == 1 && g.kh == g.kw && (g.kh == 3 || g.kh == 5 || g.kh == 7);
   if (p->vec == 4 && aligned && s1) {
-    const int64_t columns = int64_t(g.N) * (g.C / 4) * g.OW;
+    const int64_t columns = int64_t(g.N) * ((g.OH + kPoolBand - 1) / kPoolBand) * g.OW * (g.C / 4);
     const int grid = grid_for(columns, 128);
     if (g.kh == 3)
       maxpool_nhwc4_s1_kernel<3><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
@@ -406,7 +439,10 @@ int resize_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Ke
   g.out_nhwc = ty.layout == kNHWC;
   p->esize = int(dtype_size(ty.record->dtype));
   p->vec4 = p->esize == 4 && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 4 == 0;
-  p->variant = p->vec4 ? "resize_nearest_nhwc_vec4" : "resize_nearest_generic";
+  // Integer factors below 2^8 keep fp32's floor(oh / f) equal to oh / f.
+  p->int_factor = g.H > 0 && g.W > 0 && g.OH % g.H == 0 && g.OW % g.W == 0 && g.OH / g.H <= 256 && g.OW / g.W <= 256;
+  p->variant = p->vec4 ? (p->int_factor ? "resize_nearest_nhwc_vec4_int" : "resize_nearest_nhwc_vec4")
+                       : "resize_nearest_generic";
   set_node_plan(ctx, node, p);
   return 0;
 }
@@ -420,7 +456,11 @@ int resize_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   if (total == 0) return 0;
   void *y = ctx->tensors[node->outputs[0]].data;
   const void *x = ctx->tensors[node->inputs[0]].data;
-  if (p->vec4) {
+  if (p->vec4 && p->int_factor) {
+    const int64_t in4 = int64_t(g.N) * g.H * g.W * (g.C / 4);
+    resize_nearest_int_nhwc4_kernel<<<grid_for(in4, 256), 256, 0, ctx->stream>>>(
+        static_cast<float4 *>(y), static_cast<const float4 *>(x), g, g.OH / g.H, g.OW / g.W, in4);
+  } else if (p->vec4) {
     resize_nearest_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
         static_cast<float4 *>(y), static_cast<const float4 *>(x), g, total / 4);
   } else if (p->esize == 1) {
