@@ -33,6 +33,7 @@ struct PoolPlan : NodePlan {
   Geo g;
   int kind = kMax;
   int vec = 1;
+  int band = 0;  // > 0: stride-1 fp32 max pool, output rows per thread
   bool out_nhwc = false;
   bool is_int8 = false;
 };
@@ -137,37 +138,40 @@ __global__ void maxpool_nhwc4_kernel(float *__restrict__ y, const float *__restr
 
 // Stride-1 max pool with a square KH x KH window (the SPPF 5x5 windows), NHWC
 // fp32, C % 4 == 0: thread (n, band, ow, c4) walks its output column down a
-// band of kPoolBand output rows keeping the maxima of the last KH input rows
+// band of `band` output rows keeping the maxima of the last KH input rows
 // (each over the KH window columns) in registers, so an output costs one new
-// row's KH loads instead of KH x KH, and the bands give every column several
-// independent threads (a whole-height walk is a chain of dependent rows).
-// Max is order-independent, so results equal the direct window scan; rows and
+// row's KH loads instead of KH x KH.  The host picks the band height so that
+// the threads fill the resident slots of the GPU about once (a whole-height
+// walk is a chain of dependent rows; very short bands re-read more rows).
+// Offsets within an image are 32-bit (the plan checks H*W*C < 2^31).  Max is
+// order-independent, so results equal the direct window scan; rows and
 // columns outside the image are skipped as there.
-constexpr int kPoolBand = 4;
-
 template <int KH>
-__global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__restrict__ x, Geo g, int64_t columns) {
+__global__ void __launch_bounds__(128) maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__restrict__ x,
+                                                                Geo g, int band, int64_t columns) {
   const int C4 = g.C / 4;
-  const int bands = (g.OH + kPoolBand - 1) / kPoolBand;
+  const int bands = (g.OH + band - 1) / band;
+  const int row_elems = g.W * g.C;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < columns; i += int64_t(gridDim.x) * blockDim.x) {
     int64_t r = i;
     const int c4 = int(r % C4);
     r /= C4;
     const int ow = int(r % g.OW);
     r /= g.OW;
-    const int band = int(r % bands);
+    const int b = int(r % bands);
     const int n = int(r / bands);
-    const float *xb = x + int64_t(n) * g.H * g.W * g.C + c4 * 4;
-    float4 *yb = reinterpret_cast<float4 *>(y + int64_t(n) * g.OH * g.OW * g.C + int64_t(ow) * g.C + c4 * 4);
+    const float *xb = x + int64_t(n) * g.H * row_elems + c4 * 4;
+    float4 *yb = reinterpret_cast<float4 *>(y + int64_t(n) * g.OH * g.OW * g.C + ow * g.C + c4 * 4);
     const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     auto row_max = [&](int ih) {
       float4 best = ninf;
       if (ih < 0 || ih >= g.H) return best;
+      const float *xr = xb + ih * row_elems;
 #pragma unroll
       for (int s = 0; s < KH; ++s) {
         const int iw = ow + s - g.pw;
         if (iw < 0 || iw >= g.W) continue;
-        const float4 v = *reinterpret_cast<const float4 *>(xb + (int64_t(ih) * g.W + iw) * g.C);
+        const float4 v = *reinterpret_cast<const float4 *>(xr + iw * g.C);
         best.x = v.x > best.x ? v.x : best.x;
         best.y = v.y > best.y ? v.y : best.y;
         best.z = v.z > best.z ? v.z : best.z;
@@ -175,7 +179,7 @@ __global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__re
       }
       return best;
     };
-    const int oh0 = band * kPoolBand, oh1 = min(g.OH, oh0 + kPoolBand);
+    const int oh0 = b * band, oh1 = min(g.OH, oh0 + band);
     float4 rm[KH];  // rm[j]: max of input row oh - ph + j
 #pragma unroll
     for (int j = 0; j + 1 < KH; ++j) rm[j + 1] = row_max(oh0 + j - g.ph);
@@ -194,6 +198,21 @@ __global__ void maxpool_nhwc4_s1_kernel(float *__restrict__ y, const float *__re
       yb[int64_t(oh) * g.OW * C4] = best;
     }
   }
+}
+
+// Band height for the stride-1 kernel: as many bands per output column as
+// fill the GPU's resident 128-thread blocks once, at least one row each.
+template <int KH>
+int s1_band(const Geo &g) {
+  int dev = 0, sms = 148, per_sm = 8;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, maxpool_nhwc4_s1_kernel<KH>, 128, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 8;
+  const int64_t resident = int64_t(sms) * per_sm * 128;
+  const int64_t cols = int64_t(g.N) * g.OW * (g.C / 4);
+  const int64_t bands = std::max<int64_t>(1, std::min<int64_t>(g.OH, resident / std::max<int64_t>(cols, 1)));
+  return int((g.OH + bands - 1) / bands);
 }
 
 // Both tensors NHWC int8, C % 16 == 0: 16 channels (one 16-byte load) per
@@ -371,7 +390,9 @@ int pool_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   if (is_int8 && p->kind == kMax && tx.layout == kNHWC && ty.layout == kNHWC && g.C % 16 == 0 &&
       reinterpret_cast<uintptr_t>(tx.data) % 16 == 0 && reinterpret_cast<uintptr_t>(ty.data) % 16 == 0)
     p->vec = 16;
-  const bool s1 = g.sh == 1 && g.sw == 1 && g.kh == g.kw && (g.kh == 3 || g.kh == 5 || g.kh == 7);
+  const bool s1 = g.sh == 1 && g.sw == 1 && g.kh == g.kw && (g.kh == 3 || g.kh == 5 || g.kh == 7) &&
+                  int64_t(g.H) * g.W * g.C < (int64_t(1) << 31);
+  if (p->vec == 4 && s1) p->band = g.kh == 3 ? s1_band<3>(g) : g.kh == 5 ? s1_band<5>(g) : s1_band<7>(g);
   p->variant = p->vec == 4    ? (s1 ? "maxpool_nhwc_vec4_s1rows" : "maxpool_nhwc_vec4")
                : p->vec == 16 ? "maxpool_nhwc_i8_vec16"
                               : "pool_generic";
@@ -390,19 +411,18 @@ int pool_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   const void *x = ctx->tensors[node->inputs[0]].data;
   // Vector paths need 16-byte aligned tensors (a rebinding may move them).
   const bool aligned = (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0;
-  const bool s1 = g.sh == 1 && g.sw == 1 && g.kh == g.kw && (g.kh == 3 || g.kh == 5 || g.kh == 7);
-  if (p->vec == 4 && aligned && s1) {
-    const int64_t columns = int64_t(g.N) * ((g.OH + kPoolBand - 1) / kPoolBand) * g.OW * (g.C / 4);
+  if (p->vec == 4 && aligned && p->band > 0) {
+    const int64_t columns = int64_t(g.N) * ((g.OH + p->band - 1) / p->band) * g.OW * (g.C / 4);
     const int grid = grid_for(columns, 128);
     if (g.kh == 3)
       maxpool_nhwc4_s1_kernel<3><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
-                                                                   static_cast<const float *>(x), g, columns);
+                                                                   static_cast<const float *>(x), g, p->band, columns);
     else if (g.kh == 5)
       maxpool_nhwc4_s1_kernel<5><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
-                                                                   static_cast<const float *>(x), g, columns);
+                                                                   static_cast<const float *>(x), g, p->band, columns);
     else
       maxpool_nhwc4_s1_kernel<7><<<grid, 128, 0, ctx->stream>>>(static_cast<float *>(y),
-                                                                   static_cast<const float *>(x), g, columns);
+                                                                   static_cast<const float *>(x), g, p->band, columns);
   } else if (p->vec == 4 && aligned) {
     maxpool_nhwc4_kernel<<<grid_for(total / 4, 256), 256, 0, ctx->stream>>>(
         static_cast<float *>(y), static_cast<const float *>(x), g, total / 4);
