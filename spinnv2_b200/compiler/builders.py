@@ -296,7 +296,7 @@ OP_CASES = (
     "matmul", "matmul_bcast", "clip", "leakyrelu", "avgpool", "globalavgpool", "mod", "sub", "div",
     "transpose", "tile", "slice_axis1", "slice_axis3", "gather_const", "gather_input", "unsqueeze",
     "topk_ties", "topk_smallest", "topk_long", "softmax_channels", "maxpool_s1_k3", "maxpool_s1_k5",
-    "maxpool_s1_k7", "resize_3x2", "resize_frac",
+    "maxpool_s1_k7", "resize_3x2", "resize_frac", "transpose_last2",
 )
 
 
@@ -366,6 +366,11 @@ def op_case(case: str, batch: int = 2, seed: int = 0) -> Graph:
     if case == "transpose":
         x = pre([n, 8, 5, 6])
         return post(b.op("Transpose", [x], [n, 5, 6, 8], {"perm": [0, 2, 3, 1]}))
+    if case == "transpose_last2":
+        # The form of the detector head's box transpose ([N, 4, anchors] ->
+        # [N, anchors, 4]): the two inner dims swapped, odd sizes on both.
+        x = pre([n, 5, 333])
+        return post(b.op("Transpose", [x], [n, 333, 5], {"perm": [0, 2, 1]}))
     if case == "tile":
         x = pre([n, 3, 4, 5])
         return post(b.op("Tile", [x, net.const("reps", [1, 2, 1, 3])], [n, 6, 4, 15]))
