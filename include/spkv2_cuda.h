@@ -114,8 +114,10 @@ int spkv2_cuda_last_device_code(Spkv2Context *ctx);
  * it; the Python SPK writer calls it for large packages). */
 uint32_t spkv2_fnv1a32(const void *data, size_t size);
 
-/* Allocation-free GEMV: Y[M,N] = alpha * A[M,K] * B[K,N] + bias[N] (bias may
- * be NULL), all row-major fp32 device pointers, launched asynchronously on
+/* Allocation-free GEMV: Y[M,N] = alpha * A[M,K] * B[K,N] + bias[N], all
+ * row-major fp32 device pointers (bias: NULL, or a device pointer to at
+ * least N floats; a host pointer or a shorter buffer is not detected and
+ * faults asynchronously or reads the wrong memory), launched asynchronously on
  * `stream` (a cudaStream_t; NULL = legacy default stream).  This entry point
  * has no counterpart in the reference runtime.  It is for callers that must
  * not allocate device memory while they run - inside a CUDA stream capture,

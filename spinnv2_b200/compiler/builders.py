@@ -32,8 +32,8 @@ class _Init:
     def bias(self, n: int) -> np.ndarray:
         return (self.rng.standard_normal(n, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
 
-    def bn(self, c: int) -> list[np.ndarray]:
-        gamma = self.rng.uniform(0.5, 1.5, c).astype(np.float32)
+    def bn(self, c: int, gamma_scale: float = 1.0) -> list[np.ndarray]:
+        gamma = (self.rng.uniform(0.5, 1.5, c).astype(np.float32) * np.float32(gamma_scale)).astype(np.float32)
         beta = (self.rng.standard_normal(c, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
         mean = (self.rng.standard_normal(c, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
         var = self.rng.uniform(0.5, 1.5, c).astype(np.float32)
@@ -57,7 +57,7 @@ class _Net:
         return f"{kind}{self.n}"
 
     def conv(self, x: int, cout: int, k: int, s: int = 1, p: int | None = None, bias: bool = False,
-             bn: bool = False, act: str | None = None) -> int:
+             bn: bool = False, act: str | None = None, bn_gamma_scale: float = 1.0) -> int:
         nm = self._name("conv")
         n, c, h, w = self.b.shape(x)
         p = k // 2 if p is None else p
@@ -69,7 +69,7 @@ class _Net:
                                                        "pads": [p, p, p, p], "dilations": [1, 1], "group": 1},
                       name=nm)
         if bn:
-            params = [self.b.weight(f"{nm}_bn{i}", v) for i, v in enumerate(self.init.bn(cout))]
+            params = [self.b.weight(f"{nm}_bn{i}", v) for i, v in enumerate(self.init.bn(cout, bn_gamma_scale))]
             y = self.b.op("BatchNormalization", [y] + params, [n, cout, oh, ow], {"epsilon": 1e-5}, name=f"{nm}_bn")
         if act == "Relu":
             y = self.relu(y)
@@ -165,9 +165,20 @@ def conv_sweep(case: str, batch: int = 1, seed: int = 0) -> Graph:
 
 RESNET_LAYERS = {50: [3, 4, 6, 3], 101: [3, 4, 23, 3]}
 
+# Scale of the BatchNorm gamma (drawn from U(0.5, 1.5) like every other BN)
+# of the last conv of each residual branch, the BN that feeds the residual
+# Add.  With random running statistics the folded BN does not normalise, so
+# at gain 1 every bottleneck adds a branch as large as its input and the
+# activations grow ~1.8x per block: ResNet-101's logits reach ~1e8-1e9 and
+# an fp32 comparison of them measures cancellation, not arithmetic.  A small
+# gamma on the branch's last BN (the "zero-init residual" practice of
+# training recipes, here 0.2 instead of 0) keeps the logits O(1-100).
+RESIDUAL_BN_GAMMA = 0.2
+
 
 def resnet(depth: int = 101, batch: int = 1, seed: int = 0) -> Graph:
-    """ResNet v1.5 (stride on the 3x3), head ReduceMean -> Gemm -> Softmax."""
+    """ResNet v1.5 (stride on the 3x3), head ReduceMean -> Gemm -> Softmax.
+    The BN closing each residual branch has gamma scaled by RESIDUAL_BN_GAMMA."""
     net = _Net(f"resnet{depth}_b{batch}", seed)
     x = net.b.input("input", [batch, 3, 224, 224])
     y = net.conv(x, 64, 7, s=2, p=3, bn=True, act="Relu")
@@ -179,7 +190,7 @@ def resnet(depth: int = 101, batch: int = 1, seed: int = 0) -> Graph:
             shortcut = y
             t = net.conv(y, width, 1, bn=True, act="Relu")
             t = net.conv(t, width, 3, s=stride, p=1, bn=True, act="Relu")
-            t = net.conv(t, width * 4, 1, bn=True)
+            t = net.conv(t, width * 4, 1, bn=True, bn_gamma_scale=RESIDUAL_BN_GAMMA)
             if i == 0:
                 shortcut = net.conv(y, width * 4, 1, s=stride, p=0, bn=True)
             y = net.relu(net.add(t, shortcut))

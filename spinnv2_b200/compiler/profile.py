@@ -1,9 +1,12 @@
-"""Target profiles: loading and validation.
+"""Target profiles: lookup and checking against the profile schema.
 
-Same profile schema as SPINNV2 (reference compiler/target/profile.py:10-55,
-compiler/target/target_profile.schema.json): name, word size, endianness,
-alignment, memory caps, features, layouts, backends and an ordered list of
-kernel tokens per op.  Bundled profiles:
+A profile is a JSON object with the fields the SPINNV2 target-profile schema
+lists (reference compiler/target/target_profile.schema.json): name, word size
+(32 or 64), endianness, alignment, memory caps, features, layouts, backends
+and, per op, an ordered list of kernel tokens.  `check_profile` walks a field
+table derived from that schema and reports every violation at once.
+
+Bundled profiles (spinnv2_b200/compiler/profiles/*.json):
 
   cuda_b200        the B200 CUDA target (backend `delegate`, NHWC activations,
                    no `ref` token so no CPU fallback spec is ever emitted,
@@ -13,46 +16,83 @@ kernel tokens per op.  Bundled profiles:
                    package the CPU baseline the reference runtime times
   cpu_ref_large    scalar reference kernels only (strict CPU oracle)
 
-The CUDA profile adds an optional "memory_plan" object that switches off the
-planner's aliases whose meaning depends on NCHW byte order.
+The CUDA profile adds an optional "memory_plan" object (booleans) that
+switches off the planner's aliases whose meaning depends on NCHW byte order.
 """
 
 from __future__ import annotations
 
 import json
 from pathlib import Path
-from typing import Any
+from typing import Any, Callable
 
-REQUIRED_KEYS = {"name", "word_size", "endianness", "alignment", "memory", "features", "layouts", "backends", "ops"}
-
-
-def profiles_dir() -> Path:
-    return Path(__file__).resolve().parent / "profiles"
+BUNDLED = Path(__file__).resolve().parent / "profiles"
 
 
-def load_target_profile(name_or_path: str) -> dict[str, Any]:
-    path = Path(name_or_path)
-    if not path.exists():
-        path = profiles_dir() / f"{name_or_path}.json"
-    if not path.exists():
-        raise FileNotFoundError(f"target profile not found: {name_or_path}")
+def _is_int(v: Any) -> bool:
+    return isinstance(v, int) and not isinstance(v, bool)
+
+
+def _str_list(v: Any) -> bool:
+    return isinstance(v, list) and all(isinstance(x, str) for x in v)
+
+
+# field -> (required, predicate, what the predicate demands)
+_Rule = tuple[bool, Callable[[Any], bool], str]
+TOP_FIELDS: dict[str, _Rule] = {
+    "name": (True, lambda v: isinstance(v, str), "a string"),
+    "word_size": (True, lambda v: _is_int(v) and v in (32, 64), "32 or 64"),
+    "endianness": (True, lambda v: v in ("little", "big"), '"little" or "big"'),
+    "alignment": (True, lambda v: _is_int(v) and v >= 1, "an integer >= 1"),
+    "memory": (True, lambda v: isinstance(v, dict), "an object"),
+    "features": (True, _str_list, "a list of strings"),
+    "layouts": (True, _str_list, "a list of strings"),
+    "backends": (True, _str_list, "a list of strings"),
+    "ops": (True, lambda v: isinstance(v, dict) and all(_str_list(t) for t in v.values()),
+            "an object mapping op names to lists of kernel tokens"),
+    "memory_plan": (False, lambda v: isinstance(v, dict) and all(isinstance(x, bool) for x in v.values()),
+                    "an object of booleans"),
+}
+MEMORY_FIELDS: dict[str, _Rule] = {
+    "activation_arena_max": (True, lambda v: _is_int(v) and v >= 0, "an integer >= 0"),
+    "scratch_arena_max": (True, lambda v: _is_int(v) and v >= 0, "an integer >= 0"),
+    "allow_runtime_malloc": (True, lambda v: isinstance(v, bool), "a boolean"),
+}
+
+
+def _violations(obj: dict[str, Any], rules: dict[str, _Rule], where: str) -> list[str]:
+    out = []
+    for key, (required, ok, demand) in rules.items():
+        if key not in obj:
+            if required:
+                out.append(f"{where}{key}: required field is absent")
+        elif not ok(obj[key]):
+            out.append(f"{where}{key}: must be {demand}, got {obj[key]!r}")
+    return out
+
+
+def check_profile(profile: Any) -> None:
+    """Raise ValueError naming every field of `profile` that breaks the schema."""
+    if not isinstance(profile, dict):
+        raise ValueError("invalid target profile: the top level must be a JSON object")
+    problems = _violations(profile, TOP_FIELDS, "")
+    if isinstance(profile.get("memory"), dict):
+        problems += _violations(profile["memory"], MEMORY_FIELDS, "memory.")
+    if problems:
+        raise ValueError(f"invalid target profile {profile.get('name', '?')!r}: " + "; ".join(problems))
+
+
+def load_target_profile(name_or_path: str | Path) -> dict[str, Any]:
+    """A bundled profile by name, or a profile file by path, checked."""
+    candidates = [Path(name_or_path), BUNDLED / f"{name_or_path}.json"]
+    path = next((c for c in candidates if c.is_file()), None)
+    if path is None:
+        raise FileNotFoundError(f"no target profile named or at {name_or_path!s}")
     profile = json.loads(path.read_text(encoding="utf-8"))
-    validate_target_profile(profile)
+    check_profile(profile)
     return profile
 
 
-def validate_target_profile(profile: dict[str, Any]) -> None:
-    missing = sorted(REQUIRED_KEYS - set(profile))
-    if missing:
-        raise ValueError(f"target profile missing keys: {', '.join(missing)}")
-    if profile["endianness"] not in ("little", "big"):
-        raise ValueError("target profile endianness must be 'little' or 'big'")
-    for key in ("activation_arena_max", "scratch_arena_max", "allow_runtime_malloc"):
-        if key not in profile["memory"]:
-            raise ValueError(f"target profile memory missing key: {key}")
-    if not isinstance(profile["ops"], dict):
-        raise ValueError("target profile ops must be an object")
-
-
 def is_cuda_profile(profile: dict[str, Any]) -> bool:
+    """True for profiles that run on the CUDA target (backend `delegate`)."""
     return "delegate" in profile.get("backends", [])

@@ -5,8 +5,9 @@
 //   y = act(conv(x, W) + b [+ residual])   residual = inputs[3], added before
 //   the activation; act 1 = Relu, 2 = SiLU x / (1 + expf(-x)); groups,
 //   strides, pads, dilations as in the attribute record.
-// INT8 (BASELINE C4 requantisation contract, no reference counterpart on
-// x86 - the reference INT8 conv is ARM-dotprod-only, conv_int8.c:13):
+// INT8 (this target's requantisation contract for int8 networks; no
+// reference counterpart on x86 - the reference INT8 conv is
+// ARM-dotprod-only, conv_int8.c:13):
 //   acc  = sum over k of int32(w_q) * int32(x_q)              (exact int32)
 //   acc' = acc + b_q[c]                                        (int32 bias)
 //   v    = fp32(acc') * M[c],  M[c] = fp32(s_x * s_w[c]) / s_y (host, fp32)

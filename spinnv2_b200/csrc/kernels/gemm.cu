@@ -14,6 +14,7 @@
 // (a size-1 or missing dim repeats); no bias, no alpha.  Device design: the
 // 64x64x16 tiled kernel over element strides (any operand may be an NHWC
 // rank-4 activation), one grid z-slice per batch matrix.
+#include <atomic>
 #include <string.h>
 
 #include "conv.h"
@@ -292,7 +293,10 @@ constexpr size_t kNoAllocPartials = 262144;
 __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
 
 constexpr int kMaxDevices = 64;
-float *g_noalloc_ptr[kMaxDevices] = {};
+// Per-device cache of the array's device address.  Atomic slots: host
+// threads making their first call on one device at the same time each
+// resolve the address (the same value) and store it without a data race.
+std::atomic<float *> g_noalloc_ptr[kMaxDevices] = {};
 
 // Device address of g_noalloc_partials on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address must come
@@ -300,13 +304,15 @@ float *g_noalloc_ptr[kMaxDevices] = {};
 int noalloc_scratch(float **out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SPKV2_ERR_NO_DEVICE;
-  if (!g_noalloc_ptr[dev]) {
+  float *cached = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!cached) {
     void *p = nullptr;
     const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_partials);
     if (err != cudaSuccess || !p) return cuda_status(err == cudaSuccess ? cudaErrorInvalidSymbol : err);
-    g_noalloc_ptr[dev] = static_cast<float *>(p);
+    cached = static_cast<float *>(p);
+    g_noalloc_ptr[dev].store(cached, std::memory_order_release);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = cached;
   return 0;
 }
 

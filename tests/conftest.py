@@ -62,3 +62,26 @@ def reference_outputs(spk_cpu: bytes, inputs: list[np.ndarray]) -> list[np.ndarr
 
     pkg = read_spk(spk_cpu)
     return refrt.run_reference(spk_cpu, inputs, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs])
+
+
+def compile_with_outputs(name: str, batch: int, pick, targets=("cuda_b200", "cpu_generic_x86")) -> dict:
+    """Config `name` at `batch`, fused once, with extra graph outputs: the
+    tensor ids pick(graph) returns (intermediates such as the pre-softmax
+    logits) are appended to the graph's outputs, so the reference CPU runtime
+    reports them too.  The convolutions and their plans are the config's."""
+    import copy
+
+    from spinnv2_b200.compiler import builders, pipeline
+
+    graph = pipeline.fuse(builders.build_config(name, batch))
+    from spinnv2_b200.compiler.ir import ROLE_OUTPUT
+
+    extra = [t for t in pick(graph) if t not in graph.outputs]
+    for t in extra:
+        graph.tensors[t].role = ROLE_OUTPUT
+    graph.outputs = list(graph.outputs) + extra
+    return {t: pipeline.package(copy.deepcopy(graph), t) for t in targets}
+
+
+def gemm_output(graph) -> list[int]:
+    return [next(n for n in graph.nodes if n.op_type == "Gemm").outputs[0]]

@@ -1,7 +1,8 @@
 """Regenerate the compiler golden fixtures from the REFERENCE compiler.
 
-Run in a container that has the reference tree (default /root/reference):
-    python tests/golden/make_golden.py [reference_root]
+Run where the reference tree is available, giving its root as the argument
+or in SPKV2_REFERENCE_ROOT:
+    python tests/golden/make_golden.py <reference_root>
 For each config it builds the same SIR graph, runs the reference compiler's
 pass pipeline, KernelSpec planner, memory planner and SPK writer with the
 x86 CPU profile, and records the SHA-256 of the package.  The tests check
@@ -14,13 +15,17 @@ from __future__ import annotations
 import copy
 import hashlib
 import json
+import os
 import sys
 import tempfile
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO))
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPKV2_REFERENCE_ROOT")
+if not _root:
+    sys.exit("usage: make_golden.py <reference_root>  (or set SPKV2_REFERENCE_ROOT)")
+REF = Path(_root)
 sys.path.insert(0, str(REF))
 
 import numpy as np  # noqa: E402

@@ -58,6 +58,30 @@ def test_gemv_noalloc_matches_gemm_node_on_two_calls(gpu):
             np.testing.assert_allclose(y.cpu().numpy(), expected, atol=ATOL, rtol=RTOL)
 
 
+def test_gemv_noalloc_shrinks_split_to_fit_its_scratch(gpu):
+    """M = 8, K = 2048, N = 4000: the default split of K into 16 parts would
+    need 16 * 8 * 4000 partial sums, over the 262144-float scratch, so the
+    entry point drops to 8 parts (8 * 8 * 4000 = 256000 fit).  Two calls in a
+    row against A @ B + bias computed in float64 by numpy."""
+    import torch
+
+    M, K, N = 8, 2048, 4000
+    rng = np.random.default_rng(21)
+    w = (rng.standard_normal((K, N), dtype=np.float32) * np.float32(np.sqrt(2.0 / K))).astype(np.float32)
+    b = (rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    w_d, b_d = torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda()
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    fn = _fn()
+    for seed in (5, 6):
+        x = seeded_input((M, K), seed=seed)
+        a = torch.from_numpy(x).cuda()
+        torch.cuda.synchronize()
+        assert fn(a.data_ptr(), w_d.data_ptr(), b_d.data_ptr(), y.data_ptr(), M, K, N, 1.0, None) == 0
+        torch.cuda.synchronize()
+        expected = (x.astype(np.float64) @ w.astype(np.float64) + b).astype(np.float32)
+        np.testing.assert_allclose(y.cpu().numpy(), expected, atol=ATOL, rtol=RTOL)
+
+
 def test_gemv_noalloc_rejects_sizes_beyond_its_scratch(gpu):
     import torch
 
