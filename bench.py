@@ -6,15 +6,20 @@ One step = one ResNet-101 v1.5 forward pass (fp32 activations, 3xTF32 conv
 math by default) over a batch of 64 synthetic N(0,1) 3x224x224 images with
 seeded random-init weights, executed by libspkv2_runtime.so.  Multi-GPU is
 batch-sharded inference with no data-path collective: every rank holds its
-own SPK, weights and arenas and runs its own batch of 64 (weak scaling);
-torch.distributed only provides the start/stop barrier and the max-over-ranks
-of the timed region.
+own SPK, weights and arenas.  The headline runs 64 images per rank (weak
+scaling); the `strong` sub-object splits one global batch of 64 (and 256)
+into contiguous ceil(B/N) slices, one per rank.  torch.distributed only
+provides the start/stop barrier and the max-over-ranks of the timed region.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Prints one JSON line on rank 0.  --impl reference times the reference
-SPINNV2 CPU runtime (oracle/_ref, built from the reference's own sources) on
-the host cores for the same config, on a bounded batch sample per step.
+Prints one JSON line on rank 0.  On one GPU the line also carries the other
+figures of the north star: plain TF32 mode, INT8 ResNet-50 at batch 256, the
+YOLOv10n-style detector at batch 1 and 64, the memory-bound ops of that
+detector, the bs1 latency and the reference CPU runtime at all host cores and
+at one thread.  --impl reference times the reference SPINNV2 CPU runtime
+(oracle/_ref, built from the reference's own sources) on the host cores for
+the same config and batch.
 """
 
 from __future__ import annotations
@@ -34,15 +39,14 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-METRIC = "ResNet-101 img/s (bs64 per GPU)"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
 def metric_name(args) -> str:
     """The fp32 headline metric, or the INT8 ResNet-50 line (--int8)."""
     if args.int8:
         return f"ResNet-50 INT8 img/s (bs{args.batch} per GPU)"
-    return METRIC
-PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+    return f"ResNet-101 img/s (bs{args.batch} per GPU)"
 
 
 def peaks() -> tuple[dict, str]:
@@ -159,31 +163,30 @@ def conv_flops(pkg, int8_only: bool = False) -> tuple[float, list[int]]:
     return total, ids
 
 
-def conv_bytes(pkg, ids: list[int]) -> int:
-    """Algorithmic HBM bytes of the given conv nodes: every input (activation,
-    weights, bias, residual) read once and the output written once."""
+def node_bytes(pkg, ids, skip_weights: bool = False) -> int:
+    """Algorithmic HBM bytes of the given nodes: every input (activation,
+    weights, bias, residual) read once and every output written once."""
     total = 0
     for n in pkg.nodes:
         if n.id in ids:
             for t in list(n.inputs) + list(n.outputs):
                 if t >= 0:
                     ten = pkg.tensors[t]
+                    if skip_weights and ten.role_name == "weight":
+                        continue
                     total += int(np.prod(ten.shape)) * np.dtype(ten.np_dtype).itemsize
     return total
 
 
-# DRAM bytes (read + write) of the conv launches of one step, each from one
-# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
-# pass through the network:
-#   fp32: ncu ... -c 560 python bench.py --steps 2 --warmup 3 --no-cpu-baseline --latency-runs 5
-#         (the 105 conv launches of launches 433..541)
-#   int8: ncu ... -k regex:conv_i8 -s 52 -c 52 python bench.py --config resnet50 --int8 --batch 256
-#         --steps 2 --warmup 3 --no-cpu-baseline --latency-runs 5
-# Keyed by the workload it was measured on; other workloads report null.
-MEASURED_CONV_TRAFFIC = {
-    ("resnet101", 64, "3xtf32", False): 6591.0e6 + 1543.6e6,
-    # the 52 int8 conv launches of one ResNet-50 bs256 step
-    ("resnet50", 256, "int8", True): 3861.2e6 + 1179.7e6,
+# DRAM traffic of the conv kernels relative to their algorithmic bytes, from
+# ncu captures of single launches on small cases (one kernel, one launch per
+# capture, a process of a few hundred MB; cold cache, so the input is read
+# from DRAM).  traffic_step = ratio x the step's algorithmic conv bytes.
+# Keyed by conv math; each entry names its capture.
+CONV_TRAFFIC_RATIO = {
+    "3xtf32": (None, "not captured"),
+    "tf32": (None, "not captured"),
+    "int8": (None, "not captured"),
 }
 
 
@@ -194,15 +197,26 @@ def use_all_host_threads() -> None:
     os.environ["OMP_NUM_THREADS"] = os.environ.get("SPKV2_REF_THREADS", str(os.cpu_count() or 1))
 
 
+def reference_package(config: str, batch: int) -> bytes:
+    """The config packaged for the reference CPU runtime.  The package
+    checksum is computed by the compiler's pure-Python FNV-1a, so the
+    reference arm never maps this repository's CUDA library."""
+    from spinnv2_b200.compiler import pipeline, spk_writer
+
+    spk_writer.NATIVE_FNV = False
+    return pipeline.compile_config(config, batch, targets=("cpu_generic_x86",))["cpu_generic_x86"]
+
+
 def cpu_oracle_int8_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
     """INT8 CPU baseline: the reference's INT8 conv kernel is ARM-dotprod only
     (on x86 it falls back to the fp32 loop over int8 bytes), so the INT8
     baseline is the oracle's C restatement of the INT8 contract (OpenMP over
     output channels) running the same package, timed on a bounded sample."""
     from oracle import harness
-    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.compiler import pipeline, spk_writer
     from spinnv2_b200.spk import read_spk
 
+    spk_writer.NATIVE_FNV = False
     spk = pipeline.compile_config(config, batch, targets=("cuda_b200",), int8=True)["cuda_b200"]
     pkg = read_spk(spk)
     x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
@@ -220,10 +234,9 @@ def cpu_oracle_int8_throughput(config: str, batch: int, seconds: float, max_step
 def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps: int | None = None) -> dict:
     """Reference CPU runtime (oracle/_ref) img/s on a bounded sample."""
     from oracle import refrt
-    from spinnv2_b200.compiler import pipeline
     from spinnv2_b200.spk import read_spk
 
-    spk = pipeline.compile_config(config, batch, targets=("cpu_generic_x86",))["cpu_generic_x86"]
+    spk = reference_package(config, batch)
     pkg = read_spk(spk)
     x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
     rt = refrt.RefRuntime(spk, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs])
@@ -239,31 +252,158 @@ def cpu_reference_throughput(config: str, batch: int, seconds: float, max_steps:
     return {"value": batch / per, "step_s": per, "steps": len(times), "times": times}
 
 
+def cpu_one_thread(config: str, seconds: float) -> dict | None:
+    """The reference CPU runtime with one OpenMP thread (a child process, so
+    the thread count is fixed before the runtime loads), batch 1."""
+    code = ("import json, sys; sys.path.insert(0, %r); import bench; "
+            "r = bench.cpu_reference_throughput(%r, 1, %r); r.pop('times'); print(json.dumps(r))"
+            % (str(REPO), config, seconds))
+    env = dict(os.environ, OMP_NUM_THREADS="1", SPKV2_REF_THREADS="1")
+    try:
+        out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                             timeout=seconds * 6 + 120, check=True)
+        return json.loads(out.stdout.strip().splitlines()[-1])
+    except (subprocess.SubprocessError, ValueError, IndexError):
+        return None
+
+
 def run_reference_arm(args, group) -> None:
+    """The reference CPU runtime on the host cores, on the GPU arm's config
+    and batch: every step runs the whole batch (rank 0 only)."""
     if group.rank != 0:
         return
-    sample = min(args.batch, args.reference_sample)
     use_all_host_threads()
-    timer = cpu_oracle_int8_throughput if args.int8 else cpu_reference_throughput
-    res = timer(args.config, sample, seconds=1e9, max_steps=args.warmup + args.steps)
-    timed = res["times"][args.warmup:] or res["times"]
+    if args.int8:
+        res = cpu_oracle_int8_throughput(args.config, args.batch, seconds=1e9, max_steps=args.warmup + args.steps)
+        times = res["times"]
+    else:
+        from oracle import refrt
+        from spinnv2_b200.spk import read_spk
+
+        spk = reference_package(args.config, args.batch)
+        pkg = read_spk(spk)
+        x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+        rt = refrt.RefRuntime(spk, [(tuple(t.shape), t.np_dtype) for t in pkg.outputs])
+        times = []
+        for _ in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            rt.run(x)
+            times.append(time.perf_counter() - t0)
+        rt.close()
+    timed = times[args.warmup:] or times
     ms = 1000.0 * sum(timed) / len(timed)
-    value = sample / (ms / 1000.0)
+    value = args.batch / (ms / 1000.0)
     line = {
         "impl": "reference", "metric": metric_name(args), "value": value, "unit": "img/s", "n_gpus": args.gpus,
         "steps": len(timed), "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.int8 else "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config} {'int8' if args.int8 else 'fp32'} forward, batch {args.batch}",
-                   "model": args.config, "global_batch": args.batch, "sample_batch_per_step": sample,
+        "config": {"workload": workload_name(args), "model": args.config, "global_batch": args.batch,
                    "runtime": ("INT8 oracle (C restatement of the INT8 contract, OpenMP); the reference INT8 kernel "
                                "is ARM-dotprod only") if args.int8 else
                    "reference cpu_generic (AVX2/FMA, OpenMP), BNNS token removed from the profile"},
         "cpu_baseline": {"value": value, "unit": "img/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
                          "kind": "port" if args.int8 else "reference",
-                         "sample": f"{sample} images per step, {len(timed)} steps"},
+                         "sample": f"the full batch of {args.batch} per step, {len(timed)} timed steps"},
         "e2e": {"value": value, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def workload_name(args) -> str:
+    if args.int8:
+        return f"{args.config} INT8 forward, batch {args.batch} per GPU, 224x224, int8 activations between convs"
+    return f"{args.config} v1.5 forward, batch {args.batch} per GPU, 224x224, fp32 activations, conv math {args.math}"
+
+
+# ---------------------------------------------------------------- GPU timing
+
+
+def time_replays(rt, steps: int, warmup: int, flush, stream) -> list[float]:
+    """Device ms of `steps` graph replays (after `warmup`), each bracketed by
+    CUDA events on the runtime's own stream, with an L2 flush (a 256 MiB
+    write) between steps."""
+    import torch
+
+    for _ in range(warmup):
+        rt.run_async()
+    rt.synchronize()
+    torch.cuda.synchronize()
+    evs = []
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            rt.run_async()
+            e.record(stream)
+            evs.append((s, e))
+    rt.synchronize()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def node_shares(rt, repeats: int = 3) -> np.ndarray:
+    """Per-node device ms of eager, event-bracketed runs (mean of `repeats`)."""
+    return np.stack([rt.profile_nodes() for _ in range(repeats)]).mean(axis=0)
+
+
+def conv_roofline(rt, pkg, ms_per_step: float, int8: bool, math_label: str) -> dict:
+    """Conv roofline of a graph-replayed step: the conv nodes' share of the
+    eager per-node device time, times the replayed step time, gives their
+    time in the step; achieved = conv FLOPs (or int8 ops) / that time."""
+    flops, ids = conv_flops(pkg, int8_only=int8)
+    node_ms = node_shares(rt)
+    share = float(node_ms[ids].sum() / max(node_ms.sum(), 1e-9))
+    conv_ms = share * ms_per_step
+    pk, basis = peaks()
+    if int8:
+        peak, unit = pk["bf16_tflops"] * 2.0, "TOPS"
+        peak_basis = f"INT8 dense = bf16 {basis} {pk['bf16_tflops']} x 2 (derived)"
+    else:
+        peak, unit = pk["bf16_tflops"] / 2.0, "TFLOP/s"
+        peak_basis = f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"
+    achieved = flops / (conv_ms / 1000.0) / 1e12
+    alg = node_bytes(pkg, ids)
+    key = "int8" if int8 else math_label
+    ratio, capture = CONV_TRAFFIC_RATIO.get(key, (None, "not captured"))
+    out = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+           "traffic": alg * ratio if ratio else None,
+           "traffic_basis": (f"scaled: {ratio:.3f} x the step's algorithmic conv bytes, the DRAM/algorithmic "
+                             f"ratio of {capture}") if ratio else capture,
+           "algorithmic_bytes_per_step": alg,
+           "kernel": ("all int8 Conv launches" if int8 else "all Conv launches") + " of one graph-replayed step",
+           "flops_per_step": flops, "conv_share_of_step": share, "conv_ms_per_step": conv_ms,
+           "peak_basis": peak_basis, "conv_variants": sorted({rt.node_variant(i) for i in ids})}
+    if math_label == "3xtf32" and not int8:
+        # Each product is three TF32 MMAs: the tensor pipe's TF32 work rate.
+        out["tensor_pipe_frac"] = 3.0 * achieved / peak
+    return out
+
+
+def device_run(config: str, batch: int, args, local: int, math_mode: int | None, int8: bool = False,
+               want_roofline: bool = False, math_label: str = "3xtf32", flush=None) -> dict:
+    """Graph-replayed throughput of one config with the input resident in HBM."""
+    import torch
+
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import Runtime
+
+    spk = pipeline.compile_config(config, batch, targets=("cuda_b200",), seed=0, int8=int8)["cuda_b200"]
+    with Runtime(spk, device=local, math_mode=math_mode, graph=True) as rt:
+        pkg = rt.package
+        x = np.random.default_rng(5).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+        if config == "yolo_style":
+            x = np.random.default_rng(5).random(pkg.inputs[0].shape, dtype=np.float32)
+        d_in = torch.from_numpy(x).cuda(local)
+        rt.bind_input(0, d_in.data_ptr())
+        stream = torch.cuda.ExternalStream(rt.stream())
+        step_ms = time_replays(rt, args.steps, args.warmup, flush, stream)
+        ms = sum(step_ms) / len(step_ms)
+        out = {"value": batch / (ms / 1000.0), "unit": "img/s", "ms_per_step": ms, "batch": batch,
+               "steps": args.steps, "gpu_launches_per_step": rt.launches_per_run()}
+        if want_roofline:
+            out["roofline"] = conv_roofline(rt, pkg, ms, int8, math_label)
+    return out
 
 
 def latency_bs1(args, local: int, math_mode: int) -> dict:
@@ -299,61 +439,95 @@ def latency_bs1(args, local: int, math_mode: int) -> dict:
             "path": "spkv2_run: pinned host input -> graph replay -> pinned host output"}
 
 
-def run_memory_bound(args, group) -> None:
+def memory_bound(batch: int, local: int) -> dict:
     """Memory-bound ops (every node that is not a Conv/Gemm) of the
-    YOLOv10n-style config at `--mb-batch`: per node, algorithmic bytes (every
-    input and output tensor read/written once) / device time (per-node CUDA
-    events, mean of 5 passes), aggregated per op type, against the measured
-    HBM copy bandwidth.  Rank 0 prints one JSON line."""
-    if group.rank != 0:
-        return
+    YOLOv10n-style config: per node, algorithmic bytes (every input and
+    output tensor read/written once) / device time (per-node CUDA events,
+    mean of 5 passes), aggregated per op type, against the measured HBM copy
+    bandwidth."""
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import Runtime
+
+    spk = pipeline.compile_config("yolo_style", batch, targets=("cuda_b200",), seed=0)["cuda_b200"]
+    with Runtime(spk, device=local, graph=False) as rt:
+        pkg = rt.package
+        x = np.random.default_rng(3).random(pkg.inputs[0].shape, dtype=np.float32)
+        rt.set_input(0, x)
+        rt.run()
+        ms = node_shares(rt, 5)
+        per_op: dict[str, list[float]] = {}
+        nodes = []
+        for n in pkg.nodes:
+            if n.op_type in ("Conv", "Gemm") or ms[n.id] <= 0:
+                continue
+            nbytes = node_bytes(pkg, [n.id], skip_weights=True)
+            acc = per_op.setdefault(n.op_type, [0, 0.0, 0.0])
+            acc[0] += 1
+            acc[1] += nbytes
+            acc[2] += float(ms[n.id])
+            nodes.append((nbytes / (ms[n.id] * 1e-3) / 1e9, n.op_type, n.id, nbytes, float(ms[n.id]),
+                          rt.node_variant(n.id)))
+    pk, basis = peaks()
+    tot_b = sum(v[1] for v in per_op.values())
+    tot_ms = sum(v[2] for v in per_op.values())
+    big = [r for r in nodes if r[3] >= 64 * 2**20]  # tensors well above L2
+    gbs = tot_b / (tot_ms * 1e-3) / 1e9
+    return {
+        "metric": "memory-bound op GB/s (YOLOv10n-style, non-conv nodes)", "unit": "GB/s", "value": gbs,
+        "workload": f"yolo_style 640x640 fp32 forward, batch {batch}", "nodes": len(nodes),
+        "peak": pk["hbm_gbs"], "peak_basis": f"HBM copy, {basis}", "frac": gbs / pk["hbm_gbs"],
+        "ms_per_step": tot_ms,
+        "per_op": {k: {"nodes": v[0], "bytes": int(v[1]), "ms": v[2], "gbs": v[1] / (v[2] * 1e-3) / 1e9}
+                   for k, v in sorted(per_op.items(), key=lambda kv: -kv[1][2])},
+        "nodes_over_64MiB_gbs": (sum(r[3] for r in big) / (sum(r[4] for r in big) * 1e-3) / 1e9) if big else None,
+        "top_nodes": [{"op": r[1], "node": r[2], "bytes": r[3], "ms": r[4], "gbs": r[0], "variant": r[5]}
+                      for r in sorted(nodes, key=lambda r: -r[4])[:8]],
+    }
+
+
+def strong_scaling(args, group, math_mode: int, flush) -> dict:
+    """One global batch split into contiguous ceil(B/N) slices, one per rank
+    (the per-rank form of ShardedRuntime): each rank compiles and prepares
+    its slice, then every step replays it; device time per step is the max
+    over ranks.  Two figures per global batch: inputs resident in HBM, and
+    end to end through spkv2_run with the rank's slice copied from pinned
+    host memory and the outputs copied back."""
     import torch
 
     from spinnv2_b200.compiler import pipeline
     from spinnv2_b200.runtime import Runtime
 
-    torch.cuda.set_device(group.local_rank)
-    spk = pipeline.compile_config("yolo_style", args.mb_batch, targets=("cuda_b200",), seed=0)["cuda_b200"]
-    with Runtime(spk, device=group.local_rank, graph=False) as rt:
-        pkg = rt.package
-        x = np.random.default_rng(3).random(pkg.inputs[0].shape, dtype=np.float32)
-        rt.set_input(0, x)
-        rt.run()
-        ms = np.mean([rt.profile_nodes() for _ in range(5)], axis=0)
-        per_op: dict[str, list[float]] = {}
-        nodes = []
-        for n in pkg.nodes:
-            if n.op_type in ("Conv", "Gemm"):
-                continue
-            nbytes = 0
-            for t in list(n.inputs) + list(n.outputs):
-                if t >= 0 and pkg.tensors[t].role_name != "weight":
-                    ten = pkg.tensors[t]
-                    nbytes += int(np.prod(ten.shape)) * np.dtype(ten.np_dtype).itemsize
-            if ms[n.id] <= 0:
-                continue
-            acc = per_op.setdefault(n.op_type, [0, 0.0, 0.0])
-            acc[0] += 1
-            acc[1] += nbytes
-            acc[2] += float(ms[n.id])
-            nodes.append((nbytes / (ms[n.id] * 1e-3) / 1e9, n.op_type, n.id, nbytes, float(ms[n.id]), rt.node_variant(n.id)))
-    pk, basis = peaks()
-    tot_b = sum(v[1] for v in per_op.values())
-    tot_ms = sum(v[2] for v in per_op.values())
-    big = [r for r in nodes if r[3] >= 64 * 2**20]  # tensors well above L2
-    line = {
-        "metric": "memory-bound op GB/s (YOLOv10n-style, non-conv nodes)", "unit": "GB/s",
-        "value": tot_b / (tot_ms * 1e-3) / 1e9, "higher_is_better": True, "n_gpus": 1, "data": "synthetic",
-        "config": {"workload": f"yolo_style 640x640 fp32 forward, batch {args.mb_batch}", "nodes": len(nodes)},
-        "peak": {"value": pk["hbm_gbs"], "unit": "GB/s", "basis": f"HBM copy, {basis}"},
-        "frac": tot_b / (tot_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
-        "per_op": {k: {"nodes": v[0], "bytes": int(v[1]), "ms": v[2], "gbs": v[1] / (v[2] * 1e-3) / 1e9}
-                   for k, v in sorted(per_op.items(), key=lambda kv: -kv[1][2])},
-        "nodes_over_64MiB_gbs": (sum(r[3] for r in big) / (sum(r[4] for r in big) * 1e-3) / 1e9) if big else None,
-        "top_nodes": [{"op": r[1], "node": r[2], "bytes": r[3], "ms": r[4], "gbs": r[0], "variant": r[5]}
-                      for r in sorted(nodes, key=lambda r: -r[4])[:12]],
-    }
-    print(json.dumps(line), flush=True)
+    out = {}
+    for gb in args.strong_batches:
+        start, count = group.slice(gb)
+        spk = pipeline.compile_config(args.config, max(count, 1), targets=("cuda_b200",), seed=0)["cuda_b200"]
+        with Runtime(spk, device=group.local_rank, math_mode=math_mode, graph=True) as rt:
+            pkg = rt.package
+            x = np.random.default_rng(40 + group.rank).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+            d_in = torch.from_numpy(x).cuda(group.local_rank)
+            rt.bind_input(0, d_in.data_ptr())
+            stream = torch.cuda.ExternalStream(rt.stream())
+            group.barrier()
+            step_ms = time_replays(rt, args.steps, args.warmup, flush, stream) if count else [0.0] * args.steps
+            dev_ms = group.max(sum(step_ms)) / args.steps
+            h_in = torch.from_numpy(x).pin_memory()
+            h_out = [torch.empty(tuple(t.shape), dtype=torch.float32).pin_memory() for t in pkg.outputs]
+            rt.bind_input(0, h_in.data_ptr())
+            for k, o in enumerate(h_out):
+                rt.bind_output(k, o.data_ptr())
+            for _ in range(2):
+                rt._check(rt.lib.spkv2_run(rt.ctx), "run")
+            group.barrier()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                if count:
+                    rt._check(rt.lib.spkv2_run(rt.ctx), "run")
+            e2e_s = group.max(time.perf_counter() - t0)
+        out[f"global_batch_{gb}"] = {
+            "value": gb * args.steps / (dev_ms * args.steps / 1000.0), "unit": "img/s", "ms_per_step": dev_ms,
+            "e2e_value": gb * args.steps / e2e_s, "per_gpu_batch": count, "n_gpus": group.world,
+            "slices": "contiguous ceil(B/N) per rank, one SPK per slice size"}
+    return out
 
 
 def run_gpu_arm(args, group) -> None:
@@ -367,6 +541,7 @@ def run_gpu_arm(args, group) -> None:
     math_mode = {"spec": MATH_SPEC, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32, "fp32": MATH_FP32}[args.math]
     math_label = "3xtf32" if args.math in ("spec", "3xtf32") else args.math
     torch.cuda.set_device(local)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local}")  # > 126 MB L2
     spk = pipeline.compile_config(args.config, args.batch, targets=("cuda_b200",), seed=0, int8=args.int8)["cuda_b200"]
     rt = Runtime(spk, device=local, math_mode=math_mode, graph=True)
     pkg = rt.package
@@ -378,7 +553,6 @@ def run_gpu_arm(args, group) -> None:
     # ---- device-resident timing (inputs already in HBM) ----
     d_in = torch.from_numpy(x).cuda(local)
     rt.bind_input(0, d_in.data_ptr())
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local}")  # > 126 MB L2
     for _ in range(args.warmup):
         rt.run_async()
     rt.synchronize()
@@ -386,84 +560,63 @@ def run_gpu_arm(args, group) -> None:
     sampler.start()
     time.sleep(0.3)
     group.barrier()
-    torch.cuda.synchronize()
-    evs = []
-    with torch.cuda.stream(stream):
-        for _ in range(args.steps):
-            flush.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            rt.run_async()
-            e.record(stream)
-            evs.append((s, e))
-    rt.synchronize()
-    torch.cuda.synchronize()
+    step_ms = time_replays(rt, args.steps, 0, flush, stream)
     group.barrier()
     clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in evs]
-    local_total_ms = sum(step_ms)
-    total_ms = group.max(local_total_ms)
+    total_ms = group.max(sum(step_ms))
     ms_per_step = total_ms / args.steps
     value = world * args.batch * args.steps / (total_ms / 1000.0)
-
-    # ---- roofline of the conv kernels (per-node events) ----
-    flops, conv_ids = conv_flops(pkg, int8_only=args.int8)
-    prof = np.stack([rt.profile_nodes() for _ in range(3)])
-    node_ms = prof.mean(axis=0)
-    conv_ms = float(node_ms[conv_ids].sum())
-    pk, basis = peaks()
-    if args.int8:
-        peak, peak_unit = pk["bf16_tflops"] * 2.0, "TOPS"
-        peak_basis = f"INT8 dense = bf16 {basis} {pk['bf16_tflops']} x 2 (derived)"
-    else:
-        peak, peak_unit = pk["bf16_tflops"] / 2.0, "TFLOP/s"
-        peak_basis = f"TF32 dense = bf16 {basis} {pk['bf16_tflops']} / 2 (derived)"
-    achieved = flops / (conv_ms / 1000.0) / 1e12
-    variants = sorted({rt.node_variant(i) for i in conv_ids})
-    alg_bytes = conv_bytes(pkg, conv_ids)
-    eff_math = "int8" if args.int8 else math_label
-    traffic = MEASURED_CONV_TRAFFIC.get((args.config, args.batch, eff_math, args.int8))
+    roof = conv_roofline(rt, pkg, ms_per_step, args.int8, math_label)
+    launches = rt.launches_per_run() * args.steps
 
     # ---- end to end through the public API: pinned host in/out, spkv2_run ----
-    rt2 = Runtime(spk, device=local, math_mode=math_mode, graph=True)
     h_in = torch.from_numpy(x).pin_memory()
     h_out = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory()
-    rt2.bind_input(0, h_in.data_ptr())
-    rt2.bind_output(0, h_out.data_ptr())
+    rt.bind_input(0, h_in.data_ptr())
+    rt.bind_output(0, h_out.data_ptr())
     for _ in range(max(args.warmup, 2)):
-        rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
+        rt._check(rt.lib.spkv2_run(rt.ctx), "run")
     group.barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        rt2._check(rt2.lib.spkv2_run(rt2.ctx), "run")
+        rt._check(rt.lib.spkv2_run(rt.ctx), "run")
     e2e_s = group.max(time.perf_counter() - t0)
     e2e_value = world * args.batch * args.steps / e2e_s
-    launches = rt.launches_per_run() * args.steps
-    rt2.close()
+    rt.close()
+    del d_in
     lat = latency_bs1(args, local, math_mode)  # every rank, so the ranks stay in step
+    strong = strong_scaling(args, group, math_mode, flush) if not args.int8 and args.strong_batches else None
+
+    extras = {}
+    if world == 1 and not args.int8 and not args.no_extras:
+        extras["tf32_mode"] = device_run(args.config, args.batch, args, local, MATH_TF32, want_roofline=True,
+                                         math_label="tf32", flush=flush)
+        extras["int8"] = device_run("resnet50", args.int8_batch, args, local, None, int8=True, want_roofline=True,
+                                    flush=flush)
+        extras["int8"]["workload"] = f"resnet50 INT8 forward, batch {args.int8_batch}"
+        extras["yolo"] = {f"bs{b}": device_run("yolo_style", b, args, local, math_mode, flush=flush)
+                          for b in (1, args.mb_batch)}
+        extras["memory_bound"] = memory_bound(args.mb_batch, local)
 
     if rank == 0:
         line = {
             "metric": metric_name(args), "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8" if args.int8 else "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config} v1.5 forward, batch {args.batch} per GPU, 224x224, " + (
-                           "int8 activations between convs (fp32 first conv and head)" if args.int8 else
-                           f"fp32 activations, conv math {args.math}"),
-                       "model": args.config, "global_batch": args.batch * world, "per_gpu_batch": args.batch,
-                       "seq_len": None, "parallelism": f"batch-sharded x{world}, no collectives",
-                       "l2": "flushed between steps (256 MiB write)", "conv_variants": variants},
+            "config": {"workload": workload_name(args), "model": args.config, "global_batch": args.batch * world,
+                       "per_gpu_batch": args.batch, "seq_len": None,
+                       "parallelism": f"batch-sharded x{world}, no collectives",
+                       "l2": "flushed between steps (256 MiB write)"},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
                     "d2h_bytes_per_step": int(np.prod(out_t.shape) * 4)},
             "gpu_launches": int(launches),
             "latency_bs1": lat,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": peak_unit,
-                         "frac": achieved / peak, "traffic": traffic,
-                         "algorithmic_bytes_per_step": alg_bytes,
-                         "kernel": ("all int8 Conv launches" if args.int8 else "all Conv launches") + " of one step",
-                         "flops_per_step": flops, "conv_ms_per_step": conv_ms, "peak_basis": peak_basis},
+            "roofline": roof,
         }
+        if strong:
+            line["strong"] = strong
+        line.update(extras)
         if world == 1 and not args.no_cpu_baseline:
             use_all_host_threads()
             timer = cpu_oracle_int8_throughput if args.int8 else cpu_reference_throughput
@@ -472,25 +625,33 @@ def run_gpu_arm(args, group) -> None:
                                     "kind": "port" if args.int8 else "reference",
                                     "sample": f"batch 1, {cb['steps']} runs over ~{args.cpu_seconds:.0f} s",
                                     "p50_ms_bs1": 1000.0 * cb["step_s"]}
+            if not args.int8:
+                one = cpu_one_thread(args.config, args.cpu_seconds)
+                if one:
+                    line["cpu_baseline"]["one_thread"] = {
+                        "value": one["value"], "unit": "img/s", "cores": 1, "p50_ms_bs1": 1000.0 * one["step_s"],
+                        "sample": f"batch 1, {one['steps']} runs over ~{args.cpu_seconds:.0f} s"}
         print(json.dumps(line), flush=True)
-    rt.close()
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=60)  # ~0.5 s timed at bs64 3xTF32
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="resnet101")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--math", default="spec", choices=["spec", "3xtf32", "tf32", "fp32"])
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--reference-sample", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="headline only (no TF32/INT8/YOLO/memory-bound)")
     ap.add_argument("--latency-runs", type=int, default=200, help="timed spkv2_run calls for the bs1 latency")
-    ap.add_argument("--memory-bound", action="store_true", help="GB/s of the YOLOv10n-style non-conv ops instead")
+    ap.add_argument("--strong-batches", type=int, nargs="*", default=[64, 256],
+                    help="global batches split across the ranks (strong scaling)")
+    ap.add_argument("--memory-bound", action="store_true", help="only the YOLOv10n-style memory-bound line")
     ap.add_argument("--mb-batch", type=int, default=64)
+    ap.add_argument("--int8-batch", type=int, default=256)
     ap.add_argument("--int8", action="store_true", help="INT8 quantised network (use with --config resnet50)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -507,7 +668,8 @@ def main() -> None:
         if args.impl == "reference":
             run_reference_arm(args, group)
         elif args.memory_bound:
-            run_memory_bound(args, group)
+            if group.rank == 0:
+                print(json.dumps(memory_bound(args.mb_batch, group.local_rank)), flush=True)
         else:
             run_gpu_arm(args, group)
     finally:

@@ -73,9 +73,15 @@ KERNEL_SPEC = struct.Struct("<IIHHHHHHQQII")
 QUANT_PARAM = struct.Struct("<IHHIQ")
 
 
+# Large packages take the runtime library's C loop for their checksum unless
+# this is False (then the pure-Python loop, as the reference compiler does;
+# a process that must not map the CUDA library sets it).
+NATIVE_FNV = True
+
+
 def fnv1a32(data: bytes | bytearray | memoryview) -> int:
     """FNV-1a 32-bit; uses the runtime library's C loop for large packages."""
-    if len(data) > (1 << 16):
+    if NATIVE_FNV and len(data) > (1 << 16):
         fn = _native_fnv()
         if fn is not None:
             buf = (ctypes.c_char * len(data)).from_buffer_copy(data) if isinstance(data, bytes) else \

@@ -66,6 +66,12 @@ def test_int8_resnet50_bs256_every_node_on_edge_images(gpu):
     spk = pipeline.compile_config("resnet50", 256, targets=("cuda_b200",), int8=True)["cuda_b200"]
     pkg = read_spk(spk)
     pick = np.array([0, 1, 254, 255])
+    # The oracle runs each node on the 4 picked images: the same network
+    # packaged at batch 4 (same weights, same calibration, same ids).
+    pkg4 = read_spk(pipeline.compile_config("resnet50", len(pick), targets=("cuda_b200",), int8=True)["cuda_b200"])
+    assert [n.op_type for n in pkg4.nodes] == [n.op_type for n in pkg.nodes]
+    for t, q in pkg.quant.items():
+        np.testing.assert_array_equal(np.asarray(pkg4.quant[t].scales), np.asarray(q.scales), err_msg=str(t))
     x = seeded_input((256, 3, 224, 224), seed=23)
     convs = [n for n in pkg.nodes if n.op_type == "Conv"]
     with Runtime(spk, device=0) as rt:
@@ -81,7 +87,7 @@ def test_int8_resnet50_bs256_every_node_on_edge_images(gpu):
     checked = 0
     for n in pkg.nodes:
         env = {t: gpu_t[t] for t in n.inputs if t in gpu_t}
-        want = harness.run_node(pkg, n, env)[0]
+        want = harness.run_node(pkg4, n, env)[0]
         got = gpu_t[n.outputs[0]]
         if n.id == convs[0].id:
             # fp32-math stem with an int8 output: one code where fp32
