@@ -740,15 +740,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) |
                                  (uint32_t(TILE_ROWS >> 4) << 24);
-      // One flat loop over this CTA's K steps (all its tiles and stream-K
-      // segments), with the stage, segment and group positions kept as
-      // counters: the issuing thread does as little as possible between its
-      // MMA batches.
+      // The CTA's K steps (all its tiles and stream-K segments) as runs of
+      // plain steps between accumulator hand-offs, with the stage, segment
+      // and group positions kept as counters: measured with in-kernel clock
+      // traces, every instruction the issuing thread executes between MMA
+      // batches leaves the tensor pipe idle, so the inner loop holds only
+      // the barrier test, the MMAs and the stage release.
       // Segment lengths only: whole tiles (nk steps), then this CTA's
       // stream-K share cut at tile boundaries (32-bit: units < 2^31).
       const Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
       const uint32_t total = wi.total_steps();
-      const int group = tp.group;
       const uint32_t nk = uint32_t(tp.num_kb);
       uint32_t dp_left = total - uint32_t(wi.u1 - wi.u0);  // steps of whole tiles
       uint32_t u = uint32_t(wi.u0);
@@ -756,11 +757,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       int seg_left = 0;  // K steps left in the current segment
       uint32_t gi = 0;            // accumulator hand-offs issued (one per K group)
       uint32_t ab = 0, abph = 0;  // accumulator buffer and its phase parity
-      uint32_t dtm = tmem;
       int gk = 0;              // K step within its group
       int s = 0;               // stage
       uint32_t ph = 0;         // stage phase parity
-      for (uint32_t it = 0; it < total; ++it) {
+      // Waits of this thread test the barrier first (one instruction when
+      // the phase completed long ago, the common case); a pair's barriers
+      // take the cluster-scope acquire.
+      auto wait_fast = [&](uint64_t *bar, uint32_t parity, int code) {
+        return PAIR ? mbar_wait_cluster(bar, parity, &abort_flag, status, code)
+                    : mbar_wait_fast(bar, parity, &abort_flag, status, code);
+      };
+      bool ok = true;
+      for (uint32_t it = 0; ok && it < total;) {
         if (seg_left == 0) {
           if (dp_left > 0) {
             seg_left = int(nk);
@@ -772,58 +780,74 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (gk == 0) {
-          if (!wait_any(&acce_bar[ab], abph ^ 1, 7)) break;
+          if (!wait_fast(&acce_bar[ab], abph ^ 1, 7)) break;
           tc_fence_after();
-          dtm = tmem + ab * uint32_t(BN);
         }
-        // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
-        // (or, in a pair, relayed) stage is signalled on full_bar, after the
-        // A warps saw raw_bar themselves.
-        if (!(AMODE != 1 && RELAY) && !mbar_wait(&raw_bar[s], ph, &abort_flag, status, 3)) break;
-        if (RELAY && !wait_any(&full_bar[s], ph, 3)) break;
-        tc_fence_after();
-        uint8_t *a_hi = smem + s * STAGE;
-        uint8_t *a_lo = a_hi + kABytes;
-        uint8_t *b_hi = a_hi + B_OFF;
-        uint8_t *b_lo = b_hi + B_BYTES;
-        const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
-        // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
-        // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
-        const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
-        const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t step = uint64_t(kk * 32) >> 4;                          // 8 tf32 = 32 bytes along K
-          const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
-          const uint32_t acc = (gk | kk) ? 1u : 0u;                              // first MMA of a group overwrites
-          if (PAIR) {
-            if (SPLIT3) {
-              mma_tf32_pair(dtm, dal + astep, dbh + step, idesc, acc);
-              mma_tf32_pair(dtm, dah + astep, dbl + step, idesc, 1u);
-              mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, 1u);
-            } else {
-              mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, acc);
-            }
-          } else if (ALO) {
-            // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
-            mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), dbh + step, idesc, acc);
-            mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
-            mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
-          } else if (SPLIT3) {
-            mma_tf32(dtm, dal + astep, dbh + step, idesc, acc);
-            mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
-            mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
-          } else {
-            mma_tf32(dtm, dah + astep, dbh + step, idesc, acc);
+        const uint32_t dtm = tmem + ab * uint32_t(BN);
+        // A run of K steps up to the next hand-off (end of the K group or of
+        // the segment): nothing but waits, MMAs and stage releases.
+        const int run = min(tp.group - gk, seg_left);
+        for (int r = 0; r < run; ++r) {
+          // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
+          // (or, in a pair, relayed) stage is signalled on full_bar, after
+          // the A warps saw raw_bar themselves.
+          if (!(AMODE != 1 && RELAY) && !mbar_wait_fast(&raw_bar[s], ph, &abort_flag, status, 3)) {
+            ok = false;
+            break;
           }
+          if (RELAY && !wait_fast(&full_bar[s], ph, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t *a_hi = smem + s * STAGE;
+          uint8_t *a_lo = a_hi + kABytes;
+          uint8_t *b_hi = a_hi + B_OFF;
+          uint8_t *b_lo = b_hi + B_BYTES;
+          const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
+          // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
+          // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
+          const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
+          const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
+          const int gstep = gk + r;  // the group's first K step overwrites the accumulator
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t step = uint64_t(kk * 32) >> 4;                          // 8 tf32 = 32 bytes along K
+            const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
+            const uint32_t acc = (gstep | kk) ? 1u : 0u;
+            if (PAIR) {
+              if (SPLIT3) {
+                mma_tf32_pair(dtm, dal + astep, dbh + step, idesc, acc);
+                mma_tf32_pair(dtm, dah + astep, dbl + step, idesc, 1u);
+                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, 1u);
+              } else {
+                mma_tf32_pair(dtm, dah + astep, dbh + step, idesc, acc);
+              }
+            } else if (ALO) {
+              // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
+              mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), dbh + step, idesc, acc);
+              mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
+              mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
+            } else if (SPLIT3) {
+              mma_tf32(dtm, dal + astep, dbh + step, idesc, acc);
+              mma_tf32(dtm, dah + astep, dbl + step, idesc, 1u);
+              mma_tf32(dtm, dah + astep, dbh + step, idesc, 1u);
+            } else {
+              mma_tf32(dtm, dah + astep, dbh + step, idesc, acc);
+            }
+          }
+          if (PAIR)
+            mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
+          else
+            mma_commit(&empty_bar[s]);
+          s = s + 1 == STAGES ? 0 : s + 1;
+          ph ^= s == 0 ? 1u : 0u;
         }
-        if (PAIR)
-          mma_commit_pair(&empty_bar[s]);  // frees the stage in both CTAs
-        else
-          mma_commit(&empty_bar[s]);
-        ++gk;
-        const bool seg_end = --seg_left == 0;
-        if (gk == group || seg_end) {
+        if (!ok) break;
+        it += uint32_t(run);
+        gk += run;
+        seg_left -= run;
+        if (gk == tp.group || seg_left == 0) {
           if (PAIR)
             mma_commit_pair(&accf_bar[ab]);
           else
@@ -834,10 +858,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             ab = 0;
             abph ^= 1u;
           }
-        }
-        if (++s == STAGES) {
-          s = 0;
-          ph ^= 1u;
         }
       }
       // Every issued MMA must finish before TMEM is freed (also on abort):

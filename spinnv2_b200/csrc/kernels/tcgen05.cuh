@@ -48,6 +48,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: true if the phase with this parity has completed.
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: false on timeout (after `limit` clock cycles; the first
 // role to give up records `code` in the status word) or when another role
 // already aborted.
@@ -68,6 +79,13 @@ __device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, 
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
                                           int code) {
   return mbar_wait_limit(bar, parity, abort_flag, status, code, kWaitCycles);
+}
+
+// The same bounded wait with a non-blocking test first: the common case of
+// a phase that completed long ago costs one instruction.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                               int code) {
+  return mbar_test(bar, parity) || mbar_wait_limit(bar, parity, abort_flag, status, code, kWaitCycles);
 }
 
 // Programmatic dependent launch: let the stream's next kernel begin
