@@ -161,6 +161,18 @@ typedef enum {
     SPKV2_LAYOUT_NHWC = 2
 } Spkv2Layout;
 
+/* KernelSpec weight_layout codes (the reference writes OIHW = 1 only).
+ * TC_PANEL_F32X2 (CUDA target): an fp32 conv weight stored as the tcgen05
+ * operand panel [2][Npad][Kpad] float, K-major rows with k = (r*KW + s)*C + c,
+ * Npad = Cout rounded up to 256, Kpad = K rounded up to 32, zero padding;
+ * part 0 = the weight rounded to TF32 (ties away from zero), part 1 = the
+ * exact remainder.  The tensor record keeps the logical OIHW shape and gives
+ * the stored byte size. */
+typedef enum {
+    SPKV2_WEIGHT_LAYOUT_OIHW = 1,
+    SPKV2_WEIGHT_LAYOUT_TC_PANEL_F32X2 = 2
+} Spkv2WeightLayout;
+
 /* 68-byte tensor record. */
 typedef struct {
     uint32_t id;

@@ -15,6 +15,16 @@ For the CUDA target (backend `delegate`) the tokens map to device kernels:
   other cuda           -> reference  (the op's CUDA kernel)
 CUDA specs carry layout NHWC (the device activation layout), need no SPK
 scratch, and have no fallback: the profile lists no `ref` token.
+
+Weight pre-packing (the reference format's weight_layout field,
+reference compiler/planner/kernel_spec.py:43, packager/spk_writer.py:35): a
+tensor-core fp32 conv whose weights the device reads as they are packed gets
+weight_layout TC_PANEL_F32X2 and the SPK writer stores its weights as the
+tcgen05 operand panel (see spk_writer.tc_panel), so prepare on the device is
+an upload with no repacking.  Eligible: fp32 weights, group 1, Cout >= 16,
+Cin a multiple of 4 above 4 (the device then keeps Cin as the GEMM channel
+count whatever the input layout; few-channel first convs are row-packed at
+prepare and keep OIHW).
 """
 
 from __future__ import annotations
@@ -39,6 +49,9 @@ KIND_TC_3XTF32 = "tc_3xtf32"
 KIND_TC_TF32 = "tc_tf32"
 KIND_TC_INT8 = "tc_int8"
 KIND_SIMT_FP32 = "simt_fp32"
+
+WEIGHT_LAYOUT_OIHW = "OIHW"
+WEIGHT_LAYOUT_TC_PANEL = "TC_PANEL_F32X2"
 
 SIMD_TILE_BYTES = 32 * 1024 * 1024  # cap of the CPU SIMD conv's working buffers
 SIMD_IM2COL_SEGMENT = 2 * 1024 * 1024
@@ -90,7 +103,7 @@ def select_kernel_specs(graph: Graph, profile: dict) -> KernelPlan:
         tokens = profile["ops"].get(node.op_type, [])
         if not tokens:
             raise ValueError(f"target profile does not support op: {node.op_type}")
-        chosen = _primary(graph, node, tokens)
+        chosen = _primary(graph, node, tokens, profile)
         ref_spec = _spec(graph, node, KIND_REFERENCE, BACKEND_REF)
         if chosen is None:
             if "ref" not in tokens:
@@ -115,9 +128,9 @@ def select_kernel_specs(graph: Graph, profile: dict) -> KernelPlan:
     return KernelPlan(specs, by_node, peak, fallbacks)
 
 
-def _primary(graph: Graph, node: Node, tokens: list[str]) -> KernelSpec | None:
+def _primary(graph: Graph, node: Node, tokens: list[str], profile: dict) -> KernelSpec | None:
     if any(t.startswith("cuda") for t in tokens):
-        return _primary_cuda(graph, node, tokens)
+        return _primary_cuda(graph, node, tokens, "TC_PANEL_F32X2" in profile.get("weight_layouts", []))
     if node.op_type == "Conv":
         if len(node.inputs) > 1:
             w = graph.tensors[node.inputs[1]]
@@ -139,7 +152,7 @@ def _primary(graph: Graph, node: Node, tokens: list[str]) -> KernelSpec | None:
     return None
 
 
-def _primary_cuda(graph: Graph, node: Node, tokens: list[str]) -> KernelSpec | None:
+def _primary_cuda(graph: Graph, node: Node, tokens: list[str], prepack: bool = False) -> KernelSpec | None:
     if node.op_type == "Conv":
         w = graph.tensors[node.inputs[1]]
         for tok in tokens:
@@ -148,13 +161,31 @@ def _primary_cuda(graph: Graph, node: Node, tokens: list[str]) -> KernelSpec | N
                 continue
             if (kind == KIND_TC_INT8) != (w.dtype == DTYPE_INT8):
                 continue
-            return _spec(graph, node, kind, BACKEND_DELEGATE, dtype=w.dtype, layout="NHWC")
+            spec = _spec(graph, node, kind, BACKEND_DELEGATE, dtype=w.dtype, layout="NHWC")
+            if prepack and tc_panel_eligible(graph, node, kind):
+                spec.weight_layout = WEIGHT_LAYOUT_TC_PANEL
+            return spec
         return None
     if node.op_type == "Gemm" and "cuda_direct" in tokens:
         return _spec(graph, node, KIND_DIRECT, BACKEND_DELEGATE, layout="NHWC")
     if "cuda" in tokens:
         return _spec(graph, node, KIND_REFERENCE, BACKEND_DELEGATE, layout="NHWC")
     return None
+
+
+def tc_panel_eligible(graph: Graph, node: Node, kind: str) -> bool:
+    """A Conv whose fp32 weights the tcgen05 kernels read in the panel layout
+    the SPK writer can produce ahead of time (see the module docstring)."""
+    if kind not in (KIND_TC_3XTF32, KIND_TC_TF32) or len(node.inputs) < 2:
+        return False
+    w = graph.tensors[node.inputs[1]]
+    if w.dtype != DTYPE_FP32 or len(w.shape) != 4 or w.data is None:
+        return False
+    if int(node.attrs.get("group", 1)) != 1:
+        return False
+    cout, cin = int(w.shape[0]), int(w.shape[1])
+    out = graph.tensors[node.outputs[0]] if node.outputs else None
+    return cout >= 16 and cin % 4 == 0 and cin > 4 and out is not None and out.dtype == DTYPE_FP32
 
 
 def _ints(value, length: int, default: int) -> list[int]:

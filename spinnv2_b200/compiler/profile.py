@@ -16,8 +16,10 @@ Bundled profiles (spinnv2_b200/compiler/profiles/*.json):
                    package the CPU baseline the reference runtime times
   cpu_ref_large    scalar reference kernels only (strict CPU oracle)
 
-The CUDA profile adds an optional "memory_plan" object (booleans) that
-switches off the planner's aliases whose meaning depends on NCHW byte order.
+The CUDA profile adds two optional fields: "memory_plan" (booleans) switches
+off the planner's aliases whose meaning depends on NCHW byte order, and
+"weight_layouts" lists the weight layouts its packages may store ("OIHW",
+"TC_PANEL_F32X2": tensor-core convs' weights pre-packed by the SPK writer).
 """
 
 from __future__ import annotations
@@ -52,6 +54,8 @@ TOP_FIELDS: dict[str, _Rule] = {
             "an object mapping op names to lists of kernel tokens"),
     "memory_plan": (False, lambda v: isinstance(v, dict) and all(isinstance(x, bool) for x in v.values()),
                     "an object of booleans"),
+    "weight_layouts": (False, lambda v: _str_list(v) and set(v) <= {"OIHW", "TC_PANEL_F32X2"},
+                       'a list of weight layouts ("OIHW", "TC_PANEL_F32X2")'),
 }
 MEMORY_FIELDS: dict[str, _Rule] = {
     "activation_arena_max": (True, lambda v: _is_int(v) and v >= 0, "an integer >= 0"),

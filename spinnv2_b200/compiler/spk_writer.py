@@ -20,6 +20,8 @@ import json
 import struct
 from pathlib import Path
 
+import numpy as np
+
 from .ir import DTYPE_FP16, DTYPE_FP32, DTYPE_INT8, DTYPE_INT32, ROLE_ACTIVATION, ROLE_CONSTANT, ROLE_INPUT, \
     ROLE_OUTPUT, ROLE_WEIGHT, Graph, Node
 from .kernel_spec import KernelPlan, KernelSpec, select_kernel_specs
@@ -43,7 +45,40 @@ SECTION_PROTECTION_PLAN = 13
 
 DTYPE_CODES = {DTYPE_FP32: 1, DTYPE_INT8: 2, DTYPE_FP16: 3, DTYPE_INT32: 4}
 LAYOUT_CODES = {"NCHW": 1, "NHWC": 2}
-WEIGHT_LAYOUT_CODES = {"OIHW": 1}
+WEIGHT_LAYOUT_CODES = {"OIHW": 1, "TC_PANEL_F32X2": 2}
+TC_PANEL_N_ALIGN = 256  # panel rows padded for every tile width the device may pick (32..256)
+TC_PANEL_K_ALIGN = 32   # one K step of the fp32 tcgen05 kernels
+
+
+def tc_panel(w: np.ndarray) -> np.ndarray:
+    """fp32 OIHW conv weights [M, C, KH, KW] -> the tcgen05 operand panel
+    [2][Npad][Kpad] (K-major rows, k = (r * KW + s) * C + c, zero padding;
+    Npad = M rounded up to 256, Kpad = K rounded up to 32).  Part 0 is each
+    weight rounded to TF32 (10 mantissa bits, to nearest, ties away from
+    zero), part 1 the remainder w - part0, exact in fp32, so part0 + part1
+    == w bit for bit and the 3xTF32 kernels read both parts as stored."""
+    m, c, kh, kw = w.shape
+    k = c * kh * kw
+    npad = -(-m // TC_PANEL_N_ALIGN) * TC_PANEL_N_ALIGN
+    kpad = -(-k // TC_PANEL_K_ALIGN) * TC_PANEL_K_ALIGN
+    wk = np.ascontiguousarray(np.asarray(w, dtype=np.float32).transpose(0, 2, 3, 1)).reshape(m, k)
+    bits = wk.view(np.uint32)
+    finite = (bits & np.uint32(0x7F800000)) != np.uint32(0x7F800000)
+    hi_bits = np.where(finite, (bits + np.uint32(0x1000)) & np.uint32(0xFFFFE000), bits)
+    hi = hi_bits.view(np.float32)
+    lo = (wk - hi).astype(np.float32)
+    panel = np.zeros((2, npad, kpad), dtype=np.float32)
+    panel[0, :m, :k] = hi
+    panel[1, :m, :k] = lo
+    return panel
+
+
+def tc_panel_to_oihw(panel: np.ndarray, shape) -> np.ndarray:
+    """Inverse of tc_panel: the OIHW weights (part0 + part1, exact)."""
+    m, c, kh, kw = (int(d) for d in shape)
+    k = c * kh * kw
+    wk = (panel[0, :m, :k] + panel[1, :m, :k]).astype(np.float32)
+    return np.ascontiguousarray(wk.reshape(m, kh, kw, c).transpose(0, 3, 1, 2))
 BACKEND_CODES = {"ref": 1, "cpu": 2, "simd": 3, "delegate": 4}
 KERNEL_KIND_CODES = {
     "reference": 1, "direct": 2, "im2col_gemm": 3, "packed_gemm": 4, "pointwise_1x1": 5,
@@ -161,8 +196,16 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
             name_off[t.name] = len(strings)
             strings.extend(t.name.encode("utf-8") + b"\x00")
 
+    # Weights the kernel plan asks for pre-packed (weight_layout) are stored
+    # in that layout; their records keep the logical shape and give the
+    # stored byte size.
+    panel_of = {}
+    for n in graph.nodes:
+        if kernel_plan.by_node[n.id].weight_layout == "TC_PANEL_F32X2":
+            panel_of[n.inputs[1]] = True
     weights = bytearray()
     weight_off: dict[int, int] = {}
+    weight_size: dict[int, int] = {}
     for t in graph.tensors:
         if t.role != ROLE_WEIGHT:
             continue
@@ -170,7 +213,9 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
             raise ValueError(f"weight tensor missing data: {t.name}")
         weights.extend(b"\x00" * (_align(len(weights), 16) - len(weights)))
         weight_off[t.id] = len(weights)
-        weights.extend(t.data)
+        blob = tc_panel(t.array()).tobytes() if t.id in panel_of else t.data
+        weight_size[t.id] = len(blob)
+        weights.extend(blob)
 
     attrs = bytearray()
     attr_off: dict[int, tuple[int, int]] = {}
@@ -185,7 +230,8 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
         e = memory_plan.entries[t.id]
         tensors.extend(TENSOR.pack(t.id, DTYPE_CODES[t.dtype], ROLE_CODES[t.role], len(t.shape),
                                    MEMORY_CLASS_CODES[e.memory_class], *(t.shape[:8] + [1] * (8 - len(t.shape))),
-                                   t.size_bytes, weight_off.get(t.id, e.offset), name_off[t.name], 0))
+                                   weight_size.get(t.id, t.size_bytes), weight_off.get(t.id, e.offset),
+                                   name_off[t.name], 0))
     nodes = bytearray()
     for n in graph.nodes:
         spec = kernel_plan.by_node[n.id]
@@ -240,7 +286,7 @@ def build_spk(graph: Graph, profile: dict, *, memory_plan: MemoryPlan | None = N
         offset += len(data)
     header = HEADER.pack(SPKV2_MAGIC, VERSION_MAJOR, VERSION_MINOR, 0, HEADER.size, len(sections), 0,
                          len(graph.tensors), len(graph.nodes), len(graph.inputs), len(graph.outputs),
-                         sum(t.size_bytes for t in graph.tensors if t.role == ROLE_WEIGHT),
+                         sum(weight_size.values()),
                          memory_plan.planned_activation_bytes, kernel_plan.scratch_arena_bytes + prot_scratch,
                          fnv1a32(json.dumps(profile, sort_keys=True).encode("utf-8")), 1)
     package = bytearray(header + directory + payload)

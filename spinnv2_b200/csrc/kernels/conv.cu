@@ -475,33 +475,65 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   }
   p->math = math;
 
+  // Weights the compiler stored pre-packed (weight_layout TC_PANEL_F32X2):
+  // the tensor-core path reads them in place; the CUDA-core path unpacks
+  // them to OIHW first.
+  const bool prepacked = spec && spec->weight_layout == SPKV2_WEIGHT_LAYOUT_TC_PANEL_F32X2;
+  const int panel_npad = int(ceil_div(g.M, 256) * 256), panel_kpad = int(ceil_div(g.K, 32) * 32);
+  if (prepacked && (dw != SPKV2_DTYPE_FP32 || g.groups != 1 ||
+                    uint64_t(wr->size_bytes) != uint64_t(2) * panel_npad * panel_kpad * sizeof(float))) {
+    delete p;
+    return -2;  // the record's size does not match the panel of its shape
+  }
+  const void *w_oihw = tw.data;  // OIHW weights for the packers below
+  float *w_unpacked = nullptr;
+
   // Tensor-core path first; the CUDA-core kernel takes every shape it
   // declines (and every conv in FP32 math mode).
   if (math != SPKV2_CUDA_MATH_FP32) {
     const void *r_dev = g.has_res ? ctx->tensors[node->inputs[3]].data : nullptr;
     rc = int_acc ? conv_tc_i8_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream)
-                 : conv_tc_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream);
+         : prepacked ? conv_tc_prepare_ex(*p, nullptr, tx.data, ty.data, false, ctx->stream, r_dev,
+                                          reinterpret_cast<const float *>(tw.data), panel_npad)
+                     : conv_tc_prepare(*p, tw.data, tx.data, ty.data, r_dev, ctx->stream);
     if (rc == 0 && !int_acc) rc = conv_tc_attach(ctx, *p);
     if (rc != 0 && rc != SPKV2_ERR_UNSUPPORTED) {
       delete p;
       return rc;
     }
   }
+  if (!p->w_tc && prepacked) {
+    w_unpacked = static_cast<float *>(device_alloc(size_t(g.M) * g.K * sizeof(float)));
+    if (!w_unpacked || (rc = conv_unpack_panel(w_unpacked, reinterpret_cast<const float *>(tw.data), g, panel_npad,
+                                               panel_kpad, ctx->stream))) {
+      device_free(w_unpacked);
+      delete p;
+      return w_unpacked ? rc : SPKV2_ERR_DEVICE_ALLOC;
+    }
+    w_oihw = w_unpacked;
+  }
   if (!p->w_tc) {
     const size_t esz = int_acc ? 1 : 4;
     p->w_simt = device_alloc(size_t(g.M) * g.K * esz);
     if (!p->w_simt) {
+      device_free(w_unpacked);
       delete p;
       return SPKV2_ERR_DEVICE_ALLOC;
     }
     const int64_t total = int64_t(g.M) * g.K;
     if (esz == 1)
       pack_simt_kernel<int8_t><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
-          static_cast<int8_t *>(p->w_simt), reinterpret_cast<const int8_t *>(tw.data), g);
+          static_cast<int8_t *>(p->w_simt), reinterpret_cast<const int8_t *>(w_oihw), g);
     else
       pack_simt_kernel<float><<<grid_for(total, 256), 256, 0, ctx->stream>>>(
-          static_cast<float *>(p->w_simt), reinterpret_cast<const float *>(tw.data), g);
-    if ((rc = cuda_status(cudaGetLastError()))) {
+          static_cast<float *>(p->w_simt), reinterpret_cast<const float *>(w_oihw), g);
+    rc = cuda_status(cudaGetLastError());
+    if (w_unpacked) {  // the pack above reads it: free it once that finished
+      const int src = cuda_status(cudaStreamSynchronize(ctx->stream));
+      device_free(w_unpacked);
+      rc = rc ? rc : src;
+    }
+    if (rc) {
       delete p;
       return rc;
     }

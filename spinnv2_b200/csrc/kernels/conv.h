@@ -62,6 +62,7 @@ struct ConvPlan : NodePlan {
   int math = 0;            // SPKV2_CUDA_MATH_* actually used
   void *w_simt = nullptr;  // [groups][K][Mg] packed weights (fp32 or int8)
   void *w_tc = nullptr;    // tcgen05 operand panels (see conv_tc.cu)
+  bool w_tc_borrowed = false;  // w_tc points into the device weight section (pre-packed SPK panel)
   int32_t *bias_q = nullptr;  // int32 requantisation bias (kConvI8)
   float *scale_m = nullptr;   // per-channel requant multiplier M[c] (kConvI8)
   const float *bias_f = nullptr;  // fp32 bias (device weights)
@@ -83,7 +84,7 @@ struct ConvPlan : NodePlan {
     device_free(w8_cs);
     if (tc_state) tc_i8 ? conv_tc_i8_release(tc_state) : conv_tc_release(tc_state);
     device_free(w_simt);
-    device_free(w_tc);
+    if (!w_tc_borrowed) device_free(w_tc);
     device_free(bias_q);
     device_free(scale_m);
   }
@@ -96,8 +97,15 @@ int conv_simt_launch(const ConvPlan &p, const void *x, void *y, const void *res,
 int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, const void *r_dev,
                     cudaStream_t s);
 // w_kn: the weights are a [K][Cout] matrix (Gemm B, transB = 0), not OIHW.
+// panel / panel_npad: the weights already stored as the tcgen05 panel
+// (SPK weight_layout TC_PANEL_F32X2, Npad rows per part); used in place when
+// the conv keeps its channel count as the GEMM K order's (no row packing,
+// no channel padding), else SPKV2_ERR_UNSUPPORTED.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
-                       cudaStream_t s, const void *r_dev = nullptr);
+                       cudaStream_t s, const void *r_dev = nullptr, const float *panel = nullptr,
+                       int panel_npad = 0);
+// TC_PANEL_F32X2 panel -> OIHW fp32 (w = part0 + part1, exact), on `s`.
+int conv_unpack_panel(float *oihw, const float *panel, const ConvGeo &g, int npad, int kpad, cudaStream_t s);
 // sk_ws: the context's stream-K workspace (conv_tc_attach sized it); may be
 // null for plans that do not use stream-K.
 int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, int *status, cudaStream_t s,

@@ -73,9 +73,9 @@ constexpr int kStagingBytes = kEpiWarps * 4096;  // epilogue: one 32x32 fp32 til
 struct TcParams {
   ConvGeo g;       // GEMM-side geometry (C may be the padded channel count)
   int Kpad;        // K rounded up to a multiple of 32
-  int Npad;        // Cout rounded up to a multiple of BN
+  int Npad;        // rows per weight-panel part (Cout rounded up to a multiple of BN, or the stored panel's)
   int num_kb;      // Kpad / 32
-  int n_tiles;     // Npad / BN
+  int n_tiles;     // ceil(Cout / BN)
   int64_t tiles;   // m_tiles * n_tiles
   int group;       // K steps per TMEM partial when promoting (3xTF32)
   int out_i8;      // quantise the output: y = clamp(rne(act(v) * (1 / s_y)), -128, 127)
@@ -83,6 +83,7 @@ struct TcParams {
   int64_t dp_tiles;  // tiles walked whole, round-robin over the CTAs (all tiles without stream-K)
   int64_t sk_units;  // stream-K: K steps of tiles dp_tiles.. spread evenly over CTAs 0..sk_ctas-1 (0: off)
   int sk_ctas;       // CTAs sharing the stream-K units (fewer CTAs: fewer segments per tile to add up)
+  int sk_park_all;   // split-K: every segment parks its partial; conv_tc_reduce_kernel finishes all tiles
 };
 
 // One unit of a CTA's work: K steps [kb0, kb1) of output tile `tile`.  A
@@ -232,8 +233,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = BROWS * 128;
   constexpr bool ALO = alo_tmem(BN, SPLIT3, AMODE, PAIR);
   constexpr int STAGE = stage_bytes(BROWS, SPLIT3, ALO);
-  // Stream-K tails exist only in single-CTA 3xTF32 kernels.
-  constexpr bool SK = SPLIT3 && !PAIR;
+  // Stream-K (a tail past the last full wave, or split-K over all tiles)
+  // exists in single-CTA kernels.
+  constexpr bool SK = !PAIR;
   using Iter = WorkIter<SK>;
   constexpr int B_OFF = (SPLIT3 && !ALO ? 2 : 1) * kABytes;  // B hi within a stage
   // The A warps hand the stage to the MMA (full_bar) whenever they touch it:
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       bool finish = true;
       int64_t blo = 0;
-      if (SK && sg.nseg > 1) {
+      if (SK && (sg.nseg > 1 || tp.sk_park_all)) {
         // Stream-K segment: park this warp's part of the tile in the CTA's
         // workspace slot ([chunk][4-column group][row] float4s, so a warp's
         // stores are contiguous) and count the arrival; the segment's last
@@ -526,12 +528,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = col0; cb < col0 + ncol; cb += 32) {
           uint32_t acc[32];
           read_acc(cb, acc);
+          if (pv) {  // rows past the last pixel are never read back
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            __stcg(&mine[((cb >> 5) * 8 + q) * 128 + row],
-                   make_float4(__uint_as_float(acc[4 * q]), __uint_as_float(acc[4 * q + 1]),
-                               __uint_as_float(acc[4 * q + 2]), __uint_as_float(acc[4 * q + 3])));
+            for (int q = 0; q < 8; ++q)
+              __stcg(&mine[((cb >> 5) * 8 + q) * 128 + row],
+                     make_float4(__uint_as_float(acc[4 * q]), __uint_as_float(acc[4 * q + 1]),
+                                 __uint_as_float(acc[4 * q + 2]), __uint_as_float(acc[4 * q + 3])));
+          }
         }
+        if (tp.sk_park_all) continue;  // the reduce kernel finishes every tile
         __threadfence();
         __syncwarp();
         int last = 0;
@@ -884,6 +889,87 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- split-K
+// Finishes a split-K launch (sk_park_all): every CTA parked the partial sums
+// of its K range of one or two tiles in its two workspace slots
+// ([chunk][4-column group][row] float4s).  Per output element the tile's
+// segments are added in segment order (CTA order, so the result does not
+// depend on which CTA finished first), then bias, residual and activation
+// are applied as in the conv epilogue: y = act((sum + b) + r).  One thread
+// per (tile row, 4 output channels); consecutive threads take consecutive
+// rows, so the workspace reads are coalesced 16-byte loads.
+template <int BN>
+__global__ void __launch_bounds__(256) conv_tc_reduce_kernel(const float4 *__restrict__ ws,
+                                                             const float *__restrict__ bias,
+                                                             const float *__restrict__ res, float *__restrict__ y,
+                                                             TcParams tp) {
+  pdl_launch_dependents();
+  pdl_wait();  // the conv launch's partials are complete and visible
+  const ConvGeo &g = tp.g;
+  const int64_t U = tp.sk_units;
+  const int64_t G = tp.sk_ctas;
+  const int64_t nk = tp.num_kb;
+  constexpr int kGroups = BN / 4;
+  const int64_t total = tp.tiles * kBM * kGroups;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int row = int(i % kBM);
+    const int64_t rest = i / kBM;
+    const int cg = int(rest % kGroups);
+    const int64_t tt = rest / kGroups;
+    const int64_t p = (tt / tp.n_tiles) * kBM + row;
+    const int c0 = int(tt % tp.n_tiles) * BN + cg * 4;
+    if (p >= g.P || c0 >= g.M) continue;
+    // CTAs whose shares hold the tile's first and last K steps (the
+    // WorkIter owner / start arithmetic).
+    const int64_t v0 = tt * nk, v1 = v0 + nk - 1;
+    const int64_t blo = ((v0 + 1) * G - 1) / U, bhi = ((v1 + 1) * G - 1) / U;
+    const int64_t idx = int64_t(((cg >> 3) * 8 + (cg & 7)) * 128 + row);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Sixteen segments' loads in flight at a time, added in segment order.
+    for (int64_t j0 = blo; j0 <= bhi; j0 += 16) {
+      float4 f[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int64_t j = j0 + k;
+        const int slot = j * U / G >= v0 ? 0 : 1;
+        f[k] = j <= bhi ? __ldcg(&ws[(j * 2 + slot) * (BN * 32) + idx]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        if (j0 + k <= bhi) {
+          a.x += f[k].x;
+          a.y += f[k].y;
+          a.z += f[k].z;
+          a.w += f[k].w;
+        }
+      }
+    }
+    const int ow = int(p % g.OW);
+    const int64_t q = p / g.OW;
+    const int oh = int(q % g.OH), n = int(q / g.OH);
+    const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
+    const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
+    float v[4] = {a.x, a.y, a.z, a.w};
+    const int cn = g.M - c0 < 4 ? g.M - c0 : 4;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (e < cn) {
+        const int c = c0 + e;
+        if (g.has_bias) v[e] += __ldg(bias + c);
+        if (g.has_res) v[e] += __ldg(res + rbase + int64_t(c) * g.rs[1]);
+        v[e] = apply_act(v[e], g.act);
+      }
+    }
+    if (cn == 4 && g.ys[1] == 1 && ((ybase + c0) & 3) == 0) {
+      *reinterpret_cast<float4 *>(y + ybase + c0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < cn) y[ybase + int64_t(c0 + e) * g.ys[1]] = v[e];
+    }
+  }
+}
+
 // ---------------------------------------------------------------- weights
 // [part][Npad][Kpad] with k = (r*KW + s)*Cg + c over the GEMM channel count
 // Cg (which may be padded above the weight's Cw); part 0 = TF32(rna) of w,
@@ -909,6 +995,20 @@ __global__ void pack_tc_kernel(float *__restrict__ dst, const float *__restrict_
     const float hi = tf32_rna(v);
     dst[i] = hi;
     if (split3) dst[total + i] = v - hi;
+  }
+}
+
+// TC_PANEL_F32X2 panel [2][npad][kpad] (k = (r*KW + s)*C + c) -> OIHW
+// weights, w = part0 + part1 (exact: part1 is the fp32 remainder).
+__global__ void unpack_panel_kernel(float *__restrict__ oihw, const float *__restrict__ panel, ConvGeo g, int npad,
+                                    int kpad) {
+  const int64_t total = int64_t(g.M) * g.K;
+  const int64_t part = int64_t(npad) * kpad;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int m = int(i / g.K), rem = int(i % g.K);  // OIHW order: rem = (c*KH + r)*KW + s
+    const int sx = rem % g.KW, r = (rem / g.KW) % g.KH, c = rem / (g.KW * g.KH);
+    const int64_t k = (int64_t(r) * g.KW + sx) * g.Cg + c;
+    oihw[i] = panel[int64_t(m) * kpad + k] + panel[part + int64_t(m) * kpad + k];
   }
 }
 
@@ -1077,7 +1177,7 @@ int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, co
 
 // Eligible: fp32 in and out, group 1, Cout >= 16, 3xTF32 or TF32 math.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
-                       cudaStream_t s, const void *r_dev) {
+                       cudaStream_t s, const void *r_dev, const float *panel, int panel_npad) {
   const ConvGeo &g0 = p.g;
   if ((p.mode != kConvF32 && p.mode != kConvF32ToI8) || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
@@ -1132,6 +1232,11 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     x_dev = st->staged_x;
     p.launches = 2;
   }
+  if (panel && (st->packed_rows || g.Cg != g0.Cg || w_kn)) {
+    // The stored panel's K order is over the original channels.
+    delete st;
+    return SPKV2_ERR_UNSUPPORTED;
+  }
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
   // A operand: tiled TMA for 1x1 stride-1 convs, im2col TMA for other
   // square convs with C % 32 == 0, cp.async gathers otherwise.
@@ -1170,15 +1275,40 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
       bn = pbn;
     }
   }
+  // Split-K over every tile (small batches): when the tiles fill at most
+  // half of the SMs, G CTAs (up to one per SM, at least two K steps each)
+  // take even shares of all tiles' K steps, park their partial sums, and
+  // conv_tc_reduce_kernel adds each tile's segments in order and finishes
+  // it, in parallel over the whole tile instead of one CTA per tile.  The
+  // widest tile that Cout fills (fewer partial sums to add).
+  int ska_g = 0;
+  if (!st->pair && p.mode == kConvF32 && !getenv("SPKV2_TC_NO_STREAMK") && !getenv("SPKV2_TC_NO_SPLITK")) {
+    const int wide = st->split3 ? 128 : 256;
+    int bw = 32;
+    while (bw < wide && bw < g.M) bw *= 2;
+    const int64_t t = ceil_div(g.P, kBM) * ceil_div(g.M, bw);
+    const int64_t units = t * ceil_div(g.K, kBK);
+    // At least `min_steps` K steps per CTA (SPKV2_TC_SPLITK_MIN_STEPS, default
+    // 4): fewer CTAs mean fewer partial sums to add up.  Measured on
+    // ResNet-101 bs1 (p50 through spkv2_run): 2 -> 1.61 ms, 4 -> 1.57 ms,
+    // 8 -> 1.60 ms; without split-K 1.67 ms.
+    int min_steps = 4;
+    if (const char *e = getenv("SPKV2_TC_SPLITK_MIN_STEPS")) min_steps = std::max(1, atoi(e));
+    const int64_t gsk = std::min<int64_t>(sms, units / min_steps);
+    if (2 * t <= sms && gsk >= 2 * t) {
+      bn = bw;
+      ska_g = int(gsk);
+    }
+  }
   st->bn = bn;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   st->epi_tma = p.mode == kConvF32 && nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
   tp.g = g;
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);
-  tp.Npad = int(ceil_div(g.M, bn) * bn);
+  tp.Npad = panel ? panel_npad : int(ceil_div(g.M, bn) * bn);  // rows per panel part
   tp.num_kb = tp.Kpad / kBK;
-  tp.n_tiles = tp.Npad / bn;
+  tp.n_tiles = int(ceil_div(g.M, bn));
   tp.tiles = ceil_div(g.P, st->pair ? 2 * kBM : kBM) * tp.n_tiles;  // pair tiles have 256 rows
   // 3xTF32 promotes every `group` K steps; TF32 hands off once per tile.
   tp.out_i8 = p.mode == kConvF32ToI8 ? 1 : 0;
@@ -1196,15 +1326,18 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     if (const char *e = getenv("SPKV2_TC_PROMOTE_GROUP")) tp.group = std::max(1, atoi(e));
   }
   st->grid = st->pair ? 2 * int(std::min<int64_t>(tp.tiles, sms / 2)) : int(std::min<int64_t>(tp.tiles, sms));
-  const int parts = st->split3 ? 2 : 1;
-  float *wtc = static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));
+  // A pre-packed panel always holds both parts (TF32 reads part 0 only).
+  const int parts = panel ? 2 : st->split3 ? 2 : 1;
+  float *wtc = panel ? const_cast<float *>(panel)
+                     : static_cast<float *>(device_alloc(size_t(parts) * tp.Npad * tp.Kpad * sizeof(float)));
   if (!wtc) {
     delete st;
     return SPKV2_ERR_DEVICE_ALLOC;
   }
-  pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
-      wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0,
-      st->packed_rows ? g0.KW : 0);
+  if (!panel)
+    pack_tc_kernel<<<grid_for(int64_t(tp.Npad) * tp.Kpad, 256), 256, 0, s>>>(
+        wtc, static_cast<const float *>(w_raw_dev), g, g0.Cg, tp.Npad, tp.Kpad, st->split3 ? 1 : 0, w_kn ? 1 : 0,
+        st->packed_rows ? g0.KW : 0);
   int rc = cuda_status(cudaGetLastError());
   bool ok = rc == 0 && encode_2d(&st->wmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wtc, uint64_t(tp.Kpad),
                                  uint64_t(parts) * tp.Npad, uint64_t(tp.Kpad), uint32_t(st->pair ? bn / 2 : bn));
@@ -1219,7 +1352,16 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   tp.dp_tiles = tp.tiles;
   tp.sk_units = 0;
   tp.sk_ctas = sms;
-  if (ok && st->split3 && !st->pair && !getenv("SPKV2_TC_NO_STREAMK")) {
+  tp.sk_park_all = 0;
+  if (ok && ska_g > 0) {
+    tp.dp_tiles = 0;
+    tp.sk_units = tp.tiles * tp.num_kb;
+    tp.sk_ctas = ska_g;
+    tp.sk_park_all = 1;
+    st->grid = ska_g;
+    st->sk_ws_bytes = size_t(ska_g) * 2 * size_t(bn) * kBM * sizeof(float);
+    p.launches += 1;  // conv_tc_reduce_kernel
+  } else if (ok && st->split3 && !st->pair && !getenv("SPKV2_TC_NO_STREAMK")) {
     // Critical path in K steps: whole rounds, then the CTA's share of the
     // tail, then the fix-up, which adds up the tile's segments (about
     // Gs / tail + 1 of them) one L2 round trip per segment and 32-column
@@ -1259,12 +1401,13 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   st->amap_base = x_dev;
   st->ymap_base = y_dev;
   if (!ok) {
-    device_free(wtc);
+    if (!panel) device_free(wtc);
     delete st;
     return rc ? rc : SPKV2_ERR_UNSUPPORTED;
   }
   st->smem = smem_bytes(bn, st->split3, st->amode, st->pair);
   p.w_tc = wtc;
+  p.w_tc_borrowed = panel != nullptr;
   p.tc_state = st;
   p.tc_block_n = bn;
   p.tc_kpad = tp.Kpad;
@@ -1273,15 +1416,20 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   st->set_attr_only = false;
   if (rc) return rc;
   p.variant = std::string(st->split3 ? "tc_3xtf32" : "tc_tf32") + (st->pair ? "_pair" : "") +
-              (tp.sk_units ? "_sk" : "") + "_bn" + std::to_string(bn) +
+              (tp.sk_park_all ? "_splitk" : tp.sk_units ? "_sk" : "") + "_bn" + std::to_string(bn) +
               (st->amode == 4 ? "_im2col4" : st->amode == 3 ? "_im2col" : st->amode == 2 ? "_tma" : "_cpasync") + (st->epi_tma ? "_tmastore" : "") +
-              (st->packed_rows ? "_rowpack" : st->staged_x ? "_relayout" : "");
+              (st->packed_rows ? "_rowpack" : st->staged_x ? "_relayout" : "") + (panel ? "_prepacked" : "");
   return 0;
 }
 
 int conv_tc_prepare(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, const void *r_dev,
                     cudaStream_t s) {
   return conv_tc_prepare_ex(p, w_raw_dev, x_dev, y_dev, false, s, r_dev);
+}
+
+int conv_unpack_panel(float *oihw, const float *panel, const ConvGeo &g, int npad, int kpad, cudaStream_t s) {
+  unpack_panel_kernel<<<grid_for(int64_t(g.M) * g.K, 256), 256, 0, s>>>(oihw, panel, g, npad, kpad);
+  return cuda_status(cudaGetLastError());
 }
 
 void conv_tc_release(void *state) { delete static_cast<TcState *>(state); }
@@ -1328,18 +1476,31 @@ int conv_tc_launch(const ConvPlan &p, const void *x, void *y, const void *res, i
     if (st.epi_tma && yf != st.ymap_base && !encode_y(st, &mp.y, yf)) return SPKV2_ERR_UNSUPPORTED;
     if (st.tp.res_tma && rf != st.rmap_base && !encode_y(st, &mp.r, rf)) return SPKV2_ERR_UNSUPPORTED;
   }
+  int rc = 0;
   if (st.split3) {
     switch (st.bn) {
-      case 32: return launch_modes<32, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
-      case 64: return launch_modes<64, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
-      default: return launch_modes<128, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+      case 32: rc = launch_modes<32, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+      case 64: rc = launch_modes<64, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+      default: rc = launch_modes<128, true>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+    }
+  } else {
+    switch (st.bn) {
+      case 32: rc = launch_modes<32, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+      case 64: rc = launch_modes<64, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+      case 256: rc = launch_modes<256, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
+      default: rc = launch_modes<128, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s); break;
     }
   }
+  if (rc || !st.tp.sk_park_all || st.set_attr_only) return rc;
+  // Split-K: add the parked segments and finish every tile.
+  const float4 *ws = reinterpret_cast<const float4 *>(sk_ws);
+  const int64_t threads = st.tp.tiles * kBM * (st.bn / 4);
+  const unsigned blocks = unsigned(std::min<int64_t>(ceil_div(threads, 256), 148LL * 8));
   switch (st.bn) {
-    case 32: return launch_modes<32, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
-    case 64: return launch_modes<64, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
-    case 256: return launch_modes<256, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
-    default: return launch_modes<128, false>(st, mp, xf, yf, bias, rf, sk_ws, status, s);
+    case 32: return cuda_status(launch_kernel(conv_tc_reduce_kernel<32>, blocks, 256, 0, s, 1, ws, bias, rf, yf, st.tp));
+    case 64: return cuda_status(launch_kernel(conv_tc_reduce_kernel<64>, blocks, 256, 0, s, 1, ws, bias, rf, yf, st.tp));
+    case 256: return cuda_status(launch_kernel(conv_tc_reduce_kernel<256>, blocks, 256, 0, s, 1, ws, bias, rf, yf, st.tp));
+    default: return cuda_status(launch_kernel(conv_tc_reduce_kernel<128>, blocks, 256, 0, s, 1, ws, bias, rf, yf, st.tp));
   }
 }
 

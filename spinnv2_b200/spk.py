@@ -9,6 +9,7 @@ oracle harness.
 
 from __future__ import annotations
 
+import functools
 import json
 import struct
 from dataclasses import dataclass, field
@@ -87,6 +88,7 @@ class SpkKernelSpec:
     layout: int
     scratch_bytes: int
     fallback: int
+    weight_layout: int = 1  # 1 OIHW, 2 the tcgen05 panel (spk_writer.tc_panel)
 
 
 @dataclass
@@ -122,9 +124,24 @@ class SpkPackage:
             return [self.tensors[i] for i in order]
         return outs
 
+    @functools.cached_property
+    def panel_weights(self) -> frozenset[int]:
+        """Ids of the weight tensors stored pre-packed as tcgen05 panels."""
+        return frozenset(n.inputs[1] for n in self.nodes
+                if n.op_type == "Conv" and n.kernel_spec_id < len(self.specs)
+                         and self.specs[n.kernel_spec_id].weight_layout == 2)
+
     def weight(self, tid: int) -> np.ndarray:
+        """A weight tensor in its logical (OIHW / row-major) layout; panels
+        written pre-packed are unpacked (exactly: part0 + part1 == w)."""
         t = self.tensors[tid]
         buf = self.weights[t.data_offset:t.data_offset + t.size_bytes]
+        if tid in self.panel_weights:
+            m, c, kh, kw = t.shape
+            npad = -(-m // W.TC_PANEL_N_ALIGN) * W.TC_PANEL_N_ALIGN
+            kpad = -(-(c * kh * kw) // W.TC_PANEL_K_ALIGN) * W.TC_PANEL_K_ALIGN
+            panel = np.frombuffer(buf, dtype=np.float32).reshape(2, npad, kpad)
+            return W.tc_panel_to_oihw(panel, t.shape)
         return np.frombuffer(buf, dtype=t.np_dtype).reshape(t.shape)
 
 
@@ -180,7 +197,7 @@ def read_spk(src: str | Path | bytes) -> SpkPackage:
     for i in range(len(ks) // W.KERNEL_SPEC.size):
         f = W.KERNEL_SPEC.unpack_from(ks, i * W.KERNEL_SPEC.size)
         specs.append(SpkKernelSpec(f[0], f[1], KIND_NAMES.get(f[2], str(f[2])), BACKEND_NAMES.get(f[3], str(f[3])),
-                                   f[4], f[5], f[9], f[10]))
+                                   f[4], f[5], f[9], f[10], f[6]))
     quant: dict[int, SpkQuant] = {}
     qs = sec(W.SECTION_QUANTIZATION)
     if len(qs) >= W.QUANT_PARAM.size:
