@@ -103,3 +103,4 @@ def test_reference_generated_c_on_the_cuda_library(gpu, tmp_path, binary):
     ref = np.fromfile(tmp_path / "out_ref.bin", dtype=np.float32)
     assert out.size == ref.size == 10
     np.testing.assert_allclose(out, ref, atol=ATOL, rtol=RTOL)
+
