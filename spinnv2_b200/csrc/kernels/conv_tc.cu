@@ -792,36 +792,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A run of K steps up to the next hand-off (end of the K group or of
         // the segment): nothing but waits, MMAs and stage releases.
         const int run = min(tp.group - gk, seg_left);
-        int ready = 0;  // steps of this run known to have landed
         for (int r = 0; r < run; ++r) {
           // B (and, in AMODE 2/3/4, A) lands by TMA on raw_bar; a converted
           // (or, in a pair, relayed) stage is signalled on full_bar, after
-          // the A warps saw raw_bar themselves.  The A warps arrive on the
-          // stages in order, so a completed full_bar of the next step implies
-          // this one's: one wait covers two steps.
-          if (RELAY && !PAIR) {
-            if (r >= ready) {
-              const bool two = r + 1 < run;
-              const int s2 = two ? (s + 1 == STAGES ? 0 : s + 1) : s;
-              const uint32_t ph2 = two && s2 == 0 ? ph ^ 1u : ph;
-              if (!wait_fast(&full_bar[s2], ph2, 3)) {
-                ok = false;
-                break;
-              }
-              ready = r + (two ? 2 : 1);
-              tc_fence_after();
-            }
-          } else {
-            if (!(AMODE != 1 && RELAY) && !mbar_wait_fast(&raw_bar[s], ph, &abort_flag, status, 3)) {
-              ok = false;
-              break;
-            }
-            if (RELAY && !wait_fast(&full_bar[s], ph, 3)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+          // the A warps saw raw_bar themselves.  (AMODE 1: the A warps gather
+          // A and do not see raw_bar, so both are waited on here.)
+          if (!(AMODE != 1 && RELAY) && !mbar_wait_fast(&raw_bar[s], ph, &abort_flag, status, 3)) {
+            ok = false;
+            break;
           }
+          if (RELAY && !wait_fast(&full_bar[s], ph, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           uint8_t *a_hi = smem + s * STAGE;
           uint8_t *a_lo = a_hi + kABytes;
           uint8_t *b_hi = a_hi + B_OFF;
