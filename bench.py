@@ -184,7 +184,7 @@ def node_bytes(pkg, ids, skip_weights: bool = False) -> int:
 # from DRAM).  traffic_step = ratio x the step's algorithmic conv bytes.
 # Keyed by conv math; each entry names its capture.
 CONV_TRAFFIC_RATIO = {
-    "3xtf32": (0.70, "the layer-3 3x3 (0.58) and 1x1 (0.83) convs of ResNet-101 bs64, each captured as a single "
+    "3xtf32": (0.74, "the layer-3 3x3 (0.63) and 1x1 (0.85) convs of ResNet-101 bs64, each captured as a single "
                      "launch of the sweep configs conv3x3_256_14 / conv1x1_1024_256_14 at batch 64 "
                      "(profiles/conv_tc_layer3_bs64.md)"),
     "tf32": (None, "not captured"),
