@@ -1176,11 +1176,13 @@ int launch_modes(const TcState &st, const Maps &mp, const float *x, float *y, co
 
 }  // namespace
 
-// Eligible: fp32 in and out, group 1, Cout >= 16, 3xTF32 or TF32 math.
+// Eligible: fp32 in and out, group 1, 3xTF32 or TF32 math.  Narrow outputs
+// (Cout < 32, e.g. a detector's 4-channel box head) run in one 32-column
+// tile with direct stores.
 int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, const void *y_dev, bool w_kn,
                        cudaStream_t s, const void *r_dev, const float *panel, int panel_npad) {
   const ConvGeo &g0 = p.g;
-  if ((p.mode != kConvF32 && p.mode != kConvF32ToI8) || g0.groups != 1 || g0.M < 16) return SPKV2_ERR_UNSUPPORTED;
+  if ((p.mode != kConvF32 && p.mode != kConvF32ToI8) || g0.groups != 1 || g0.M < 1) return SPKV2_ERR_UNSUPPORTED;
   if (p.math != SPKV2_CUDA_MATH_3XTF32 && p.math != SPKV2_CUDA_MATH_TF32) return SPKV2_ERR_UNSUPPORTED;
   if (!encode_fn()) return SPKV2_ERR_UNSUPPORTED;
   TcState *st = new TcState();
@@ -1192,7 +1194,11 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   ConvGeo g = g0;
   const bool nhwc_in = g.xs[1] == 1 && g.xs[3] == g.C && g.xs[2] == int64_t(g.W) * g.C;
   const bool aligned_in = reinterpret_cast<uintptr_t>(x_dev) % 16 == 0;
-  const bool row_pack = !(nhwc_in && g.C % 4 == 0 && aligned_in) && g.C <= 4 && 4 * g.KW <= 32 &&
+  // Row packing pays for wide filters (a 7x7 first conv: ResNet-50 INT8 bs256
+  // 55.5k img/s packed vs 46.2k re-laid out); a 3x3 first conv is faster
+  // re-laid out to 4 channels and read by 4-channel im2col TMA (detector bs64
+  // 4215 vs 4083 img/s).
+  const bool row_pack = !(nhwc_in && g.C % 4 == 0 && aligned_in) && g.C <= 4 && 4 * g.KW <= 32 && g.KW >= 5 &&
                         encode_im2col_fn() && !getenv("SPKV2_TC_NO_ROWPACK");
   if (row_pack) {
     // Few-channel input: pack each filter row's KW x 4 channels into one
@@ -1303,7 +1309,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   }
   st->bn = bn;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
-  st->epi_tma = p.mode == kConvF32 && nhwc_out && g.M % 4 == 0 && reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
+  st->epi_tma = p.mode == kConvF32 && nhwc_out && g.M % 4 == 0 && g.M >= 32 &&
+                reinterpret_cast<uintptr_t>(y_dev) % 16 == 0;
   TcParams &tp = st->tp;
   tp.g = g;
   tp.Kpad = int(ceil_div(g.K, kBK) * kBK);

@@ -258,6 +258,28 @@ def test_split_k_with_residual_and_relu_matches_reference(gpu):
     np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("cout,k", [(4, 1), (10, 3), (17, 3)])
+@pytest.mark.parametrize("batch", [2, 64])
+def test_narrow_output_convs_on_tensor_cores_match_reference(gpu, cout, k, batch):
+    """Convs with fewer than 32 output channels (the detector's 4-channel box
+    head) run in one 32-column tensor-core tile with direct stores."""
+    import copy
+
+    from spinnv2_b200.compiler import builders, pipeline
+
+    net = builders._Net(f"narrow_{cout}_{k}", 7)
+    x_id = net.b.input("input", [batch, 64, 20, 20])
+    net.b.mark_output(net.conv(x_id, cout, k, s=1, p=k // 2, bias=True, act="Relu" if k == 3 else None))
+    graph = pipeline.fuse(net.b.graph)
+    spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+    spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+    x = seeded_input((batch, 64, 20, 20), seed=8)
+    ref = reference_outputs(spk_cpu, [x])[0]
+    out, variants = _run_gpu(spk_gpu, [x])
+    assert any(v.startswith("Conv:tc_3xtf32") for v in variants), variants
+    np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+
+
 @pytest.mark.parametrize("widths", [(8, 12, 4), (6, 10), (16, 16, 16, 16)])
 def test_split_and_concat_match_reference(gpu, widths):
     """Channel Split and Concat between convs (NHWC on the device): 16-byte
