@@ -62,15 +62,33 @@ __global__ void elt_fast_kernel(float *__restrict__ y, const float *__restrict__
                      (b ? reinterpret_cast<uintptr_t>(b) : 0)) & 15) == 0;
   int64_t start = 0;
   if (vec) {
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += stride) {
-      float4 va = reinterpret_cast<const float4 *>(a)[i];
-      float4 vb = b ? reinterpret_cast<const float4 *>(b)[i] : make_float4(0, 0, 0, 0);
-      float4 r;
-      r.x = elt_apply(op, va.x, vb.x, act, alpha, lo, hi);
-      r.y = elt_apply(op, va.y, vb.y, act, alpha, lo, hi);
-      r.z = elt_apply(op, va.z, vb.z, act, alpha, lo, hi);
-      r.w = elt_apply(op, va.w, vb.w, act, alpha, lo, hi);
-      reinterpret_cast<float4 *>(y)[i] = r;
+    // Four float4s per thread per pass, all loads issued before any math:
+    // a unary op (one input stream) otherwise keeps only one 16-byte load
+    // in flight per thread, too few to cover HBM latency.
+    constexpr int U = 4;
+    const float4 *a4 = reinterpret_cast<const float4 *>(a);
+    const float4 *b4 = reinterpret_cast<const float4 *>(b);
+    float4 *y4 = reinterpret_cast<float4 *>(y);
+    for (int64_t i0 = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i0 < n4; i0 += U * stride) {
+      float4 va[U], vb[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = i0 + u * stride;
+        va[u] = i < n4 ? __ldg(a4 + i) : make_float4(0, 0, 0, 0);
+        vb[u] = b && i < n4 ? __ldg(b4 + i) : make_float4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < n4) {
+          float4 r;
+          r.x = elt_apply(op, va[u].x, vb[u].x, act, alpha, lo, hi);
+          r.y = elt_apply(op, va[u].y, vb[u].y, act, alpha, lo, hi);
+          r.z = elt_apply(op, va[u].z, vb[u].z, act, alpha, lo, hi);
+          r.w = elt_apply(op, va[u].w, vb[u].w, act, alpha, lo, hi);
+          y4[i] = r;
+        }
+      }
     }
     start = n4 * 4;
   }
@@ -176,10 +194,87 @@ __global__ void __launch_bounds__(256) transpose_hw_c_kernel(T *__restrict__ dst
   }
 }
 
+// 4-byte elements with C % 4 == 0, P % 4 == 0 and 16-byte aligned tensors:
+// 16-byte accesses on both sides.  A block moves a tile of 32 channels x 128
+// positions (16 KB) through shared memory held channel-major, tile[c][p];
+// the NHWC side moves 4 channels of one position per float4 (a warp covers
+// 4 positions x 32 channels, four 128-byte rows), the [N, C, P] side 4
+// positions of one channel per float4 (a warp covers one 512-byte channel
+// run).  The position quads of channel row c are stored XOR-swizzled by
+// (c / 4) % 8, so the scalar side's 32 lanes (8 channel quads x 4
+// positions) hit 32 distinct banks and the float4 side still reads or
+// writes whole 16-byte groups.  Four float4s per thread, loads first.
+constexpr int kTrP4 = 128;
+
+__device__ __forceinline__ int tr_col(int c, int p) { return ((((p >> 2) ^ ((c >> 2) & 7))) << 2) | (p & 3); }
+
+__global__ void __launch_bounds__(256) transpose_hw_c_vec_kernel(float *__restrict__ dst, const float *__restrict__ src,
+                                                                 int64_t P, int64_t C, int to_nchw) {
+  __shared__ __align__(16) float tile[32][kTrP4];
+  const int t = threadIdx.x;
+  const int64_t n = blockIdx.z;
+  const int64_t p0 = int64_t(blockIdx.x) * kTrP4, c0 = int64_t(blockIdx.y) * 32;
+  float4 v[4];
+  if (to_nchw) {  // src [N,P,C] -> dst [N,C,P]
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, pl = f >> 3, cq = f & 7;
+      const bool in = p0 + pl < P && c0 + 4 * cq < C;
+      v[i] = in ? __ldg(reinterpret_cast<const float4 *>(src + (n * P + p0 + pl) * C + c0 + 4 * cq))
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, pl = f >> 3, c = 4 * (f & 7);
+      tile[c][tr_col(c, pl)] = v[i].x;
+      tile[c + 1][tr_col(c + 1, pl)] = v[i].y;
+      tile[c + 2][tr_col(c + 2, pl)] = v[i].z;
+      tile[c + 3][tr_col(c + 3, pl)] = v[i].w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, c = f >> 5, q = f & 31;
+      if (c0 + c < C && p0 + 4 * q < P)
+        *reinterpret_cast<float4 *>(dst + (n * C + c0 + c) * P + p0 + 4 * q) =
+            *reinterpret_cast<const float4 *>(&tile[c][tr_col(c, 4 * q)]);
+    }
+  } else {  // src [N,C,P] -> dst [N,P,C]
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, c = f >> 5, q = f & 31;
+      const bool in = c0 + c < C && p0 + 4 * q < P;
+      v[i] = in ? __ldg(reinterpret_cast<const float4 *>(src + (n * C + c0 + c) * P + p0 + 4 * q))
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, c = f >> 5, q = f & 31;
+      *reinterpret_cast<float4 *>(&tile[c][tr_col(c, 4 * q)]) = v[i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int f = t + 256 * i, pl = f >> 3, c = 4 * (f & 7);
+      if (p0 + pl < P && c0 + c < C)
+        *reinterpret_cast<float4 *>(dst + (n * P + p0 + pl) * C + c0 + c) =
+            make_float4(tile[c][tr_col(c, pl)], tile[c + 1][tr_col(c + 1, pl)], tile[c + 2][tr_col(c + 2, pl)],
+                        tile[c + 3][tr_col(c + 3, pl)]);
+    }
+  }
+}
+
 template <typename T>
 int launch_transpose_hw_c(T *dst, const T *src, const Spkv2TensorRecord *r, int to_nchw, cudaStream_t s) {
   const int64_t N = r->shape[0], C = r->shape[1], P = int64_t(r->shape[2]) * r->shape[3];
   if (N > 65535 || ceil_div(C, 32) > 65535) return SPKV2_ERR_UNSUPPORTED;
+  if (sizeof(T) == 4 && C % 4 == 0 && P % 4 == 0 &&
+      ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0) {
+    dim3 grid(unsigned(ceil_div(P, kTrP4)), unsigned(ceil_div(C, 32)), unsigned(N));
+    transpose_hw_c_vec_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<float *>(dst), reinterpret_cast<const float *>(src),
+                                                   P, C, to_nchw);
+    return cuda_status(cudaGetLastError());
+  }
   dim3 grid(unsigned(ceil_div(P, kTransP)), unsigned(ceil_div(C, 32)), unsigned(N));
   transpose_hw_c_kernel<T><<<grid, dim3(32, 8), 0, s>>>(dst, src, N, P, C, to_nchw);
   return cuda_status(cudaGetLastError());
@@ -267,8 +362,8 @@ int eltwise_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *scratch) {
   }
   const int threads = 256;
   if (p->fast) {
-    elt_fast_kernel<<<grid_for(ceil_div(p->count, 4), threads), threads, 0, ctx->stream>>>(y, a, b, p->count, p->op,
-                                                                                             p->act, p->alpha, lo, hi);
+    elt_fast_kernel<<<grid_for(ceil_div(p->count, 16), threads), threads, 0, ctx->stream>>>(y, a, b, p->count, p->op,
+                                                                                              p->act, p->alpha, lo, hi);
   } else {
     elt_strided_kernel<<<grid_for(p->count, threads), threads, 0, ctx->stream>>>(y, a, b, p->it, p->count, p->op,
                                                                                   p->act, p->alpha, lo, hi);

@@ -397,6 +397,22 @@ inline bool encode_im2col_nhwc2(CUtensorMap *map, CUtensorMapDataType dtype, uin
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// im2col map of a dense NHWC tensor with explicit window-origin corners
+// (lower[0] / upper[0] along W, [1] along H: origins run from lower to
+// dim - 1 + upper) and traversal strides sw x sh.
+inline bool encode_im2col_corners(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
+                                  int N, int H, int W, int C, const int lower[2], const int upper[2], int sw, int sh,
+                                  uint32_t channels, uint32_t pixels, CUtensorMapSwizzle swizzle) {
+  if (!encode_im2col_fn()) return false;
+  const cuuint64_t dims[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(N)};
+  const cuuint64_t strides[3] = {cuuint64_t(C) * elem_bytes, cuuint64_t(W) * C * elem_bytes,
+                                 cuuint64_t(H) * W * C * elem_bytes};
+  const cuuint32_t estr[4] = {1, cuuint32_t(sw), cuuint32_t(sh), 1};
+  return encode_im2col_fn()(map, dtype, 4, const_cast<void *>(base), dims, strides, lower, upper, channels, pixels,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool encode_im2col_nhwc(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void *base,
                                int N, int H, int W, int C, int k, int s, int p, int d, uint32_t channels,
                                uint32_t pixels, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {

@@ -62,41 +62,53 @@ struct PartPlan : NodePlan {
   uint32_t seg[kMaxParts + 1] = {};
 };
 
-// Segmented row copy of 16-byte vectors (32-bit indices; the plan checks the
-// sizes): vector v of the big tensor is in outer row v / row_vecs, at column
-// c = v % row_vecs, which part k holds at column c - seg[k] of its own row of
-// seg[k+1] - seg[k] vectors.  Four grid-strided vectors per thread per
-// iteration keep four independent 16-byte loads in flight.
-struct RowSegs {
-  FastDiv row_vecs;
-  uint32_t seg[kMaxParts + 1];  // in vectors
-  int parts;
+// Dense row copy of 16-byte vectors, part-major: blockIdx.y selects part k
+// (uniform per block, so its row width, offset and pointer are read once),
+// and the part is walked in its own contiguous order.  Vector v of part k
+// is at row v / w_k, column v % w_k of its rows of w_k vectors; in the big
+// tensor it sits at row * W + off_k + column.  One division per vector and
+// no search over the parts; each block moves kRowsPerBlock vectors of one
+// part, four 16-byte loads in flight per thread (blocks past a smaller
+// part's end exit at once).  32-bit indices: the plan checks the sizes.
+struct PartRows {
+  uint32_t W;                   // big row width, vectors
+  uint32_t off[kMaxParts];      // part k's column offset in a big row
+  uint32_t n[kMaxParts];        // vectors of part k
+  FastDiv w[kMaxParts];         // part k's row width
   void *ptr[kMaxParts];
 };
 
+constexpr int kRowsThreads = 256, kRowsUnroll = 4, kRowsIters = 4;
+constexpr uint32_t kRowsPerBlock = kRowsThreads * kRowsUnroll * kRowsIters;
+
 template <bool GATHER>
-__global__ void __launch_bounds__(256) rows_kernel(uint4 *__restrict__ big, RowSegs r, uint32_t total) {
-  constexpr int U = 4;
-  const uint32_t stride = gridDim.x * blockDim.x;
-  for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < total; v0 += U * stride) {
-    uint4 *src[U], *dst[U];
-    uint4 val[U];
+__global__ void __launch_bounds__(kRowsThreads) rows_kernel(uint4 *__restrict__ big, PartRows r) {
+  const int k = blockIdx.y;
+  const uint32_t n = r.n[k];
+  const uint32_t base = blockIdx.x * kRowsPerBlock;
+  if (base >= n) return;
+  const FastDiv w = r.w[k];
+  const uint32_t off = r.off[k], W = r.W;
+  uint4 *part = static_cast<uint4 *>(r.ptr[k]);
+#pragma unroll 1
+  for (int it = 0; it < kRowsIters; ++it) {
+    const uint32_t v0 = base + uint32_t(it * kRowsUnroll * kRowsThreads) + threadIdx.x;
+    uint4 val[kRowsUnroll];
+    uint4 *dst[kRowsUnroll];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint32_t v = v0 + u * stride;
-      const uint32_t vv = v < total ? v : v0;  // lanes past the end redo v0 (same value, same place)
-      const uint32_t row = r.row_vecs.div(vv), c = vv - row * r.row_vecs.d;
-      int k = 0;
-#pragma unroll
-      for (int j = 1; j < kMaxParts; ++j) k += (j < r.parts && c >= r.seg[j]) ? 1 : 0;
-      uint4 *part = static_cast<uint4 *>(r.ptr[k]) + size_t(row) * (r.seg[k + 1] - r.seg[k]) + (c - r.seg[k]);
-      src[u] = GATHER ? part : big + vv;
-      dst[u] = GATHER ? big + vv : part;
+    for (int u = 0; u < kRowsUnroll; ++u) {
+      const uint32_t v = v0 + uint32_t(u * kRowsThreads);
+      dst[u] = nullptr;
+      if (v < n) {
+        const uint32_t row = w.div(v);
+        uint4 *b = big + (size_t(row) * W + off + (v - row * w.d));
+        val[u] = GATHER ? __ldg(part + v) : __ldg(b);
+        dst[u] = GATHER ? b : part + v;
+      }
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) val[u] = *src[u];
-#pragma unroll
-    for (int u = 0; u < U; ++u) *dst[u] = val[u];
+    for (int u = 0; u < kRowsUnroll; ++u)
+      if (dst[u]) *dst[u] = val[u];
   }
 }
 
@@ -243,15 +255,21 @@ int run_parts(Spkv2Context *ctx, const Spkv2NodeRecord *node) {
   for (int k = 0; k < d.parts; ++k) d.ptr[k] = ctx->tensors[GATHER ? node->inputs[k] : node->outputs[k]].data;
   void *big = ctx->tensors[GATHER ? node->outputs[0] : node->inputs[0]].data;
   if (p->rows_path) {
-    RowSegs r;
+    PartRows r;
     memset(&r, 0, sizeof(r));
-    r.parts = d.parts;
-    r.row_vecs = FastDiv(p->seg[d.parts]);
-    for (int k = 0; k <= d.parts; ++k) r.seg[k] = p->seg[k];
-    for (int k = 0; k < d.parts; ++k) r.ptr[k] = d.ptr[k];
-    const uint32_t total = p->rows * r.row_vecs.d;
-    if (total == 0) return 0;
-    rows_kernel<GATHER><<<grid_for(total, 256), 256, 0, ctx->stream>>>(static_cast<uint4 *>(big), r, total);
+    r.W = p->seg[d.parts];
+    uint32_t most = 0;
+    for (int k = 0; k < d.parts; ++k) {
+      const uint32_t wk = p->seg[k + 1] - p->seg[k];
+      r.off[k] = p->seg[k];
+      r.w[k] = FastDiv(wk);
+      r.n[k] = p->rows * wk;
+      r.ptr[k] = d.ptr[k];
+      most = std::max(most, r.n[k]);
+    }
+    if (most == 0) return 0;
+    const dim3 grid(unsigned((most + kRowsPerBlock - 1) / kRowsPerBlock), unsigned(d.parts));
+    rows_kernel<GATHER><<<grid, kRowsThreads, 0, ctx->stream>>>(static_cast<uint4 *>(big), r);
     return cuda_status(cudaGetLastError());
   }
   const int g = grid_for(p->total, 256);

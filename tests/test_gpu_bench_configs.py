@@ -33,8 +33,10 @@ def _report(name: str, got: np.ndarray, want: np.ndarray) -> None:
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
     i = int(np.argmax(err))
     rel = err / np.maximum(np.abs(want.astype(np.float64)), 1e-30)
+    used = err / (ATOL + RTOL * np.abs(want.astype(np.float64)))
     print(f"{name}: worst abs {err.flat[i]:.3e} at ref {want.flat[i]:.4g}; worst rel {rel.max():.3e}; "
-          f"|ref| max {np.abs(want).max():.4g}; allowed at worst abs {ATOL + RTOL * abs(want.flat[i]):.3e}")
+          f"|ref| max {np.abs(want).max():.4g}; allowed at worst abs {ATOL + RTOL * abs(want.flat[i]):.3e}; "
+          f"largest share of the tolerance used {used.max():.3f}")
 
 
 @pytest.mark.parametrize("batch", [64, 256])

@@ -280,6 +280,52 @@ def test_narrow_output_convs_on_tensor_cores_match_reference(gpu, cout, k, batch
     np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
 
 
+@pytest.mark.parametrize("cin,k,pad,hw,cout,batch", [
+    (3, 7, 3, (224, 224), 64, 2),  # ResNet stem
+    (3, 7, 3, (31, 29), 64, 3),    # odd extents: the last s2d row / column is half padding
+    (3, 3, 1, (64, 64), 16, 2),    # detector stem
+    (3, 3, 1, (33, 17), 32, 1),
+    (1, 5, 2, (28, 28), 20, 2),    # even padding: taps start at the sub-pixel 0
+    (4, 4, 1, (20, 22), 64, 2),    # even kernel
+    (2, 3, 0, (15, 15), 40, 2),    # no padding
+])
+@pytest.mark.parametrize("math", ["spec", "tf32"])
+def test_stride2_few_channel_convs_space_to_depth_match_reference(gpu, cin, k, pad, hw, cout, batch, math):
+    """Stride-2 convs over <= 4 channels (a network's first conv) run as a
+    stride-1 conv over the 2 x 2 space-to-depth input (16 channels, two-tap
+    im2col TMA): against the reference, and in TF32 mode against the row-packed
+    / re-laid-out path (SPKV2_TC_NO_S2D) on the same package."""
+    import copy
+    import os
+
+    from spinnv2_b200.compiler import builders, pipeline
+    from spinnv2_b200.runtime import MATH_SPEC, MATH_TF32
+
+    net = builders._Net(f"s2d_{cin}_{k}_{pad}", 9)
+    shape = [batch, cin, hw[0], hw[1]]
+    x_id = net.b.input("input", shape)
+    net.b.mark_output(net.conv(x_id, cout, k, s=2, p=pad, bias=True, act="Relu"))
+    graph = pipeline.fuse(net.b.graph)
+    spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+    x = seeded_input(tuple(shape), seed=12)
+    mode = MATH_TF32 if math == "tf32" else MATH_SPEC
+    out, variants = _run_gpu(spk_gpu, [x], math_mode=mode)
+    assert any("_s2d" in v and "_im2col2tap" in v for v in variants), variants
+    if math == "spec":
+        spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+        ref = reference_outputs(spk_cpu, [x])[0]
+        np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+    else:
+        os.environ["SPKV2_TC_NO_S2D"] = "1"
+        try:
+            base, base_variants = _run_gpu(spk_gpu, [x], math_mode=mode)
+        finally:
+            del os.environ["SPKV2_TC_NO_S2D"]
+        assert not any("_s2d" in v for v in base_variants), base_variants
+        # Same TF32 products, different summation order.
+        np.testing.assert_allclose(out[0], base[0], atol=2e-3, rtol=2e-3)
+
+
 @pytest.mark.parametrize("widths", [(8, 12, 4), (6, 10), (16, 16, 16, 16)])
 def test_split_and_concat_match_reference(gpu, widths):
     """Channel Split and Concat between convs (NHWC on the device): 16-byte
