@@ -830,36 +830,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
           const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
           const int gstep = gk + r;  // the group's first K step overwrites the accumulator
+          // Operand descriptors of K slice kk (8 tf32 = 32 bytes along K).
+          // AMODE 4: two 2 KB core-matrix columns per slice; AMODE 5: slices
+          // 0-1 in the first 64-byte-swizzled half (tap 2kb), 2-3 in the
+          // second (tap 2kb + 1).
+          auto a_desc = [&](uint8_t *base, uint64_t d, int kk) -> uint64_t {
+            return AMODE == 5   ? smem_desc_sw64(base + (kk >> 1) * (kABytes / 2)) + uint64_t((kk & 1) * 2)
+                   : AMODE == 4 ? d + (uint64_t(kk * 4096) >> 4)
+                                : d + (uint64_t(kk * 32) >> 4);
+          };
+          // 3xTF32 issues the step's 12 MMAs pass by pass (A_lo*B_hi over the
+          // four K slices, then A_hi*B_lo, then A_hi*B_hi), so consecutive
+          // MMAs read different K slices.  Measured with a probe kernel on
+          // the B200 (148 CTAs, one issuing thread each): 1259 cycles per
+          // step when the three MMAs of one slice are issued back to back,
+          // 937 cycles pass by pass (768 ideal).
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t step = uint64_t(kk * 32) >> 4;                          // 8 tf32 = 32 bytes along K
-            const uint64_t astep = AMODE == 4 ? uint64_t(kk * 4096) >> 4 : step;  // two 2 KB columns
-            // AMODE 5: K slices 0-1 in the first 64-byte-swizzled half (tap
-            // 2kb), 2-3 in the second (tap 2kb + 1).
-            const uint64_t ah = AMODE == 5 ? smem_desc_sw64(a_hi + (kk >> 1) * (kABytes / 2)) + uint64_t((kk & 1) * 2)
-                                           : dah + astep;
-            const uint64_t al = AMODE == 5 ? smem_desc_sw64(a_lo + (kk >> 1) * (kABytes / 2)) + uint64_t((kk & 1) * 2)
-                                           : dal + astep;
-            const uint32_t acc = (gstep | kk) ? 1u : 0u;
-            if (PAIR) {
-              if (SPLIT3) {
-                mma_tf32_pair(dtm, al, dbh + step, idesc, acc);
-                mma_tf32_pair(dtm, ah, dbl + step, idesc, 1u);
-                mma_tf32_pair(dtm, ah, dbh + step, idesc, 1u);
+          for (int pass = 0; pass < (SPLIT3 ? 3 : 1); ++pass) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bstep = uint64_t(kk * 32) >> 4;
+              const uint64_t db = (SPLIT3 && pass == 1 ? dbl : dbh) + bstep;
+              const uint32_t acc = (pass | gstep | kk) ? 1u : 0u;
+              if (SPLIT3 && pass == 0 && ALO) {
+                // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
+                mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), db, idesc, acc);
               } else {
-                mma_tf32_pair(dtm, ah, dbh + step, idesc, acc);
+                const uint64_t da = SPLIT3 && pass == 0 ? a_desc(a_lo, dal, kk) : a_desc(a_hi, dah, kk);
+                if (PAIR)
+                  mma_tf32_pair(dtm, da, db, idesc, acc);
+                else
+                  mma_tf32(dtm, da, db, idesc, acc);
               }
-            } else if (ALO) {
-              // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
-              mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), dbh + step, idesc, acc);
-              mma_tf32(dtm, ah, dbl + step, idesc, 1u);
-              mma_tf32(dtm, ah, dbh + step, idesc, 1u);
-            } else if (SPLIT3) {
-              mma_tf32(dtm, al, dbh + step, idesc, acc);
-              mma_tf32(dtm, ah, dbl + step, idesc, 1u);
-              mma_tf32(dtm, ah, dbh + step, idesc, 1u);
-            } else {
-              mma_tf32(dtm, ah, dbh + step, idesc, acc);
             }
           }
           if (PAIR)
