@@ -84,7 +84,40 @@ struct TcParams {
   int64_t sk_units;  // stream-K: K steps of tiles dp_tiles.. spread evenly over CTAs 0..sk_ctas-1 (0: off)
   int sk_ctas;       // CTAs sharing the stream-K units (fewer CTAs: fewer segments per tile to add up)
   int sk_park_all;   // split-K: every segment parks its partial; conv_tc_reduce_kernel finishes all tiles
+  int p32;           // output pixel count < 2^31: pixel coordinates by 32-bit multiply-shift divisions
+  FastDiv ow_div, oh_div;
 };
+
+// Epilogue activation over a register array (one branch per call).  SiLU
+// as v / (1 + e^-v) with the fast exponential and divide intrinsics: a few
+// ulp from the correctly rounded quotient, far inside the fp32 output
+// tolerance, and a third of the instructions of expf and an IEEE divide.
+template <int N>
+__device__ __forceinline__ void epi_act(float (&v)[N], int act) {
+  if (act == 1) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+  } else if (act == 2) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = __fdividef(v[j], 1.0f + __expf(-v[j]));
+  }
+}
+
+// Output pixel p -> (n, oh, ow).
+__device__ __forceinline__ void pixel_nhw(const TcParams &tp, int64_t p, int &n, int &oh, int &ow) {
+  if (tp.p32) {
+    const uint32_t q = tp.ow_div.div(uint32_t(p));
+    ow = int(uint32_t(p) - q * uint32_t(tp.g.OW));
+    const uint32_t r = tp.oh_div.div(q);
+    oh = int(q - r * uint32_t(tp.g.OH));
+    n = int(r);
+  } else {
+    ow = int(p % tp.g.OW);
+    const int64_t q = p / tp.g.OW;
+    oh = int(q % tp.g.OH);
+    n = int(q / tp.g.OH);
+  }
+}
 
 // One unit of a CTA's work: K steps [kb0, kb1) of output tile `tile`.  A
 // stream-K tile whose K steps are spread over several CTAs has nseg > 1
@@ -344,12 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t p = m0 + row;
       const bool pv = p < g.P;
       int n = 0, oh = 0, ow = 0;
-      if (pv) {
-        ow = int(p % g.OW);
-        const int64_t q = p / g.OW;
-        oh = int(q % g.OH);
-        n = int(q / g.OH);
-      }
+      if (pv) pixel_nhw(tp, p, n, oh, ow);
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
       if (g.has_res && pv && rvec) {
@@ -408,12 +436,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             vals[j + 2] = __uint_as_float(acc[j + 2]) + b.z + rr.z;
             vals[j + 3] = __uint_as_float(acc[j + 3]) + b.w + rr.w;
           }
-        } else if (cn == 32 && (!g.has_res || rvec)) {
+        } else if ((cn & 3) == 0 && (!g.has_res || rvec)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const float4 b = g.has_bias ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j)) : make_float4(0, 0, 0, 0);
-            const float4 rr = (g.has_res && pv) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
-                                                : make_float4(0, 0, 0, 0);
+            const bool in = j < cn;  // a narrow tile's padding columns load nothing
+            const float4 b = g.has_bias && in ? __ldg(reinterpret_cast<const float4 *>(bias + c0 + j))
+                                              : make_float4(0, 0, 0, 0);
+            const float4 rr = (g.has_res && pv && in) ? __ldg(reinterpret_cast<const float4 *>(res + rbase + c0 + j))
+                                                      : make_float4(0, 0, 0, 0);
             vals[j] = __uint_as_float(acc[j]) + b.x + rr.x;
             vals[j + 1] = __uint_as_float(acc[j + 1]) + b.y + rr.y;
             vals[j + 2] = __uint_as_float(acc[j + 2]) + b.z + rr.z;
@@ -431,7 +461,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             vals[j] = v;
           }
         }
-        apply_act32(vals, g.act);  // one uniform branch per chunk
+        // Activation, one uniform branch per chunk; a narrow tile's padding
+        // columns (cn <= 16) are skipped.
+        if (cn > 16) {
+          epi_act<32>(vals, g.act);
+        } else {
+          epi_act<16>(reinterpret_cast<float(&)[16]>(vals), g.act);
+        }
         if (tp.out_i8) {
           // fp32 conv with an int8 output (the first conv of an INT8 network).
           if (!pv) return;
@@ -468,11 +504,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0 && m0 + quarter * 32 < g.P) tma_store_2d(&ymap, c0, int(m0 + quarter * 32), buf);
           ++sc;
         } else if (pv) {
-          if (cn == 32 && g.ys[1] == 1 && (g.M % 4) == 0) {
+          if (g.ys[1] == 1 && (g.M % 4) == 0 && (cn & 3) == 0) {
+            // NHWC rows of 4-aligned channel counts: 16-byte stores (a
+            // narrow tile stores only its cn real columns).
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4 *>(y + ybase + c0 + j) =
-                  make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
+              if (j < cn)
+                *reinterpret_cast<float4 *>(y + ybase + c0 + j) =
+                    make_float4(vals[j], vals[j + 1], vals[j + 2], vals[j + 3]);
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -687,11 +726,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int brow = n0 + int(rank) * BROWS;  // first weight row this CTA loads
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
         if (AMODE == 3 || AMODE == 4 || AMODE == 5) {
-          const int ow = int(m0 % g.OW);
-          const int64_t q = m0 / g.OW;
+          int ow, oh;
+          pixel_nhw(tp, m0, bn, oh, ow);
           bw = ow * g.sw - g.pw;
-          bh = int(q % g.OH) * g.sh - g.ph;
-          bn = int(q / g.OH);
+          bh = oh * g.sh - g.ph;
         }
         // AMODE 3 position of K step kb (C % 32 == 0: one filter tap per K
         // step), advanced incrementally so no division sits between the
@@ -1161,7 +1199,6 @@ struct TcState {
   float *staged_x = nullptr;   // NHWC4 (or row-packed) copy of an input that needs relayout
   bool packed_rows = false;    // staged_x is row-packed (pack_rows_kernel)
   bool s2d = false;            // staged_x is space-to-depth by 2 (to_s2d_kernel), AMODE 5
-  int s2d_pad_hi[2] = {0, 0};  // s2d: bottom / right padding of the transformed conv (H, W)
   ConvGeo src;                 // geometry of the original input (relayout source)
   const void *amap_base = nullptr, *ymap_base = nullptr, *rmap_base = nullptr;  // pointers the maps were encoded for
   int *sk_cnt = nullptr;   // stream-K arrival counters [stream-K tiles][epilogue warps]
@@ -1182,12 +1219,12 @@ bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
     return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 4, g.KH, g.sh, g.ph, g.dh, 4,
                               kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st.amode == 5) {
-    // Stride-1 windows from (-ph, -pw) to (dim - 1) + pad_hi - (k - 1); 16
-    // channels (64 bytes) per pixel, 64-byte swizzle.
+    // 16 channels (64 bytes) per pixel, 64-byte swizzle; window origins from
+    // (-pw, -ph) to the last output pixel's, (OW - 1) * sw - pw (and H).
     const int lower[2] = {-g.pw, -g.ph};
-    const int upper[2] = {st.s2d_pad_hi[1] - (g.KW - 1), st.s2d_pad_hi[0] - (g.KH - 1)};
-    return encode_im2col_corners(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 16, lower, upper, 1, 1, 16,
-                                 kBM, CU_TENSOR_MAP_SWIZZLE_64B);
+    const int upper[2] = {(g.OW - 1) * g.sw - g.pw - (g.W - 1), (g.OH - 1) * g.sh - g.ph - (g.H - 1)};
+    return encode_im2col_corners(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 16, lower, upper, g.sw,
+                                 g.sh, 16, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
 }
@@ -1285,9 +1322,6 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
       return SPKV2_ERR_DEVICE_ALLOC;
     }
     st->s2d = true;
-    // Bottom / right padding that keeps the output extent: H2 + pad + hi - k' + 1 = OH.
-    st->s2d_pad_hi[0] = g.OH - H2 - pad + k2 - 1;
-    st->s2d_pad_hi[1] = g.OW - W2 - pad + k2 - 1;
     g.C = g.Cg = 16;
     g.H = H2;
     g.W = W2;
@@ -1349,13 +1383,16 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   // A operand: tiled TMA for 1x1 stride-1 convs, im2col TMA for other
   // square convs with C % 32 == 0, cp.async gathers otherwise.
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
+  const bool im2col_ok = encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL");
   if (st->s2d)
     st->amode = 5;
-  else if (g.C % 32 == 0 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
-    st->amode = 2;
-  else if (g.C % 32 == 0 && (square || st->packed_rows) && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
+  else if (g.C % 4 == 0 && g.C >= 32 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
+    st->amode = 2;  // [P][C] rows; a last K step past C reads zeros (outside the tensor)
+  else if (g.C % 32 == 0 && (square || st->packed_rows) && im2col_ok)
     st->amode = 3;
-  else if (g.C == 4 && square && encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL"))
+  else if (g.C == 16 && im2col_ok)
+    st->amode = 5;  // 16-channel inputs: two 64-byte taps per K step
+  else if (g.C == 4 && square && im2col_ok)
     st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
   else
     st->amode = 1;
@@ -1426,6 +1463,9 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   const bool nhwc_res = g.has_res && g.rs[1] == 1 && g.rs[3] == g.M && g.rs[2] == int64_t(g.OW) * g.M;
   tp.res_tma = (st->epi_tma && nhwc_res && reinterpret_cast<uintptr_t>(r_dev) % 16 == 0) ? 1 : 0;
   tp.group = tp.num_kb;
+  tp.p32 = g.P < (int64_t(1) << 31) ? 1 : 0;
+  tp.ow_div = FastDiv(uint32_t(g.OW));
+  tp.oh_div = FastDiv(uint32_t(g.OH));
   if (st->split3) {
     // Promotion interval: each add of a group into the running sums costs
     // the epilogue warps TMEM round trips, and the truncating accumulation

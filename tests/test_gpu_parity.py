@@ -326,6 +326,38 @@ def test_stride2_few_channel_convs_space_to_depth_match_reference(gpu, cin, k, p
         np.testing.assert_allclose(out[0], base[0], atol=2e-3, rtol=2e-3)
 
 
+@pytest.mark.parametrize("cin,cout,k,stride,hw,amode", [
+    (16, 16, 3, 1, (40, 36), "_im2col2tap"),   # 16-channel input: two 64-byte taps per K step
+    (16, 32, 3, 2, (41, 40), "_im2col2tap"),
+    (16, 64, 1, 1, (20, 20), "_im2col2tap"),
+    (48, 32, 1, 1, (40, 40), "_tma"),          # 1x1, C % 32 != 0: the last K step reads zeros past C
+    (80, 80, 1, 1, (20, 22), "_tma"),
+])
+@pytest.mark.parametrize("math", ["spec", "tf32"])
+def test_tma_fed_convs_with_channel_counts_off_32_match_reference(gpu, cin, cout, k, stride, hw, amode, math):
+    import copy
+
+    from spinnv2_b200.compiler import builders, pipeline
+    from spinnv2_b200.runtime import MATH_SPEC, MATH_TF32
+
+    net = builders._Net(f"c{cin}_{cout}_{k}_{stride}", 10)
+    shape = [2, cin, hw[0], hw[1]]
+    x_id = net.b.input("input", shape)
+    y = net.conv(x_id, cin, 1, s=1, p=0, bias=True)  # the tested conv reads an NHWC device tensor
+    net.b.mark_output(net.conv(y, cout, k, s=stride, p=k // 2, bias=True, act="Relu"))
+    graph = pipeline.fuse(net.b.graph)
+    spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+    spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+    x = seeded_input(tuple(shape), seed=13)
+    ref = reference_outputs(spk_cpu, [x])[0]
+    out, variants = _run_gpu(spk_gpu, [x], math_mode=MATH_TF32 if math == "tf32" else MATH_SPEC)
+    assert sum(amode + "_" in v for v in variants) >= 2, variants  # both convs
+    if math == "spec":
+        np.testing.assert_allclose(out[0], ref, atol=ATOL, rtol=RTOL)
+    else:
+        np.testing.assert_allclose(out[0], ref, atol=2e-2, rtol=2e-2)
+
+
 @pytest.mark.parametrize("widths", [(8, 12, 4), (6, 10), (16, 16, 16, 16)])
 def test_split_and_concat_match_reference(gpu, widths):
     """Channel Split and Concat between convs (NHWC on the device): 16-byte
