@@ -313,12 +313,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&raw_bar[s], 1);                     // TMA producer's arrive.expect_tx (+ transaction bytes)
-      mbar_init(&full_bar[s], PAIR ? 256 : 128);     // A warps (of both CTAs of a pair)
+      mbar_init(&full_bar[s], PAIR ? 8 : 4);         // one arrival per A warp (of both CTAs of a pair)
       mbar_init(&empty_bar[s], 1);                   // MMA commit
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], 32 * kEpiWarps * (PAIR ? 2 : 1));
+      mbar_init(&acce_bar[b], kEpiWarps * (PAIR ? 2 : 1));  // one arrival per epilogue warp
     }
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bar[w], 1);
     abort_flag = 0;
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool failed = false;
       for (int gidx = 0; gidx + 1 < ngroups; ++gidx, ++gi) {
         const int pb = int(gi % NBUF);
-        if (!wait_any(&accf_bar[pb], (gi / NBUF) & 1, 4)) {
+        if (!__all_sync(0xffffffffu, wait_any(&accf_bar[pb], (gi / NBUF) & 1, 4))) {
           failed = true;
           break;
         }
@@ -409,11 +409,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        arrive_leader(&acce_bar[pb]);
+        __syncwarp();
+        if (lane == 0) arrive_leader(&acce_bar[pb]);
       }
       if (failed) break;
       const int ab = int(gi % NBUF);
-      if (!wait_any(&accf_bar[ab], (gi / NBUF) & 1, 4)) break;
+      if (!__all_sync(0xffffffffu, wait_any(&accf_bar[ab], (gi / NBUF) & 1, 4))) break;
       tc_fence_after();
       // Bias, residual, activation and store of accumulator columns
       // cb..cb+31 of this thread's row.
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (res_tma) {
           // (acc + bias) + residual, the residual read from the staging tile
           // its TMA load filled (rows past the end of the tensor read zeros).
-          if (!mbar_wait(&res_bar[warp], rc & 1, &abort_flag, status, 6)) return;
+          if (!__all_sync(0xffffffffu, mbar_wait(&res_bar[warp], rc & 1, &abort_flag, status, 6))) return;
           ++rc;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
@@ -544,13 +545,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (cb + 32 >= col0 + ncol) {
           tc_fence_before();
-          arrive_leader(&acce_bar[ab]);
+          __syncwarp();
+          if (lane == 0) arrive_leader(&acce_bar[ab]);
           ++gi;
         }
       };
       if (ncol == 0) {
         tc_fence_before();
-        arrive_leader(&acce_bar[ab]);
+        __syncwarp();
+        if (lane == 0) arrive_leader(&acce_bar[ab]);
         ++gi;
         continue;
       }
@@ -626,7 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t total = Iter(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x)).total_steps();
         for (; it < total; ++it) {
           const int s = it % STAGES;
-          if (!mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5)) break;
+          const bool landed = mbar_wait(&raw_bar[s], (it / STAGES) & 1, &abort_flag, status, 5);
+          if (!__all_sync(0xffffffffu, landed)) break;  // the warp leaves together
           uint8_t *a_hi = smem + s * STAGE;
           if constexpr (ALO) {
             // Row r = this warp's TMEM lane quarter + lane: its 32 K values
@@ -648,7 +652,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (SPLIT3) convert_tile<SPLIT3>(a_hi, a_hi, a_hi + kABytes, at);
             fence_proxy_async();
           }
-          arrive_leader(&full_bar[s]);
+          // One arrival per warp (each mbarrier arrival is a shared-memory
+          // read-modify-write the barrier serialises): every lane's writes
+          // are fenced above and ordered before lane 0's arrival here.
+          __syncwarp();
+          if (lane == 0) arrive_leader(&full_bar[s]);
         }
       }
     } else {
@@ -658,11 +666,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // once the MMA has released that stage.
       auto finish = [&](uint32_t pit) -> bool {
         const int s = pit % STAGES;
-        if (!mbar_wait(&empty_bar[s], ((pit / STAGES) & 1) ^ 1, &abort_flag, status, 1)) return false;
+        const bool freed = mbar_wait(&empty_bar[s], ((pit / STAGES) & 1) ^ 1, &abort_flag, status, 1);
+        if (!__all_sync(0xffffffffu, freed)) return false;
         uint8_t *a_hi = smem + s * STAGE;
         convert_tile<SPLIT3>(land + (pit % LAND) * kABytes, a_hi, a_hi + kABytes, at);
         fence_proxy_async();
-        mbar_arrive(&full_bar[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_bar[s]);
         return true;
       };
       Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
