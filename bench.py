@@ -487,6 +487,36 @@ def memory_bound(batch: int, local: int) -> dict:
     }
 
 
+def node_times(config: str, batch: int, local: int, int8: bool, math_mode: int | None) -> dict:
+    """Per-node device time of one config (eager, per-node CUDA events, mean
+    of 5 passes): the conv nodes with their shapes, FLOP rate and kernel
+    variant, and every other node's time.  A diagnostic line, not a bench
+    figure: no graph replay, no PDL overlap between nodes."""
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.runtime import Runtime
+
+    spk = pipeline.compile_config(config, batch, targets=("cuda_b200",), int8=int8)["cuda_b200"]
+    kw = {} if math_mode is None else {"math_mode": math_mode}
+    with Runtime(spk, device=local, graph=False, **kw) as rt:
+        pkg = rt.package
+        x = np.random.default_rng(1).standard_normal(pkg.inputs[0].shape, dtype=np.float32)
+        rt.set_input(0, x)
+        rt.run()
+        ms = node_shares(rt, 5)
+        rows = []
+        for n in pkg.nodes:
+            row = {"node": n.id, "op": n.op_type, "ms": float(ms[n.id]), "variant": rt.node_variant(n.id)}
+            if n.op_type == "Conv":
+                w = pkg.tensors[n.inputs[1]].shape
+                y = pkg.tensors[n.outputs[0]].shape
+                flop = 2.0 * y[0] * y[1] * y[2] * y[3] * w[1] * w[2] * w[3]
+                row.update({"shape": f"{w[1]}->{w[0]} k{w[2]}x{w[3]} out{y[2]}x{y[3]}",
+                            "tflops": flop / (float(ms[n.id]) * 1e-3) / 1e12 if ms[n.id] > 0 else None})
+            rows.append(row)
+    return {"config": config, "batch": batch, "int8": int8, "total_ms": float(sum(r["ms"] for r in rows)),
+            "nodes": rows}
+
+
 def strong_scaling(args, group, math_mode: int, flush) -> dict:
     """One global batch split into contiguous ceil(B/N) slices, one per rank
     (the per-rank form of ShardedRuntime): each rank compiles and prepares
@@ -655,6 +685,8 @@ def main() -> None:
     ap.add_argument("--mb-batch", type=int, default=64)
     ap.add_argument("--int8-batch", type=int, default=256)
     ap.add_argument("--int8", action="store_true", help="INT8 quantised network (use with --config resnet50)")
+    ap.add_argument("--nodes", action="store_true",
+                    help="only per-node device times of --config at --batch (eager, per-node events; diagnostic)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     from spinnv2_b200.shard import RankGroup
@@ -672,6 +704,12 @@ def main() -> None:
         elif args.memory_bound:
             if group.rank == 0:
                 print(json.dumps(memory_bound(args.mb_batch, group.local_rank)), flush=True)
+        elif args.nodes:
+            if group.rank == 0:
+                from spinnv2_b200.runtime import MATH_3XTF32, MATH_FP32, MATH_TF32
+
+                mm = {"spec": None, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32, "fp32": MATH_FP32}[args.math]
+                print(json.dumps(node_times(args.config, args.batch, group.local_rank, args.int8, mm)), flush=True)
         else:
             run_gpu_arm(args, group)
     finally:

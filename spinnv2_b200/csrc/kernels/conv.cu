@@ -421,15 +421,6 @@ int conv_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
     cudaMemsetAsync(p->bias_q, 0, sizeof(int32_t) * mpad, ctx->stream);
     cudaMemcpyAsync(p->bias_q, ctx->tensors[node->inputs[2]].data, sizeof(int32_t) * size_t(g.M),
                     cudaMemcpyDeviceToDevice, ctx->stream);
-    // Largest |bias| from the package's host copy (unknown: no bound).
-    const Spkv2TensorRecord *br = ctx->tensors[node->inputs[2]].record;
-    p->bias_absmax = int64_t(1) << 40;
-    if (br->role == SPKV2_ROLE_WEIGHT && br->data_offset + br->size_bytes <= ctx->weights_size) {
-      const int32_t *hb = reinterpret_cast<const int32_t *>(ctx->weights + br->data_offset);
-      int64_t mx = 0;
-      for (int c = 0; c < g.M; ++c) mx = std::max<int64_t>(mx, hb[c] < 0 ? -int64_t(hb[c]) : int64_t(hb[c]));
-      p->bias_absmax = mx;
-    }
   }
   if (ok && p->mode == kConvI8) {
     const float sx = per_tensor_scale(ctx, node->inputs[0], &ok);

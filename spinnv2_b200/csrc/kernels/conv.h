@@ -64,7 +64,6 @@ struct ConvPlan : NodePlan {
   void *w_tc = nullptr;    // tcgen05 operand panels (see conv_tc.cu)
   bool w_tc_borrowed = false;  // w_tc points into the device weight section (pre-packed SPK panel)
   int32_t *bias_q = nullptr;  // int32 requantisation bias (kConvI8)
-  int64_t bias_absmax = 0;    // max |bias_q| (kConvI8): bounds the epilogue's int32 sums
   float *scale_m = nullptr;   // per-channel requant multiplier M[c] (kConvI8)
   const float *bias_f = nullptr;  // fp32 bias (device weights)
   int tc_block_n = 0;      // tcgen05 tile width in output channels

@@ -1510,7 +1510,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   // critical path (each CTA gets an even share of their K steps; a tile
   // split across CTAs is finished by the last epilogue warp to arrive).
   // 3xTF32 only: measured on B200, TF32 main loops are short enough that
-  // writing and re-reading the partial tiles costs more than it saves.
+  // writing and re-reading the partial tiles costs more than it saves
+  // (ResNet-101 bs64 TF32 with the same model applied: 15.2k -> 13.5k img/s).
   tp.dp_tiles = tp.tiles;
   tp.sk_units = 0;
   tp.sk_ctas = sms;

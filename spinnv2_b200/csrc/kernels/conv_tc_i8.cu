@@ -65,18 +65,7 @@ struct I8Params {
   int64_t tiles;
   int out_i32;  // 1: int32 output (acc + b_q), no requantisation
   int epi_tma;  // 1: NHWC int8 output (and residual) through TMA tiles
-  int small_acc;  // every acc + b_q is inside (-2^22, 2^22): exact int -> float by the magic constant
 };
-
-// Exact integer <-> fp32 conversions on the FMA / integer pipes instead of
-// the quarter-rate conversion unit.  For |i| < 2^22 the bit pattern
-// 0x4B400000 + i is the float 1.5 * 2^23 + i, so subtracting 1.5 * 2^23
-// gives float(i) exactly; adding 1.5 * 2^23 to a float v with |v| < 2^22
-// rounds it to the nearest integer, ties to even (the sum's spacing is 1),
-// and leaves that integer in the low mantissa bits (low byte = the int8
-// code for v in [-128, 127]).
-constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-__device__ __forceinline__ float i2f_small(int32_t i) { return __fsub_rn(__int_as_float(i + 0x4B400000), kMagic); }
 
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -89,15 +78,17 @@ __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
 // source lands in bits 15:8, the second in bits 7:0, the third operand's
 // low half in bits 31:16).
 __device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, int lo) {
-  // Clamping to [lo, 127] before rounding gives the same code as rounding
-  // and then saturating (the bounds are integers).
-  const float flo = float(lo);
-  const uint32_t qa = __float_as_uint(__fadd_rn(fminf(fmaxf(a, flo), 127.0f), kMagic));
-  const uint32_t qb = __float_as_uint(__fadd_rn(fminf(fmaxf(b, flo), 127.0f), kMagic));
-  const uint32_t qc = __float_as_uint(__fadd_rn(fminf(fmaxf(c, flo), 127.0f), kMagic));
-  const uint32_t qd = __float_as_uint(__fadd_rn(fminf(fmaxf(d, flo), 127.0f), kMagic));
-  // Low bytes: [qa.b0, qb.b0, qc.b0, qd.b0].
-  return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
+  if (lo == 0) {
+    a = fmaxf(a, 0.0f);
+    b = fmaxf(b, 0.0f);
+    c = fmaxf(c, 0.0f);
+    d = fmaxf(d, 0.0f);
+  }
+  const int qa = __float2int_rn(a), qb = __float2int_rn(b), qc = __float2int_rn(c), qd = __float2int_rn(d);
+  uint32_t hi, w;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(qd), "r"(qc), "r"(0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(qb), "r"(qa), "r"(hi));
+  return w;
 }
 
 // Epilogue warps: 4 with gathered A (warps 4-7 gather), else 8, or 16 for
@@ -265,17 +256,10 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 m = __ldg(reinterpret_cast<const float4 *>(scale_m + c0 + j));
-          if (tp.small_acc) {
-            v[j] = __fmul_rn(i2f_small(a[j]), m.x);
-            v[j + 1] = __fmul_rn(i2f_small(a[j + 1]), m.y);
-            v[j + 2] = __fmul_rn(i2f_small(a[j + 2]), m.z);
-            v[j + 3] = __fmul_rn(i2f_small(a[j + 3]), m.w);
-          } else {
-            v[j] = __fmul_rn(float(a[j]), m.x);
-            v[j + 1] = __fmul_rn(float(a[j + 1]), m.y);
-            v[j + 2] = __fmul_rn(float(a[j + 2]), m.z);
-            v[j + 3] = __fmul_rn(float(a[j + 3]), m.w);
-          }
+          v[j] = __fmul_rn(float(a[j]), m.x);
+          v[j + 1] = __fmul_rn(float(a[j + 1]), m.y);
+          v[j + 2] = __fmul_rn(float(a[j + 2]), m.z);
+          v[j + 3] = __fmul_rn(float(a[j + 3]), m.w);
         }
         uint8_t *srow = stile + lane * CW + cb;  // this thread's 32 bytes of the staging tile
         if (g.has_res) {
@@ -291,7 +275,7 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
             for (int j = 0; j < 32; ++j) r[j] = (pv && j < cn) ? res[rbase + int64_t(c0 + j) * g.rs[1]] : int8_t(0);
           }
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __fmul_rn(i2f_small(int32_t(r[j])), g.res_scale));
+          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], __fmul_rn(float(r[j]), g.res_scale));
         }
         uint32_t w[8];
 #pragma unroll
@@ -625,8 +609,6 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
   tp.out_i32 = p.mode == kConvI8ToI32 ? 1 : 0;
-  // |x * w| <= 128 * 128 per product of int8 codes.
-  tp.small_acc = int64_t(g.K) * 128 * 128 + p.bias_absmax < (int64_t(1) << 22) ? 1 : 0;
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   const bool nhwc_res = !g.has_res || (g.rs[1] == 1 && g.rs[3] == g.M && g.rs[2] == int64_t(g.OW) * g.M);
   tp.epi_tma = (!tp.out_i32 && nhwc_out && nhwc_res && g.M % 16 == 0 &&
