@@ -773,17 +773,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (AMODE == 5) {
-            // Space-to-depth input (C == 16, 64 bytes per pixel): two taps
-            // per K step, each a 128 pixel x 64 byte column in its own
-            // 64-byte-swizzled half of the A tile; a tap past the filter
+            // C % 16 == 0 (16 for space-to-depth inputs): each K step is two
+            // 16-channel halves, k = 32 kb + 16 j, each a 128 pixel x 64 byte
+            // im2col column of filter tap k / C at channel k % C in its own
+            // 64-byte-swizzled half of the A tile; a half past the filter
             // reads an image past the batch (zeros).
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-              const int tap = 2 * kb + j;
+              const int k = kb * kBK + j * 16;
+              const int tap = k / g.C;
               const bool real = tap < g.KH * g.KW;
               const int r = real ? tap / g.KW : 0, sx = real ? tap - r * g.KW : 0;
-              tma_load_im2col_4d(a_hi + j * (kABytes / 2), &amap, 0, bw, bh, real ? bn : g.N, uint16_t(sx * g.dw),
-                                 uint16_t(r * g.dh), &raw_bar[s]);
+              tma_load_im2col_4d(a_hi + j * (kABytes / 2), &amap, real ? k - tap * g.C : 0, bw, bh, real ? bn : g.N,
+                                 uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
             }
           }
           if (AMODE == 4) {
@@ -1229,11 +1231,11 @@ bool encode_a(const TcState &st, CUtensorMap *map, const void *x) {
     return encode_im2col_nhwc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 4, g.KH, g.sh, g.ph, g.dh, 4,
                               kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st.amode == 5) {
-    // 16 channels (64 bytes) per pixel, 64-byte swizzle; window origins from
+    // 16-channel (64-byte) boxes, 64-byte swizzle; window origins from
     // (-pw, -ph) to the last output pixel's, (OW - 1) * sw - pw (and H).
     const int lower[2] = {-g.pw, -g.ph};
     const int upper[2] = {(g.OW - 1) * g.sw - g.pw - (g.W - 1), (g.OH - 1) * g.sh - g.ph - (g.H - 1)};
-    return encode_im2col_corners(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, 16, lower, upper, g.sw,
+    return encode_im2col_corners(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, g.N, g.H, g.W, g.C, lower, upper, g.sw,
                                  g.sh, 16, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
   }
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, uint64_t(g.C), uint64_t(g.P), uint64_t(g.C), kBM);
@@ -1400,8 +1402,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     st->amode = 2;  // [P][C] rows; a last K step past C reads zeros (outside the tensor)
   else if (g.C % 32 == 0 && (square || st->packed_rows) && im2col_ok)
     st->amode = 3;
-  else if (g.C == 16 && im2col_ok)
-    st->amode = 5;  // 16-channel inputs: two 64-byte taps per K step
+  else if (g.C % 16 == 0 && im2col_ok)
+    st->amode = 5;  // C % 16 == 0: two 64-byte (16-channel) im2col columns per K step
   else if (g.C == 4 && square && im2col_ok)
     st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
   else

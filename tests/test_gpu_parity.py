@@ -327,9 +327,11 @@ def test_stride2_few_channel_convs_space_to_depth_match_reference(gpu, cin, k, p
 
 
 @pytest.mark.parametrize("cin,cout,k,stride,hw,amode", [
-    (16, 16, 3, 1, (40, 36), "_im2col2tap"),   # 16-channel input: two 64-byte taps per K step
+    (16, 16, 3, 1, (40, 36), "_im2col2tap"),   # C % 16 == 0: two 16-channel im2col columns per K step
     (16, 32, 3, 2, (41, 40), "_im2col2tap"),
     (16, 64, 1, 1, (20, 20), "_im2col2tap"),
+    (80, 80, 3, 1, (20, 18), "_im2col2tap"),   # C % 32 == 16: K steps cross filter taps
+    (48, 32, 3, 2, (21, 22), "_im2col2tap"),
     (48, 32, 1, 1, (40, 40), "_tma"),          # 1x1, C % 32 != 0: the last K step reads zeros past C
     (80, 80, 1, 1, (20, 22), "_tma"),
 ])
