@@ -193,11 +193,14 @@ struct WorkIter {
 // warps write A's low part into a TMEM ring (one 32-column slot per stage)
 // instead of shared memory and the A_lo * B_hi MMAs read A from TMEM.  The
 // stage shrinks to [A hi][B hi][B lo] (48 KB), so four stages fit instead of
-// three: the tensor pipe idles about half the time on the hand-off chain
-// with three.  Two accumulator buffers (promotion every few K steps leaves
-// the epilogue a group's time per add) free the TMEM for the ring.
+// three.  Two accumulator buffers (promotion every few K steps leaves the
+// epilogue a group's time per add) free the TMEM for the ring.  Narrow tiles
+// keep A's low part in shared memory: measured on B200 with the ring at BN =
+// 64 / 32 (6 / 8 stages), the detector's 3x3 16-channel convs took 375
+// instead of 335 us and ResNet-50 INT8 bs256 (its fp32 BN = 64 first conv)
+// dropped from 57.7k to 55.6k img/s.
 constexpr bool alo_tmem(int bn, bool split3, int amode, bool pair) {
-  return split3 && !pair && bn == 128 && (amode == 2 || amode == 3);
+  return split3 && !pair && bn == 128 && (amode == 2 || amode == 3 || amode == 5);
 }
 
 // One pipeline stage: [A (hi)][A lo (3xTF32)][B hi][B lo (3xTF32)], or
@@ -639,7 +642,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t lo[32];
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-              const float4 v = *reinterpret_cast<const float4 *>(a_hi + swz_off(r, c));
+              // AMODE 5: K elements 0-15 in the first 64-byte-swizzled half
+              // (16-byte chunk cc of row r at r * 64 + (cc ^ (r / 2 % 4)) * 16),
+              // 16-31 in the second.
+              const uint32_t off = AMODE == 5 ? uint32_t((c >> 2) * (kABytes / 2) + r * 64 + (((c & 3) ^ ((r >> 1) & 3)) << 4))
+                                              : swz_off(r, c);
+              const float4 v = *reinterpret_cast<const float4 *>(a_hi + off);
               lo[4 * c] = __float_as_uint(v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u));
               lo[4 * c + 1] = __float_as_uint(v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u));
               lo[4 * c + 2] = __float_as_uint(v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u));
@@ -1176,12 +1184,15 @@ struct PipeShape {
 };
 // In a CTA pair each CTA holds BN/2 weight rows, so its stages are those of
 // a BN/2-wide single-CTA tile.
+// With A's low part in TMEM (BN = 128) a stage is [A hi][B hi][B lo], 48 KB:
+// four stages (the ring takes 32 TMEM columns per stage).
 constexpr PipeShape pipe_shape(int bn, bool split3, int amode, bool pair = false) {
-  return pair ? pipe_shape(bn / 2, split3, amode)
-              : amode != 1 ? (split3 ? PipeShape{bn == 256 ? 2 : bn == 128 ? (alo_tmem(bn, split3, amode, false) ? 4 : 3) : 4, 0}
-                                     : PipeShape{bn == 256 ? 4 : 6, 0})
-                           : (split3 ? PipeShape{bn == 256 ? 1 : bn == 128 ? 2 : 3, bn == 128 ? 4 : 3}
-                                     : PipeShape{bn == 256 ? 3 : 4, bn == 256 ? 3 : 4});
+  const int b = pair ? bn / 2 : bn;  // weight rows per CTA
+  return amode != 1 ? (split3 ? (alo_tmem(bn, split3, amode, pair) ? PipeShape{b == 128 ? 4 : b == 64 ? 6 : 8, 0}
+                                                                   : PipeShape{b == 256 ? 2 : b == 128 ? 3 : 4, 0})
+                              : PipeShape{b == 256 ? 4 : 6, 0})
+                    : (split3 ? PipeShape{b == 256 ? 1 : b == 128 ? 2 : 3, b == 128 ? 4 : 3}
+                              : PipeShape{b == 256 ? 3 : 4, b == 256 ? 3 : 4});
 }
 
 size_t smem_bytes(int bn, bool split3, int amode, bool pair) {
