@@ -750,10 +750,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           bh = oh * g.sh - g.ph;
         }
         // AMODE 3 position of K step kb (C % 32 == 0: one filter tap per K
-        // step), advanced incrementally so no division sits between the
-        // stage becoming free and the loads.
+        // step), AMODE 5 position of its first 16-channel half, advanced
+        // incrementally so no division sits between the stage becoming free
+        // and the loads (two divisions per K step there cost the fp32 first
+        // convs 13 % on B200).
         int c0 = 0, sx = 0, r = 0;
-        if (AMODE == 3) {
+        if (AMODE == 3 || AMODE == 5) {
           const int k0 = sg.kb0 * kBK, tap = k0 / g.C;
           c0 = k0 - tap * g.C;
           r = tap / g.KW;
@@ -788,12 +790,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             // reads an image past the batch (zeros).
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-              const int k = kb * kBK + j * 16;
-              const int tap = k / g.C;
-              const bool real = tap < g.KH * g.KW;
-              const int r = real ? tap / g.KW : 0, sx = real ? tap - r * g.KW : 0;
-              tma_load_im2col_4d(a_hi + j * (kABytes / 2), &amap, real ? k - tap * g.C : 0, bw, bh, real ? bn : g.N,
-                                 uint16_t(sx * g.dw), uint16_t(r * g.dh), &raw_bar[s]);
+              const bool real = r < g.KH;
+              tma_load_im2col_4d(a_hi + j * (kABytes / 2), &amap, real ? c0 : 0, bw, bh, real ? bn : g.N,
+                                 uint16_t(real ? sx * g.dw : 0), uint16_t(real ? r * g.dh : 0), &raw_bar[s]);
+              if ((c0 += 16) == g.C) {
+                c0 = 0;
+                if (++sx == g.KW) {
+                  sx = 0;
+                  ++r;
+                }
+              }
             }
           }
           if (AMODE == 4) {
