@@ -7,7 +7,7 @@
 // fly (implicit im2col), B = packed weights [Cout_pad][K_pad] K-major.
 //
 // Persistent kernel: one CTA per SM walks output tiles (128 pixels x BN
-// channels) in a static round-robin.  Warp roles (448 threads):
+// channels) in a static round-robin.  Warp roles (480 threads):
 //   warps 0-7   epilogue: warps w and w+4 read TMEM lanes 32(w%4).. (tile
 //               rows) and split the tile's columns -> registers -> bias,
 //               residual (prefetched into L2 when the tile starts), Relu /
@@ -32,9 +32,13 @@
 //               high part and lo = x - trunc_tf32(x) is exact in fp32 (half
 //               the shared-memory traffic of writing a rounded high part).
 //   warp 12     TMA producer (one thread): weight panels (hi, and lo for
-//               3xTF32), and the A tile in AMODE 2/3.  No multicast.
+//               3xTF32).  No multicast.
 //   warp 13     TMEM allocation; one thread issues tcgen05.mma (M=128, N=BN,
 //               K=8) and commits stage releases and finished accumulators.
+//   warp 14     TMA producer (one thread) of the A tile in the TMA A modes
+//               (2-5): the weight and activation loads of a stage are issued
+//               by two threads, measured on B200: neutral on the ResNet-101
+//               3xTF32 step, +2 % TF32 mode and detector bs64.
 // 3xTF32: acc += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi (three MMAs per K step).
 // The tensor core's fp32 accumulation truncates, which over long K chains
 // biases the sum (the error grows linearly with K).  In 3xTF32 mode each
@@ -65,7 +69,7 @@ using namespace tc;
 constexpr int kBM = 128;          // tile rows (pixels) = UMMA M
 constexpr int kBK = 32;           // fp32 elements per K step = 128 bytes
 constexpr int kABytes = kBM * 128;
-constexpr int kThreads = 448;               // 8 epilogue + 4 A-operand + TMA + MMA warps
+constexpr int kThreads = 480;               // 8 epilogue + 4 A-operand + weight TMA + MMA + A TMA warps
 constexpr int kEpiWarps = 8;
 constexpr int kStagingBytes = kEpiWarps * 4096;  // epilogue: one 32x32 fp32 tile per warp
 
@@ -279,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // in a CTA pair, to tell the leader that this CTA's operands have landed.
   // Otherwise TF32 TMA tiles go to the tensor core as loaded.
   constexpr bool CONVERT = (AMODE == 1) || SPLIT3;
+  constexpr bool SEP_A = AMODE != 1;  // a second TMA thread (warp 14) loads the A tiles
   constexpr bool RELAY = CONVERT || PAIR;
   // TMEM: the accumulator buffers + the promoted sums for 3xTF32, rounded
   // up to a power of two >= 32 columns.
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&raw_bar[s], 1);                     // TMA producer's arrive.expect_tx (+ transaction bytes)
+      mbar_init(&raw_bar[s], SEP_A ? 2 : 1);         // TMA producers' arrive.expect_tx (+ transaction bytes)
       mbar_init(&full_bar[s], PAIR ? 8 : 4);         // one arrival per A warp (of both CTAs of a pair)
       mbar_init(&empty_bar[s], 1);                   // MMA commit
     }
@@ -729,10 +734,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t pit = first; pit < it && ok; ++pit) ok = finish(pit);
       }
     }
-  } else if (warp == kEpiWarps + 4) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const uint32_t bytes = (SPLIT3 ? 2 : 1) * B_BYTES + (AMODE != 1 ? kABytes : 0);
+  } else if (warp == kEpiWarps + 4 || warp == kEpiWarps + 6) {
+    // ------------------------------------------------------------ TMA producers
+    // Warp 12 loads the weight panels; in the TMA A modes warp 14 loads the A
+    // tile of the same stage, so the loads of one stage do not queue behind
+    // each other in one issuing thread (every instruction between a stage
+    // becoming free and its loads lengthens the K step).
+    const bool a_role = warp == kEpiWarps + 6;
+    if (lane == 0 && (!a_role || SEP_A)) {
+      const uint32_t bytes = a_role ? uint32_t(kABytes) : uint32_t((SPLIT3 ? 2 : 1) * B_BYTES);
       uint32_t it = 0;
       bool ok = true;
       Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
@@ -743,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
         const int brow = n0 + int(rank) * BROWS;  // first weight row this CTA loads
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
-        if (AMODE == 3 || AMODE == 4 || AMODE == 5) {
+        if (a_role && (AMODE == 3 || AMODE == 4 || AMODE == 5)) {
           int ow, oh;
           pixel_nhw(tp, m0, bn, oh, ow);
           bw = ow * g.sw - g.pw;
@@ -755,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // and the loads (two divisions per K step there cost the fp32 first
         // convs 13 % on B200).
         int c0 = 0, sx = 0, r = 0;
-        if (AMODE == 3 || AMODE == 5) {
+        if (a_role && (AMODE == 3 || AMODE == 5)) {
           const int k0 = sg.kb0 * kBK, tap = k0 / g.C;
           c0 = k0 - tap * g.C;
           r = tap / g.KW;
@@ -769,8 +779,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *a_hi = smem + s * STAGE;
           uint8_t *b_hi = a_hi + B_OFF;
           mbar_arrive_expect_tx(&raw_bar[s], bytes);
-          tma_load_2d(b_hi, &wmap, kb * kBK, brow, &raw_bar[s]);
-          if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + brow, &raw_bar[s]);
+          if (!a_role) {
+            tma_load_2d(b_hi, &wmap, kb * kBK, brow, &raw_bar[s]);
+            if (SPLIT3) tma_load_2d(b_hi + B_BYTES, &wmap, kb * kBK, tp.Npad + brow, &raw_bar[s]);
+            continue;
+          }
           if (AMODE == 2) tma_load_2d(a_hi, &amap, kb * kBK, int(m0), &raw_bar[s]);
           if (AMODE == 3) {
             tma_load_im2col_4d(a_hi, &amap, c0, bw, bh, bn, woff, hoff, &raw_bar[s]);
