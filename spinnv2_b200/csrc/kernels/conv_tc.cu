@@ -863,6 +863,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         return PAIR ? mbar_wait_cluster(bar, parity, &abort_flag, status, code)
                     : mbar_wait_fast(bar, parity, &abort_flag, status, code);
       };
+      // Stage 0's operand descriptors.  AMODE 4 A tiles are unswizzled
+      // 4-channel columns: core matrices of 8 pixels x 16 bytes, 2 KB apart
+      // along K, 128 B apart along M; AMODE 5 A tiles are two 64-byte-swizzled
+      // halves.
+      auto a_base_desc = [&](const uint8_t *p) -> uint64_t {
+        return AMODE == 4 ? smem_desc_noswz(p, 2048, 128) : AMODE == 5 ? smem_desc_sw64(p) : smem_desc(p);
+      };
+      const uint64_t dah0 = a_base_desc(smem), dal0 = a_base_desc(smem + kABytes);
+      const uint64_t dbh0 = smem_desc(smem + B_OFF), dbl0 = smem_desc(smem + B_OFF + B_BYTES);
       bool ok = true;
       for (uint32_t it = 0; ok && it < total;) {
         if (seg_left == 0) {
@@ -888,6 +897,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // (or, in a pair, relayed) stage is signalled on full_bar, after
           // the A warps saw raw_bar themselves.  (AMODE 1: the A warps gather
           // A and do not see raw_bar, so both are waited on here.)
+          // This stage's descriptors: stage 0's plus the stage offset (the
+          // 14-bit address field is linear in the shared-memory address),
+          // computed before the waits so nothing but the fence sits between
+          // the stage becoming ready and its MMAs.
+          const uint64_t soff = uint64_t(s) * uint64_t(STAGE >> 4);
+          const uint64_t dbh = dbh0 + soff, dbl = dbl0 + soff, dah = dah0 + soff, dal = dal0 + soff;
           if (!(AMODE != 1 && RELAY) && !mbar_wait_fast(&raw_bar[s], ph, &abort_flag, status, 3)) {
             ok = false;
             break;
@@ -897,22 +912,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          uint8_t *a_hi = smem + s * STAGE;
-          uint8_t *a_lo = a_hi + kABytes;
-          uint8_t *b_hi = a_hi + B_OFF;
-          uint8_t *b_lo = b_hi + B_BYTES;
-          const uint64_t dbh = smem_desc(b_hi), dbl = smem_desc(b_lo);
-          // AMODE 4 A tiles are unswizzled 4-channel columns: core matrices
-          // of 8 pixels x 16 bytes, 2 KB apart along K, 128 B apart along M.
-          const uint64_t dah = AMODE == 4 ? smem_desc_noswz(a_hi, 2048, 128) : smem_desc(a_hi);
-          const uint64_t dal = AMODE == 4 ? smem_desc_noswz(a_lo, 2048, 128) : smem_desc(a_lo);
           const int gstep = gk + r;  // the group's first K step overwrites the accumulator
           // Operand descriptors of K slice kk (8 tf32 = 32 bytes along K).
           // AMODE 4: two 2 KB core-matrix columns per slice; AMODE 5: slices
-          // 0-1 in the first 64-byte-swizzled half (tap 2kb), 2-3 in the
-          // second (tap 2kb + 1).
-          auto a_desc = [&](uint8_t *base, uint64_t d, int kk) -> uint64_t {
-            return AMODE == 5   ? smem_desc_sw64(base + (kk >> 1) * (kABytes / 2)) + uint64_t((kk & 1) * 2)
+          // 0-1 in the first 64-byte-swizzled half, 2-3 in the second.
+          auto a_desc = [&](uint64_t d, int kk) -> uint64_t {
+            return AMODE == 5   ? d + uint64_t((kk >> 1) * (kABytes / 2 / 16) + (kk & 1) * 2)
                    : AMODE == 4 ? d + (uint64_t(kk * 4096) >> 4)
                                 : d + (uint64_t(kk * 32) >> 4);
           };
@@ -933,7 +938,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // A_lo from TMEM: slot s, columns kk*8.. (one 32-bit column per K element).
                 mma_tf32_ta(dtm, tmem + uint32_t(Acc::alo_col + s * 32 + kk * 8), db, idesc, acc);
               } else {
-                const uint64_t da = SPLIT3 && pass == 0 ? a_desc(a_lo, dal, kk) : a_desc(a_hi, dah, kk);
+                const uint64_t da = SPLIT3 && pass == 0 ? a_desc(dal, kk) : a_desc(dah, kk);
                 if (PAIR)
                   mma_tf32_pair(dtm, da, db, idesc, acc);
                 else
