@@ -106,13 +106,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
-// Prefetch a tile of a 2-D tensor map into L2 (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // im2col load of a 4-D NHWC tensor map: `pixels x channels` box starting at
 // base position {c, w, h, n}, shifted by the filter tap {w_off, h_off}.
 __device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap *map, int c, int w, int h, int n,
