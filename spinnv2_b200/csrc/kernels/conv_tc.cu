@@ -90,6 +90,7 @@ struct TcParams {
   int sk_park_all;   // split-K: every segment parks its partial; conv_tc_reduce_kernel finishes all tiles
   int p32;           // output pixel count < 2^31: pixel coordinates by 32-bit multiply-shift divisions
   FastDiv ow_div, oh_div;
+  FastDiv nt_div, u_div, g_div;  // split-K reduce: n_tiles, sk_units, sk_ctas
 };
 
 // Epilogue activation over a register array (one branch per call).  SiLU
@@ -1011,33 +1012,35 @@ __global__ void __launch_bounds__(256) conv_tc_reduce_kernel(const float4 *__res
   pdl_launch_dependents();
   pdl_wait();  // the conv launch's partials are complete and visible
   const ConvGeo &g = tp.g;
-  const int64_t U = tp.sk_units;
-  const int64_t G = tp.sk_ctas;
-  const int64_t nk = tp.num_kb;
-  constexpr int kGroups = BN / 4;
-  const int64_t total = tp.tiles * kBM * kGroups;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-    const int row = int(i % kBM);
-    const int64_t rest = i / kBM;
-    const int cg = int(rest % kGroups);
-    const int64_t tt = rest / kGroups;
-    const int64_t p = (tt / tp.n_tiles) * kBM + row;
-    const int c0 = int(tt % tp.n_tiles) * BN + cg * 4;
+  // 32-bit index arithmetic with multiply-shift divisions (split-K runs only
+  // for a few tiles: the host keeps every product below 2^31).
+  const uint32_t U = uint32_t(tp.sk_units), G = uint32_t(tp.sk_ctas);
+  const uint32_t nk = uint32_t(tp.num_kb), n_tiles = uint32_t(tp.n_tiles);
+  constexpr uint32_t kGroups = BN / 4;
+  const uint32_t total = uint32_t(tp.tiles) * kBM * kGroups;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t row = i % kBM;
+    const uint32_t rest = i / kBM;
+    const uint32_t cg = rest % kGroups;
+    const uint32_t tt = rest / kGroups;
+    const uint32_t mt = tp.nt_div.div(tt);
+    const int64_t p = int64_t(mt) * kBM + row;
+    const int c0 = int(tt - mt * n_tiles) * BN + int(cg) * 4;
     if (p >= g.P || c0 >= g.M) continue;
     // CTAs whose shares hold the tile's first and last K steps (the
     // WorkIter owner / start arithmetic).
-    const int64_t v0 = tt * nk, v1 = v0 + nk - 1;
-    const int64_t blo = ((v0 + 1) * G - 1) / U, bhi = ((v1 + 1) * G - 1) / U;
-    const int64_t idx = int64_t(((cg >> 3) * 8 + (cg & 7)) * 128 + row);
+    const uint32_t v0 = tt * nk, v1 = v0 + nk - 1;
+    const uint32_t blo = tp.u_div.div((v0 + 1) * G - 1), bhi = tp.u_div.div((v1 + 1) * G - 1);
+    const uint32_t idx = cg * 128 + row;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     // Sixteen segments' loads in flight at a time, added in segment order.
-    for (int64_t j0 = blo; j0 <= bhi; j0 += 16) {
+    for (uint32_t j0 = blo; j0 <= bhi; j0 += 16) {
       float4 f[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
-        const int64_t j = j0 + k;
-        const int slot = j * U / G >= v0 ? 0 : 1;
-        f[k] = j <= bhi ? __ldcg(&ws[(j * 2 + slot) * (BN * 32) + idx]) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t j = j0 + k;
+        const uint32_t slot = tp.g_div.div(j * U) >= v0 ? 0 : 1;
+        f[k] = j <= bhi ? __ldcg(&ws[size_t(j * 2 + slot) * (BN * 32) + idx]) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
@@ -1049,9 +1052,8 @@ __global__ void __launch_bounds__(256) conv_tc_reduce_kernel(const float4 *__res
         }
       }
     }
-    const int ow = int(p % g.OW);
-    const int64_t q = p / g.OW;
-    const int oh = int(q % g.OH), n = int(q / g.OH);
+    int n, oh, ow;
+    pixel_nhw(tp, p, n, oh, ow);
     const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
     const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
     float v[4] = {a.x, a.y, a.z, a.w};
@@ -1489,7 +1491,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     int min_steps = 4;
     if (const char *e = getenv("SPKV2_TC_SPLITK_MIN_STEPS")) min_steps = std::max(1, atoi(e));
     const int64_t gsk = std::min<int64_t>(sms, units / min_steps);
-    if (2 * t <= sms && gsk >= 2 * t) {
+    // (units * G < 2^31: the reduce kernel's 32-bit index arithmetic.)
+    if (2 * t <= sms && gsk >= 2 * t && units * sms < (int64_t(1) << 31)) {
       bn = bw;
       ska_g = int(gsk);
     }
@@ -1557,6 +1560,9 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     tp.dp_tiles = 0;
     tp.sk_units = tp.tiles * tp.num_kb;
     tp.sk_ctas = ska_g;
+    tp.nt_div = FastDiv(uint32_t(tp.n_tiles));
+    tp.u_div = FastDiv(uint32_t(tp.sk_units));
+    tp.g_div = FastDiv(uint32_t(ska_g));
     tp.sk_park_all = 1;
     st->grid = ska_g;
     st->sk_ws_bytes = size_t(ska_g) * 2 * size_t(bn) * kBM * sizeof(float);
