@@ -90,7 +90,7 @@ struct TcParams {
   int sk_park_all;   // split-K: every segment parks its partial; conv_tc_reduce_kernel finishes all tiles
   int p32;           // output pixel count < 2^31: pixel coordinates by 32-bit multiply-shift divisions
   FastDiv ow_div, oh_div;
-  FastDiv nt_div, u_div, g_div;  // split-K reduce: n_tiles, sk_units, sk_ctas
+  FastDiv nt_div, u_div, g_div, nk_div;  // n_tiles, sk_units, sk_ctas, num_kb (stream-K / split-K schedule)
 };
 
 // Epilogue activation over a register array (one branch per call).  SiLU
@@ -148,20 +148,25 @@ struct WorkIter {
   int64_t t, tstep, dp_tiles;
   int64_t u, u0, u1, U;
   int nk, G, b;
+  // The stream-K arithmetic is 32-bit with the host's multiply-shift
+  // divisors (the host keeps U * G below 2^31): it runs in every role
+  // before the first load or MMA of the kernel.
+  FastDiv u_div, g_div, nk_div;
   __device__ WorkIter(const TcParams &tp, int64_t tile0, int64_t step, int cta, int grid)
       : t(tile0), tstep(step), dp_tiles(SK ? tp.dp_tiles : tp.tiles), U(SK ? tp.sk_units : 0), nk(tp.num_kb),
-        G(SK && tp.sk_units ? tp.sk_ctas : grid), b(cta) {
-    u0 = U ? (b < G ? int64_t(b) * U / G : U) : 0;
-    u1 = U ? (b < G ? int64_t(b + 1) * U / G : U) : 0;
+        G(SK && tp.sk_units ? tp.sk_ctas : grid), b(cta), u_div(tp.u_div), g_div(tp.g_div), nk_div(tp.nk_div) {
+    u0 = U ? (b < G ? int64_t(start_of(b)) : U) : 0;
+    u1 = U ? (b < G ? int64_t(start_of(b + 1)) : U) : 0;
     u = u0;
   }
-  __device__ int64_t start_of(int64_t cta) const { return cta * U / G; }
-  __device__ int64_t owner(int64_t v) const { return ((v + 1) * G - 1) / U; }  // CTA whose share holds unit v
+  __device__ int64_t start_of(int64_t cta) const { return g_div.div(uint32_t(cta) * uint32_t(U)); }
+  // CTA whose share holds unit v.
+  __device__ int64_t owner(int64_t v) const { return u_div.div((uint32_t(v) + 1) * uint32_t(G) - 1); }
   // Workspace slot in which CTA `cta` keeps its segment of stream-K tile tt.
   __device__ int slot_of(int64_t cta, int64_t tt) const { return start_of(cta) >= tt * nk ? 0 : 1; }
   // K steps of this CTA's whole schedule.
   __device__ uint32_t total_steps() const {
-    const int64_t mine = t < dp_tiles ? (dp_tiles - 1 - t) / tstep + 1 : 0;
+    const int64_t mine = t < dp_tiles ? int64_t(uint32_t(dp_tiles - 1 - t) / uint32_t(tstep)) + 1 : 0;
     return uint32_t(mine * nk + (u1 - u0));
   }
   __device__ bool next(Seg &s) {
@@ -175,7 +180,7 @@ struct WorkIter {
       return true;
     }
     if (!SK || u >= u1) return false;
-    const int64_t tt = u / nk;
+    const int64_t tt = nk_div.div(uint32_t(u));
     s.tt = int(tt);
     s.tile = dp_tiles + tt;
     s.kb0 = int(u - tt * nk);
@@ -1561,8 +1566,6 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     tp.sk_units = tp.tiles * tp.num_kb;
     tp.sk_ctas = ska_g;
     tp.nt_div = FastDiv(uint32_t(tp.n_tiles));
-    tp.u_div = FastDiv(uint32_t(tp.sk_units));
-    tp.g_div = FastDiv(uint32_t(ska_g));
     tp.sk_park_all = 1;
     st->grid = ska_g;
     st->sk_ws_bytes = size_t(ska_g) * 2 * size_t(bn) * kBM * sizeof(float);
@@ -1592,7 +1595,7 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
       if (gs == sms) break;
     }
     if (const char *e = getenv("SPKV2_TC_SK_CTAS")) best_g = tail > 0 ? std::min(sms, std::max(1, atoi(e))) : 0;
-    if (best_g > 0) {
+    if (best_g > 0 && tail * nk * sms < (int64_t(1) << 31)) {  // 32-bit schedule arithmetic
       tp.dp_tiles = rounds * sms;
       tp.sk_units = tail * nk;
       tp.sk_ctas = best_g;
@@ -1602,6 +1605,11 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
       ok = st->sk_cnt && cudaMemsetAsync(st->sk_cnt, 0, st->sk_cnt_bytes, s) == cudaSuccess;
       st->sk_ws_bytes = size_t(sms) * 2 * size_t(bn) * kBM * sizeof(float);
     }
+  }
+  tp.nk_div = FastDiv(uint32_t(tp.num_kb));
+  if (tp.sk_units) {
+    tp.u_div = FastDiv(uint32_t(tp.sk_units));
+    tp.g_div = FastDiv(uint32_t(tp.sk_ctas));
   }
   st->rmap_base = r_dev;
   st->amap_base = x_dev;
