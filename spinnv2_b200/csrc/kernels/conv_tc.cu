@@ -385,8 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (wi.next(sg)) {
       const int64_t t = sg.tile;
       const int ngroups = (sg.kb1 - sg.kb0 + tp.group - 1) / tp.group;
-      const int n0 = int(t % tp.n_tiles) * BN;
-      const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
+      const uint32_t mt = tp.nt_div.div(uint32_t(t));  // tile row, column (tiles < 2^31)
+      const int n0 = int(uint32_t(t) - mt * uint32_t(tp.n_tiles)) * BN;
+      const int64_t m0 = int64_t(mt) * TILE_ROWS + rank * kBM;
       const int row = quarter * 32 + lane;
       const int64_t p = m0 + row;
       const bool pv = p < g.P;
@@ -697,19 +698,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       Iter wi(tp, tile0, tstep, int(blockIdx.x), int(gridDim.x));
       Seg sg;
       while (ok && wi.next(sg)) {
-        const int64_t m0 = (sg.tile / tp.n_tiles) * kBM;
+        const int64_t m0 = int64_t(tp.nt_div.div(uint32_t(sg.tile))) * kBM;
         int rn[8], rih[8], riw[8];
         bool rvalid[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int64_t p = m0 + i * 16 + rsub;
           rvalid[i] = p < g.P;
-          const int64_t pp = rvalid[i] ? p : 0;
-          const int ow = int(pp % g.OW);
-          const int64_t q = pp / g.OW;
-          rih[i] = int(q % g.OH) * g.sh - g.ph;
+          int ow, oh;
+          pixel_nhw(tp, rvalid[i] ? p : 0, rn[i], oh, ow);
+          rih[i] = oh * g.sh - g.ph;
           riw[i] = ow * g.sw - g.pw;
-          rn[i] = int(q / g.OH);
         }
         for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb, ++it) {
           // Gather K step `it` into landing slot it % LAND.  That slot's
@@ -755,8 +754,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       Seg sg;
       while (ok && wi.next(sg)) {
         const int64_t t = sg.tile;
-        const int n0 = int(t % tp.n_tiles) * BN;
-        const int64_t m0 = (t / tp.n_tiles) * TILE_ROWS + rank * kBM;
+        const uint32_t mt = tp.nt_div.div(uint32_t(t));  // tile row, column (tiles < 2^31)
+        const int n0 = int(uint32_t(t) - mt * uint32_t(tp.n_tiles)) * BN;
+        const int64_t m0 = int64_t(mt) * TILE_ROWS + rank * kBM;
         const int brow = n0 + int(rank) * BROWS;  // first weight row this CTA loads
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
         if (a_role && (AMODE == 3 || AMODE == 4 || AMODE == 5)) {
@@ -1565,7 +1565,6 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     tp.dp_tiles = 0;
     tp.sk_units = tp.tiles * tp.num_kb;
     tp.sk_ctas = ska_g;
-    tp.nt_div = FastDiv(uint32_t(tp.n_tiles));
     tp.sk_park_all = 1;
     st->grid = ska_g;
     st->sk_ws_bytes = size_t(ska_g) * 2 * size_t(bn) * kBM * sizeof(float);
@@ -1607,6 +1606,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
     }
   }
   tp.nk_div = FastDiv(uint32_t(tp.num_kb));
+  tp.nt_div = FastDiv(uint32_t(tp.n_tiles));
+  if (tp.tiles >= (int64_t(1) << 31)) ok = false;  // 32-bit tile arithmetic
   if (tp.sk_units) {
     tp.u_div = FastDiv(uint32_t(tp.sk_units));
     tp.g_div = FastDiv(uint32_t(tp.sk_ctas));

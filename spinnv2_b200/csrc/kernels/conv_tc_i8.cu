@@ -65,7 +65,21 @@ struct I8Params {
   int64_t tiles;
   int out_i32;  // 1: int32 output (acc + b_q), no requantisation
   int epi_tma;  // 1: NHWC int8 output (and residual) through TMA tiles
+  // Tile and pixel coordinates in 32 bits by multiply-shift division (the
+  // host keeps tiles and pixels below 2^31): a 64-bit division per tile and
+  // pixel would cost each epilogue thread more instructions than a chunk of
+  // requantisation.
+  FastDiv nt_div, ow_div, oh_div;
 };
+
+// Output pixel p -> (n, oh, ow).
+__device__ __forceinline__ void pixel_nhw_i8(const I8Params &tp, int64_t p, int &n, int &oh, int &ow) {
+  const uint32_t q = tp.ow_div.div(uint32_t(p));
+  ow = int(uint32_t(p) - q * uint32_t(tp.g.OW));
+  const uint32_t r = tp.oh_div.div(q);
+  oh = int(q - r * uint32_t(tp.g.OH));
+  n = int(r);
+}
 
 __device__ __forceinline__ uint32_t swz_off(int row, int chunk) {
   return uint32_t(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -167,8 +181,9 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
     // issued[b] counts the loads into buffer b.
     int issued[RB] = {};
     auto load_res = [&](int64_t tt, int b) {
-      const int tn0 = int(tt % tp.n_tiles) * BN;
-      const int64_t trow0 = (tt / tp.n_tiles) * kBM + quarter * 32;
+      const uint32_t tm = tp.nt_div.div(uint32_t(tt));
+      const int tn0 = int(uint32_t(tt) - tm * uint32_t(tp.n_tiles)) * BN;
+      const int64_t trow0 = int64_t(tm) * kBM + quarter * 32;
       mbar_arrive_expect_tx(&res_bar[warp * RB + b], 32 * CW);
       tma_load_2d(staging + (warp * RB + b) * (32 * CW), &rmap, tn0 + col0, int(trow0), &res_bar[warp * RB + b]);
       ++issued[b];
@@ -178,8 +193,9 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
     int ti = 0;
     bool failed = false;
     for (int64_t t = blockIdx.x; t < tp.tiles; t += gridDim.x, ++ti) {
-      const int n0 = int(t % tp.n_tiles) * BN;
-      const int64_t m0 = (t / tp.n_tiles) * kBM;
+      const uint32_t mt = tp.nt_div.div(uint32_t(t));
+      const int n0 = int(uint32_t(t) - mt * uint32_t(tp.n_tiles)) * BN;
+      const int64_t m0 = int64_t(mt) * kBM;
       const int64_t row0 = m0 + quarter * 32;  // first output pixel of this warp
       const int ab = ti & 1;
       const int rb = RB == 2 ? (ti & 1) : 0;  // staging buffer of this tile
@@ -209,12 +225,7 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
       const int64_t p = row0 + lane;
       const bool pv = p < g.P;
       int n = 0, oh = 0, ow = 0;
-      if (pv) {
-        ow = int(p % g.OW);
-        const int64_t q = p / g.OW;
-        oh = int(q % g.OH);
-        n = int(q / g.OH);
-      }
+      if (pv) pixel_nhw_i8(tp, p, n, oh, ow);
       const int64_t ybase = int64_t(n) * g.ys[0] + int64_t(oh) * g.ys[2] + int64_t(ow) * g.ys[3];
       const int64_t rbase = int64_t(n) * g.rs[0] + int64_t(oh) * g.rs[2] + int64_t(ow) * g.rs[3];
 #pragma unroll 1
@@ -327,19 +338,17 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
         if (lane == 0) mbar_arrive(&full_bar[pit % STAGES]);
       };
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
-        const int64_t m0 = (t / tp.n_tiles) * kBM;
+        const int64_t m0 = int64_t(tp.nt_div.div(uint32_t(t))) * kBM;
         int rn[8], rih[8], riw[8];
         bool rvalid[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int64_t p = m0 + i * 16 + rsub;
           rvalid[i] = p < g.P;
-          const int64_t pp = rvalid[i] ? p : 0;
-          const int ow = int(pp % g.OW);
-          const int64_t q = pp / g.OW;
-          rih[i] = int(q % g.OH) * g.sh - g.ph;
+          int ow, oh;
+          pixel_nhw_i8(tp, rvalid[i] ? p : 0, rn[i], oh, ow);
+          rih[i] = oh * g.sh - g.ph;
           riw[i] = ow * g.sw - g.pw;
-          rn[i] = int(q / g.OH);
         }
         for (int kb = 0; kb < tp.num_kb && ok; ++kb, ++it) {
           if (it >= uint32_t(STAGES - 1)) {
@@ -377,15 +386,15 @@ __global__ void __launch_bounds__(threads_of(BN, AMODE), 1)
       uint32_t it = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tp.tiles && ok; t += gridDim.x) {
-        const int n0 = int(t % tp.n_tiles) * BN;
-        const int64_t m0 = (t / tp.n_tiles) * kBM;
+        const uint32_t mt = tp.nt_div.div(uint32_t(t));
+        const int n0 = int(uint32_t(t) - mt * uint32_t(tp.n_tiles)) * BN;
+        const int64_t m0 = int64_t(mt) * kBM;
         int bw = 0, bh = 0, bn = 0;  // im2col base of the tile's first output pixel
         if (AMODE == 3 || AMODE == 5) {
-          const int ow = int(m0 % g.OW);
-          const int64_t q = m0 / g.OW;
+          int ow, oh;
+          pixel_nhw_i8(tp, m0, bn, oh, ow);
           bw = ow * g.sw - g.pw;
-          bh = int(q % g.OH) * g.sh - g.ph;
-          bn = int(q / g.OH);
+          bh = oh * g.sh - g.ph;
         }
         for (int kb = 0; kb < tp.num_kb; ++kb, ++it) {
           const int s = it % STAGES;
@@ -609,6 +618,13 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
   tp.n_tiles = tp.Npad / bn;
   tp.tiles = ceil_div(g.P, kBM) * tp.n_tiles;
   tp.out_i32 = p.mode == kConvI8ToI32 ? 1 : 0;
+  if (g.P >= (int64_t(1) << 31) || tp.tiles >= (int64_t(1) << 31)) {  // 32-bit coordinates
+    delete st;
+    return SPKV2_ERR_UNSUPPORTED;
+  }
+  tp.nt_div = FastDiv(uint32_t(tp.n_tiles));
+  tp.ow_div = FastDiv(uint32_t(g.OW));
+  tp.oh_div = FastDiv(uint32_t(g.OH));
   const bool nhwc_out = g.ys[1] == 1 && g.ys[3] == g.M && g.ys[2] == int64_t(g.OW) * g.M;
   const bool nhwc_res = !g.has_res || (g.rs[1] == 1 && g.rs[3] == g.M && g.rs[2] == int64_t(g.OW) * g.M);
   tp.epi_tma = (!tp.out_i32 && nhwc_out && nhwc_res && g.M % 16 == 0 &&
