@@ -17,7 +17,8 @@
 // adjacent reduced axes forming one strided run are walked as one); the
 // threads of a warp take adjacent outputs, so NHWC global pooling reads
 // coalesce along C.  Softmax uses a warp per row when the axis is innermost in
-// row-major tensors, else one thread per row over any layouts.
+// row-major tensors (a block per row for a few rows of 512 or more), else one
+// thread per row over any layouts.
 // TopK (one block per row) radix-selects the k smallest (value, index) keys
 // and sorts those (k <= 2048; rows of any length, keys in shared memory up
 // to 16384 elements, recomputed from global memory beyond), else
@@ -39,7 +40,34 @@ struct ReduceDesc {
   int64_t red_dim[kMaxRank];
   int64_t red_xstride[kMaxRank];
   float denom;
+  int o32;                       // output count < 2^31: coordinates by 32-bit multiply-shift divisions
+  FastDiv keep_div[kMaxRank];    // keep_dim[k]
 };
+
+// Input and output offsets of output element o (row-major over the kept
+// dims).
+__device__ __forceinline__ void reduce_bases(const ReduceDesc &d, int64_t o, int64_t &xb, int64_t &yo) {
+  xb = 0;
+  yo = 0;
+  if (d.o32) {
+    uint32_t rem = uint32_t(o);
+    for (int k = d.keep_rank - 1; k >= 0; --k) {
+      const uint32_t q = d.keep_div[k].div(rem);
+      const int64_t c = int64_t(rem - q * d.keep_div[k].d);
+      rem = q;
+      xb += c * d.keep_xstride[k];
+      yo += c * d.keep_ystride[k];
+    }
+    return;
+  }
+  int64_t rem = o;
+  for (int k = d.keep_rank - 1; k >= 0; --k) {
+    const int64_t c = rem % d.keep_dim[k];
+    rem /= d.keep_dim[k];
+    xb += c * d.keep_xstride[k];
+    yo += c * d.keep_ystride[k];
+  }
+}
 
 struct ReducePlan : NodePlan {
   ReduceDesc d;
@@ -53,27 +81,22 @@ template <bool IS_MAX>
 __global__ void reduce_kernel(float *__restrict__ y, const float *__restrict__ x, ReduceDesc d, int64_t outputs,
                               int64_t red_count) {
   for (int64_t o = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; o < outputs; o += int64_t(gridDim.x) * blockDim.x) {
-    int64_t rem = o, xb = 0, yo = 0;
-    for (int k = d.keep_rank - 1; k >= 0; --k) {
-      const int64_t c = rem % d.keep_dim[k];
-      rem /= d.keep_dim[k];
-      xb += c * d.keep_xstride[k];
-      yo += c * d.keep_ystride[k];
-    }
+    int64_t xb, yo;
+    reduce_bases(d, o, xb, yo);
     float acc = IS_MAX ? -INFINITY : 0.0f;
     if (d.red_rank == 1) {
       // One reduced axis (adjacent reduced axes are merged at prepare): a
-      // strided walk, eight loads in flight; the accumulation order stays
+      // strided walk, sixteen loads in flight; the accumulation order stays
       // r = 0, 1, 2, ... as in the reference.
       const int64_t st = d.red_xstride[0];
       const float *p = x + xb;
       int64_t r = 0;
-      for (; r + 8 <= red_count; r += 8) {
-        float v[8];
+      for (; r + 16 <= red_count; r += 16) {
+        float v[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = p[(r + j) * st];
+        for (int j = 0; j < 16; ++j) v[j] = p[(r + j) * st];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 16; ++j) {
           if (IS_MAX)
             acc = v[j] > acc ? v[j] : acc;
           else
@@ -111,13 +134,8 @@ __global__ void reduce_kernel(float *__restrict__ y, const float *__restrict__ x
 __global__ void reduce_mean_i8_kernel(float *__restrict__ y, const int8_t *__restrict__ x, ReduceDesc d,
                                       int64_t outputs, int64_t red_count, float factor) {
   for (int64_t o = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; o < outputs; o += int64_t(gridDim.x) * blockDim.x) {
-    int64_t rem = o, xb = 0, yo = 0;
-    for (int k = d.keep_rank - 1; k >= 0; --k) {
-      const int64_t c = rem % d.keep_dim[k];
-      rem /= d.keep_dim[k];
-      xb += c * d.keep_xstride[k];
-      yo += c * d.keep_ystride[k];
-    }
+    int64_t xb, yo;
+    reduce_bases(d, o, xb, yo);
     int32_t acc = 0;
     if (d.red_rank == 1) {
       // Integer sums are exact in any order: eight loads in flight.
@@ -205,6 +223,45 @@ __global__ void softmax_rows_kernel(float *__restrict__ y, const float *__restri
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     __syncwarp();
     for (int64_t i = lane; i < dim; i += 32) yr[i] = yr[i] / s;
+  }
+}
+
+// Few long rows (a batch-1 classifier head): one 256-thread block per row,
+// block-wide max and sum through shared memory.
+constexpr int kSoftmaxBlock = 256;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  __syncthreads();  // sh is free (an earlier reduction has been read)
+  if (lane == 0) sh[w] = v;
+  __syncthreads();
+  v = sh[0];
+  for (int i = 1; i < kSoftmaxBlock / 32; ++i) v = is_max ? fmaxf(v, sh[i]) : v + sh[i];
+  return v;
+}
+
+__global__ void __launch_bounds__(kSoftmaxBlock) softmax_row_block_kernel(float *__restrict__ y,
+                                                                          const float *__restrict__ x, int64_t rows,
+                                                                          int64_t dim) {
+  __shared__ float sh[kSoftmaxBlock / 32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float *xr = x + row * dim;
+    float *yr = y + row * dim;
+    float m = -INFINITY;
+    for (int64_t i = threadIdx.x; i < dim; i += kSoftmaxBlock) m = fmaxf(m, xr[i]);
+    m = block_reduce(m, true, sh);
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < dim; i += kSoftmaxBlock) {
+      const float e = expf(xr[i] - m);
+      yr[i] = e;
+      s += e;
+    }
+    s = block_reduce(s, false, sh);
+    for (int64_t i = threadIdx.x; i < dim; i += kSoftmaxBlock) yr[i] = yr[i] / s;
   }
 }
 
@@ -475,6 +532,8 @@ int reduce_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Ke
   }
   p->outputs = 1;
   for (int k = 0; k < d.keep_rank; ++k) p->outputs *= d.keep_dim[k];
+  d.o32 = p->outputs < (int64_t(1) << 31) ? 1 : 0;
+  for (int k = 0; k < d.keep_rank; ++k) d.keep_div[k] = FastDiv(uint32_t(d.o32 ? d.keep_dim[k] : 1));
   if (p->int8_in) {
     const float *sx = quant_scales(ctx, find_quant_param(ctx, node->inputs[0]));
     if (!sx) {
@@ -561,7 +620,9 @@ int softmax_run(Spkv2Context *ctx, const Spkv2NodeRecord *node, void *) {
     softmax_view_kernel<<<grid_for(p->outer, 128), 128, 0, ctx->stream>>>(y, x, p->v, p->outer);
     return cuda_status(cudaGetLastError());
   }
-  if (p->inner == 1)
+  if (p->inner == 1 && p->outer <= 256 && p->dim >= 512)
+    softmax_row_block_kernel<<<int(p->outer), kSoftmaxBlock, 0, ctx->stream>>>(y, x, p->outer, p->dim);
+  else if (p->inner == 1)
     softmax_rows_kernel<<<grid_for(p->outer * 32, 256), 256, 0, ctx->stream>>>(y, x, p->outer, p->dim);
   else
     softmax_strided_kernel<<<grid_for(p->outer * p->inner, 128), 128, 0, ctx->stream>>>(y, x, p->outer, p->dim,
