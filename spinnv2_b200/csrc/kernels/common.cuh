@@ -109,9 +109,13 @@ struct FastDiv {
     m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
     s = l - 1;
   }
-  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+  __host__ __device__ __forceinline__ uint32_t div(uint32_t n) const {
     if (d == 1) return n;
+#ifdef __CUDA_ARCH__
     const uint32_t t = __umulhi(m, n);
+#else
+    const uint32_t t = uint32_t((uint64_t(m) * n) >> 32);
+#endif
     return (t + ((n - t) >> 1)) >> s;
   }
 };
