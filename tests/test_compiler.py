@@ -84,7 +84,9 @@ def test_cuda_plan_keeps_nhwc_safe_aliases_only():
                 assert not (out.data_offset <= t.data_offset < out.data_offset + out.size_bytes)
 
 
-def test_resnet_flops_match_survey():
+def test_resnet_flops_match_published_counts():
+    """2 x MACs of the convs and the FC at 224x224: ResNet-101 v1.5 15.60 and
+    ResNet-50 v1.5 8.18 GFLOP per image."""
     assert abs(builders.resnet_gflop_per_image(101) - 15.60) < 0.05
     assert abs(builders.resnet_gflop_per_image(50) - 8.18) < 0.05
 
