@@ -1435,18 +1435,27 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   }
   st->split3 = p.math == SPKV2_CUDA_MATH_3XTF32;
   // A operand: tiled TMA for 1x1 stride-1 convs, im2col TMA for other
-  // square convs with C % 32 == 0, cp.async gathers otherwise.
+  // square convs with C % 32 == 0, cp.async gathers otherwise.  The
+  // one-column im2col maps (AMODE 3, 4) walk window origins from (-pw, -ph)
+  // over the extent that bottom / right padding equal to the top / left
+  // padding gives, and the row map (AMODE 2) assumes the output extent is
+  // the input's: a conv whose output extent says otherwise (asymmetric
+  // padding) takes the two-column map, whose corners follow the output
+  // extent, or the gathers.
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
+  const bool sym_extent = g.OW == (g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1) / g.sw + 1 &&
+                          g.OH == (g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1) / g.sh + 1;
   const bool im2col_ok = encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL");
   if (st->s2d)
     st->amode = 5;
-  else if (g.C % 4 == 0 && g.C >= 32 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
+  else if (g.C % 4 == 0 && g.C >= 32 && g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 &&
+           g.OH == g.H && g.OW == g.W)
     st->amode = 2;  // [P][C] rows; a last K step past C reads zeros (outside the tensor)
-  else if (g.C % 32 == 0 && (square || st->packed_rows) && im2col_ok)
+  else if (g.C % 32 == 0 && (square || st->packed_rows) && sym_extent && im2col_ok)
     st->amode = 3;
   else if (g.C % 16 == 0 && im2col_ok)
     st->amode = 5;  // C % 16 == 0: two 64-byte (16-channel) im2col columns per K step
-  else if (g.C == 4 && square && im2col_ok)
+  else if (g.C == 4 && square && sym_extent && im2col_ok)
     st->amode = 4;  // 4-channel (re-laid-out) inputs: eight 16-byte im2col columns per K step
   else
     st->amode = 1;

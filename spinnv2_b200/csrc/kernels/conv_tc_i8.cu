@@ -589,12 +589,17 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
   memset(&st->amap, 0, sizeof(st->amap));
   memset(&st->ymap, 0, sizeof(st->ymap));
   memset(&st->rmap, 0, sizeof(st->rmap));
+  // The im2col maps walk window origins over the extent that bottom / right
+  // padding equal to the top / left padding gives, and the row map assumes
+  // the output extent is the input's: asymmetric padding takes the gathers.
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
-  if (g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0)
+  const bool sym_extent = g.OW == (g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1) / g.sw + 1 &&
+                          g.OH == (g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1) / g.sh + 1;
+  if (g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 && g.OH == g.H && g.OW == g.W)
     st->amode = 2;
-  else if (square && g.C % kBK == 0 && encode_im2col_fn())
+  else if (square && sym_extent && g.C % kBK == 0 && encode_im2col_fn())
     st->amode = 3;
-  else if (square && g.C == 64 && encode_im2col_fn() && !getenv("SPKV2_I8_NO_IM2COL64"))
+  else if (square && sym_extent && g.C == 64 && encode_im2col_fn() && !getenv("SPKV2_I8_NO_IM2COL64"))
     st->amode = 5;
   else
     st->amode = 1;
