@@ -1356,9 +1356,10 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   // Row packing pays for wide filters (a 7x7 first conv: ResNet-50 INT8 bs256
   // 55.5k img/s packed vs 46.2k re-laid out); a 3x3 first conv is faster
   // re-laid out to 4 channels and read by 4-channel im2col TMA (detector bs64
-  // 4215 vs 4083 img/s).
+  // 4215 vs 4083 img/s).  The packed row holds KW adjacent pixels, so only
+  // for convs without horizontal dilation.
   const bool row_pack = !(nhwc_in && g.C % 4 == 0 && aligned_in) && g.C <= 4 && 4 * g.KW <= 32 && g.KW >= 5 &&
-                        encode_im2col_fn() && !getenv("SPKV2_TC_NO_ROWPACK");
+                        g.dw == 1 && encode_im2col_fn() && !getenv("SPKV2_TC_NO_ROWPACK");
   // Space-to-depth for stride-2 few-channel convs (a network's first conv):
   // pixel (i, j) of the staged input holds the 2 x 2 input pixels (2i.., 2j..)
   // x 4 channels, so the conv becomes a stride-1 k' x k' conv over 16

@@ -4,7 +4,7 @@ grouped and depthwise convs, dilations, non-square kernels and strides, odd and
 rectangular extents, and a bias with Relu fused.
 
 CPU: the oracle restatement matches the reference runtime built from its own
-sources.  B200: the CUDA runtime (tensor-core path where it accepts the form,
+sources, on these forms and on forty seeded random ones.  B200: the CUDA runtime (tensor-core path where it accepts the form,
 the CUDA-core conv otherwise) matches the reference runtime within the fp32
 tolerance of the parity suite, np.allclose(gpu, ref, atol=1e-3, rtol=1e-4),
 eager and graph-replayed runs bit-identical."""
@@ -74,6 +74,41 @@ def test_oracle_matches_reference_runtime_on_conv_form(built, case):
     mine, _ = harness.run_spk(spk_gpu, [x])
     for r, o in zip(ref, mine):
         np.testing.assert_allclose(o, r, rtol=1e-5, atol=1e-5)
+
+
+def _random_forms(count: int, seed: int):
+    """Seeded random conv attribute forms: groups 1/2/4, 1-8 channels per
+    group, kernels 1-5 per side, strides 1-3, dilations 1-2, each pad 0-2,
+    extents 1-15."""
+    rng = np.random.default_rng(seed)
+    forms = []
+    while len(forms) < count:
+        group = int(rng.choice([1, 1, 2, 4]))
+        c, m = group * int(rng.integers(1, 9)), group * int(rng.integers(1, 9))
+        kh, kw = int(rng.integers(1, 6)), int(rng.integers(1, 6))
+        sh, sw = int(rng.integers(1, 4)), int(rng.integers(1, 4))
+        dh, dw = int(rng.integers(1, 3)), int(rng.integers(1, 3))
+        pads = tuple(int(v) for v in rng.integers(0, 3, 4))
+        h, w = int(rng.integers(1, 16)), int(rng.integers(1, 16))
+        if (h + pads[0] + pads[2] - dh * (kh - 1) - 1) < 0 or (w + pads[1] + pads[3] - dw * (kw - 1) - 1) < 0:
+            continue
+        forms.append((int(rng.integers(1, 3)), c, h, w, m, (kh, kw), (sh, sw), pads, (dh, dw), group,
+                      bool(rng.integers(0, 2))))
+    return forms
+
+
+def test_oracle_matches_reference_runtime_on_random_conv_forms(built):
+    from oracle import harness
+
+    for i, form in enumerate(_random_forms(40, 123)):
+        CASES[f"random_{i}"] = form
+        try:
+            spk_gpu, spk_cpu, x = _packages(f"random_{i}")
+        finally:
+            del CASES[f"random_{i}"]
+        ref = reference_outputs(spk_cpu, [x])[0]
+        mine = harness.run_spk(spk_gpu, [x])[0][0]
+        np.testing.assert_allclose(mine, ref, rtol=1e-5, atol=1e-5, err_msg=str(form))
 
 
 @pytest.mark.gpu
