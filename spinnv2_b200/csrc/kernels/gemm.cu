@@ -339,6 +339,13 @@ int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
   p->M = int(a.trans_a ? ta.record->shape[1] : ta.record->shape[0]);
   p->K = int(a.trans_a ? ta.record->shape[0] : ta.record->shape[1]);
   p->N = int(a.trans_b ? tb.record->shape[0] : tb.record->shape[1]);
+  // The reference adds c[n] to column n whatever C's shape (a [M, N] C
+  // contributes its first row); a C with fewer than N elements would be read
+  // past its end there, and is rejected here.
+  if (node->input_count > 2 && elem_count(ctx->tensors[node->inputs[2]].record) < size_t(p->N)) {
+    delete p;
+    return -11;
+  }
   if (!p->trans_a && !p->trans_b && p->M <= kGemvMaxM) {
     p->ksplit = std::max(1, std::min(16, p->K / 128));
     p->partials = static_cast<float *>(device_alloc(size_t(p->ksplit) * p->M * p->N * sizeof(float) + 16));
@@ -366,7 +373,6 @@ int gemm_prepare(Spkv2Context *ctx, const Spkv2NodeRecord *node, const Spkv2Kern
       c->mode = kConvF32;
       c->math = math;
       c->bias_f = g.has_bias ? reinterpret_cast<const float *>(ctx->tensors[node->inputs[2]].data) : nullptr;
-      if (g.has_bias && elem_count(ctx->tensors[node->inputs[2]].record) != size_t(p->N)) g.has_bias = 0;
       int trc = conv_tc_prepare_ex(*c, tb.data, ta.data, ty.data, true, ctx->stream);
       if (trc == 0) trc = conv_tc_attach(ctx, *c);
       if (trc == 0) {
