@@ -1444,8 +1444,8 @@ int conv_tc_prepare_ex(ConvPlan &p, const void *w_raw_dev, const void *x_dev, co
   // padding) takes the two-column map, whose corners follow the output
   // extent, or the gathers.
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
-  const bool sym_extent = g.OW == (g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1) / g.sw + 1 &&
-                          g.OH == (g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1) / g.sh + 1;
+  const int span_w = g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1, span_h = g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1;
+  const bool sym_extent = span_w >= 0 && span_h >= 0 && g.OW == span_w / g.sw + 1 && g.OH == span_h / g.sh + 1;
   const bool im2col_ok = encode_im2col_fn() && !getenv("SPKV2_TC_NO_IM2COL");
   if (st->s2d)
     st->amode = 5;

@@ -593,8 +593,8 @@ int conv_tc_i8_prepare(ConvPlan &p, const void *w_dev, const void *x_dev, const 
   // padding equal to the top / left padding gives, and the row map assumes
   // the output extent is the input's: asymmetric padding takes the gathers.
   const bool square = g.KH == g.KW && g.sh == g.sw && g.ph == g.pw && g.dh == g.dw;
-  const bool sym_extent = g.OW == (g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1) / g.sw + 1 &&
-                          g.OH == (g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1) / g.sh + 1;
+  const int span_w = g.W + 2 * g.pw - (g.KW - 1) * g.dw - 1, span_h = g.H + 2 * g.ph - (g.KH - 1) * g.dh - 1;
+  const bool sym_extent = span_w >= 0 && span_h >= 0 && g.OW == span_w / g.sw + 1 && g.OH == span_h / g.sh + 1;
   if (g.KH == 1 && g.KW == 1 && g.sh == 1 && g.sw == 1 && g.ph == 0 && g.pw == 0 && g.OH == g.H && g.OW == g.W)
     st->amode = 2;
   else if (square && sym_extent && g.C % kBK == 0 && encode_im2col_fn())
