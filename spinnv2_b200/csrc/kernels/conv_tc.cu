@@ -14,12 +14,17 @@
 //               SiLU -> TMA store staged through shared memory (NHWC
 //               outputs) or direct stores.  TMEM holds two accumulator
 //               buffers, so the epilogue overlaps the next tile's mainloop.
-//   warps 8-11  A operand.  AMODE 2 (1x1, stride 1, C % 32 == 0): the tile
-//               arrives by a tiled TMA load; AMODE 3 (other square convs,
-//               C % 32 == 0): by an im2col TMA load (128 output pixels x 32
-//               channels of one filter tap, padding zero-filled by the TMA
-//               unit); AMODE 4 (4-channel inputs): eight 16-byte im2col
-//               columns per K step in an unswizzled core-matrix layout.  The
+//   warps 8-11  A operand.  AMODE 2 (1x1, stride 1, C % 32 == 0, output
+//               extent = input extent): the tile arrives by a tiled TMA load;
+//               AMODE 3 (other square convs, C % 32 == 0, the output extent
+//               of equal top / bottom and left / right padding): by an im2col
+//               TMA load (128 output pixels x 32 channels of one filter tap,
+//               padding zero-filled by the TMA unit); AMODE 5 (C % 16 == 0,
+//               space-to-depth first convs, any padding: window corners from
+//               the output extent): two 16-channel 64-byte im2col columns per
+//               K step; AMODE 4 (4-channel inputs, as AMODE 3's extent): eight
+//               16-byte im2col columns per K step in an unswizzled
+//               core-matrix layout.  The
 //               tile lands straight in the operand stage; for 3xTF32 these
 //               warps add its low part.  AMODE 1 (any other conv): each
 //               thread gathers its 16-byte chunks with cp.async (zero-fill
