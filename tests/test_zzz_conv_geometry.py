@@ -129,3 +129,42 @@ def test_conv_form_matches_reference_on_b200(gpu, case):
         err = np.abs(a - r)
         print(case, variant, "max abs", float(err.max()))
         np.testing.assert_allclose(a, r, atol=ATOL, rtol=RTOL)
+
+
+def test_oracle_matches_reference_runtime_on_random_pool_forms(built):
+    """MaxPool / AveragePool (reference runtime/kernels/reference/pool/
+    maxpool.c, avgpool.c: pads[0], pads[1] at the top / left, the output
+    extent from the output tensor, averages over the in-image taps) on
+    seeded random kernels 1-5, strides 1-3, pads below the kernel and odd
+    extents: the oracle matches the reference runtime."""
+    import copy
+
+    from oracle import harness
+    from spinnv2_b200.compiler import pipeline
+    from spinnv2_b200.compiler.ir import GraphBuilder
+
+    rng = np.random.default_rng(7)
+    checked = 0
+    while checked < 40:
+        op = str(rng.choice(["MaxPool", "AveragePool"]))
+        kh, kw = int(rng.integers(1, 6)), int(rng.integers(1, 6))
+        sh, sw = int(rng.integers(1, 4)), int(rng.integers(1, 4))
+        p = [int(v) for v in rng.integers(0, 3, 4)]
+        pads = [min(p[0], kh - 1), min(p[1], kw - 1), min(p[2], kh - 1), min(p[3], kw - 1)]
+        n, c, h, w = (int(rng.integers(1, 3)), int(rng.integers(1, 10)), int(rng.integers(1, 14)),
+                      int(rng.integers(1, 14)))
+        oh, ow = (h + pads[0] + pads[2] - kh) // sh + 1, (w + pads[1] + pads[3] - kw) // sw + 1
+        if oh < 1 or ow < 1:
+            continue
+        b = GraphBuilder(f"pool_form_{checked}")
+        x = b.input("input", [n, c, h, w])
+        x1 = b.op("Add", [x, b.weight("pre_c", np.array([0.125], np.float32))], [n, c, h, w])
+        b.mark_output(b.op(op, [x1], [n, c, oh, ow], {"kernel_shape": [kh, kw], "strides": [sh, sw], "pads": pads}))
+        graph = pipeline.fuse(b.graph)
+        spk_gpu = pipeline.package(copy.deepcopy(graph), "cuda_b200")
+        spk_cpu = pipeline.package(copy.deepcopy(graph), "cpu_generic_x86")
+        xin = rng.standard_normal((n, c, h, w)).astype(np.float32)
+        ref = reference_outputs(spk_cpu, [xin])[0]
+        mine = harness.run_spk(spk_gpu, [xin])[0][0]
+        np.testing.assert_allclose(mine, ref, rtol=1e-6, atol=1e-6, err_msg=f"{op} {kh}x{kw} s{sh}x{sw} {pads}")
+        checked += 1
